@@ -1,0 +1,291 @@
+"""Benchmark of the B200 token sampler on the metric's configuration.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--rows R]
+
+Workload (per GPU): the headline configuration, 1024 rows x 151,936 f32 logits with the
+mixed per-row parameters of the benchmark's config 3 (temperature U[0.5,1.5], top_k in
+{0,20,40,100}, top_p U[0.8,1.0], repetition penalty U[1.0,1.3] over a 64-token window),
+seeded synthetic data.  A step samples every row once (one kernel launch).  Rows are
+independent, so N GPUs run N replicas on different rows (weak scaling, no collective).
+
+value      rows/s over all GPUs with inputs resident in HBM (CUDA events, max over ranks)
+e2e        the same metric through the host-buffer entry point (lrs_sample): pinned host
+           logits copied in and tokens/statuses copied out inside the timed region
+roofline   algorithmic bytes (4 * vocab + 4 * window per row) / kernel time vs measured HBM copy bandwidth
+cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of the same rows
+--impl reference  times that CPU restatement alone (all host threads) on the same workload
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "llama.rs_b200"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "sampled rows/s at 1024×151,936 f32 logits; % of HBM roofline at 1/2/4/8 GPUs"
+WORKLOAD = ("headline: 1024 rows x 151,936 f32 logits per GPU, Gumbel + Zipf-like head under a per-row "
+            "permutation, temperature U[0.5,1.5], top_k {0,20,40,100}, top_p U[0.8,1.0], "
+            "repetition penalty U[1.0,1.3] over a 64-token window")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(REPO, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name="lrs_sample_rows_headline.txt"):
+    """dram bytes per launch from the committed ncu summary, if present."""
+    path = os.path.join(REPO, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch_full_size:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"lrs_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        self.proc.wait()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+def cpu_sample(w, rows, threads):
+    """Times the CPU restatement on `rows` rows of workload w; returns rows/s."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import oracle as O
+    O.build()
+    sl = slice(0, rows)
+    t = time.perf_counter()
+    O.sample_batch(w.logits[sl], w.vocab, w.hist[sl], w.hist_len[sl], w.params[sl], w.state[sl], threads=threads)
+    dt = time.perf_counter() - t
+    return rows / dt, dt
+
+
+def run_reference(args, world, rank):
+    """--impl reference: the CPU restatement of sampler.rs on the host cores."""
+    if rank != 0:
+        return
+    from lrs import workloads as W
+    rows = min(args.rows, args.ref_rows)
+    w = W.headline(row_ids=range(rows))
+    threads = os.cpu_count() or 1
+    times = []
+    for i in range(args.warmup + args.steps):
+        _, dt = cpu_sample(w, rows, threads)
+        if i >= args.warmup:
+            times.append(dt)
+    value = rows * len(times) / sum(times)
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "rows_per_step": rows, "vocab": w.vocab, "window": w.window},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
+                         "sample": f"{rows} rows of the headline workload per step, one sampler per row, "
+                                   f"rows spread over {threads} host threads"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--rows", type=int, default=1024)
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--ref-rows", type=int, default=128)
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+
+    import torch
+    import lrs
+    from lrs import workloads as W
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        pg = dist
+
+    rows = args.rows
+    w = W.headline(row_ids=range(rank * rows, (rank + 1) * rows))
+    V, Wn = w.vocab, w.window
+    bs = lrs.BatchSampler(rows, V, Wn, device=local)
+    logits = torch.from_numpy(w.logits).to(dev)
+    hist = torch.from_numpy(w.hist.view(np.int32)).to(dev)
+    hlen = torch.from_numpy(w.hist_len.view(np.int32)).to(dev)
+    params = torch.from_numpy(w.params.view(np.uint8)).to(dev)
+    state = torch.from_numpy(w.state.view(np.int64)).to(dev)
+    tokens = torch.zeros(rows, dtype=torch.int32, device=dev)
+    status = torch.zeros(rows, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        bs.sample_device(logits, params, state, tokens, n=V, hist=hist, hist_len=hlen, status=status,
+                         stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    bad = int((status != 0).sum())
+    if bad:
+        raise SystemExit(f"{bad} rows reported a non-zero status")
+
+    clocks = Clocks(local)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        ev[i][0].record(stream)
+        step()
+        ev[i][1].record(stream)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    clk = clocks.stop()
+    total_ms = t0.elapsed_time(t1)
+    launch_ms = [a.elapsed_time(b) for a, b in ev]
+    if pg:
+        tt = torch.tensor([total_ms], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        total_ms = float(tt.item())
+    value = world * rows * args.steps / (total_ms / 1000.0)
+
+    # e2e: host buffers through lrs_sample (pinned logits, synchronous call)
+    pinned = torch.from_numpy(w.logits).pin_memory()
+    host_logits = pinned.numpy()
+    bs.set_params(w.params)
+    bs.set_state(w.state)
+    bs.sample(host_logits, hist=w.hist, hist_len=w.hist_len)  # warm
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    te = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        bs.sample(host_logits, hist=w.hist, hist_len=w.hist_len)
+    e2e_s = time.perf_counter() - te
+    if pg:
+        tt = torch.tensor([e2e_s], device=dev)
+        pg.all_reduce(tt, op=pg.ReduceOp.MAX)
+        e2e_s = float(tt.item())
+    e2e_value = world * rows * args.e2e_steps / e2e_s
+    h2d = rows * V * 4 + rows * Wn * 4 + rows * 4
+    d2h = rows * 4 * 2
+
+    bytes_per_row = 4 * V + 4 * Wn
+    mean_launch = statistics.mean(launch_ms)
+    achieved = rows * bytes_per_row / (mean_launch / 1000.0) / 1e9
+    peak, kind = peaks()
+    traffic = profile_traffic()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        threads = os.cpu_count() or 1
+        nrows = min(args.cpu_rows, rows)
+        v, dt = cpu_sample(w, nrows, threads)
+        cpu = {"value": v, "unit": "rows/s", "cores": threads, "kind": "port",
+               "sample": f"first {nrows} rows of this rank's headline workload, one sampler per row over "
+                         f"{threads} host threads ({dt:.1f} s)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "rows_per_gpu": rows, "vocab": V, "window": Wn,
+                       "parallelism": f"rows sharded over {world} GPU(s), replicas, no collective",
+                       "l2": "inputs larger than L2 (622 MB of logits per GPU per step)"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "peak_kind": kind, "kernel": "lrs_sample_rows",
+                         "kernel_ms_mean": mean_launch, "bytes_per_launch": rows * bytes_per_row},
+            "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    bs.close()
+    if pg:
+        pg.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,151 @@
+/*
+ * llamars_sampler.h — C ABI of the B200 batched token sampler.
+ *
+ * Drop-in replacement for rust-llama's token sampler:
+ *   src/sampler.rs:3-13    pub struct SamplingParams { temperature, top_k, top_p,
+ *                                                      repetition_penalty, repeat_last_n, seed }
+ *   src/sampler.rs:28-37   pub struct Sampler { state }, Sampler::new(seed) -> state = seed | 1
+ *   src/sampler.rs:56-163  Sampler::sample(&mut self, logits: &[f32], params, recent: &[u32]) -> u32
+ *   src/ops.rs:397-419     ops::softmax_inplace (called by sample, fused into the kernels here)
+ *
+ * Results are those of sampler.rs on the same inputs: the same token, the same
+ * probability bits and the same PRNG state after the call (the sequential f32
+ * accumulations and libm expf of the reference are reproduced exactly on the GPU).
+ *
+ * Error behaviour.  Sampler::sample is infallible except that a NaN probability makes
+ * the `partial_cmp().unwrap()` at sampler.rs:129/132 panic, which aborts the process
+ * (Cargo.toml:25 sets panic = "abort").  Here such a row gets status LRS_E_NAN, its
+ * token is LRS_TOKEN_NONE and its PRNG state is left unchanged; the call returns
+ * LRS_E_NAN after finishing every other row.  No entry point aborts the process.
+ *
+ * Threading.  A context is bound to one CUDA device and is not reentrant: drive it
+ * from one host thread (or serialise calls).  Several contexts (one per GPU) may be
+ * driven from several threads at once.
+ */
+#ifndef LLAMARS_SAMPLER_H
+#define LLAMARS_SAMPLER_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes --------------------------------------------------------- */
+#define LRS_OK            0
+#define LRS_E_INVALID    -1  /* bad argument (null pointer, size out of range, ...) */
+#define LRS_E_NAN        -2  /* a row's probabilities contain NaN: the reference would panic */
+#define LRS_E_CUDA       -3  /* a CUDA runtime call failed; see lrs_last_error */
+#define LRS_E_NOMEM      -4  /* device or pinned-host allocation failed */
+#define LRS_E_TIMEOUT    -5  /* a bounded wait (multi-GPU exchange) ran out */
+#define LRS_E_NCCL       -6  /* an NCCL call failed */
+#define LRS_E_INTERNAL   -7  /* an internal consistency check failed (a bug; please report) */
+
+#define LRS_TOKEN_NONE   0xFFFFFFFFu
+
+/* ---- per-row parameters ----------------------------------------------------
+ * One row's SamplingParams (sampler.rs:3-13) without the seed: the seed only
+ * initialises the PRNG state (Sampler::new, sampler.rs:33-37), which the batched
+ * API carries separately as uint64_t state[rows].
+ * top_k == 0 means "off" exactly as in the reference (sampler.rs:122).
+ * repeat_last_n == 0 means "the whole history" (sampler.rs:84-88).           */
+typedef struct lrs_params {
+    float    temperature;
+    uint32_t top_k;
+    float    top_p;
+    float    repetition_penalty;
+    uint32_t repeat_last_n;
+    uint32_t reserved;          /* must be 0 */
+} lrs_params;
+
+/* Defaults of SamplingParams::default() (sampler.rs:15-26). */
+#define LRS_DEFAULT_TEMPERATURE   0.7f
+#define LRS_DEFAULT_TOP_K         40u
+#define LRS_DEFAULT_TOP_P         0.95f
+#define LRS_DEFAULT_PENALTY       1.1f
+#define LRS_DEFAULT_LAST_N        64u
+#define LRS_DEFAULT_SEED          0x123456789abcdef0ull
+
+/* Optional per-row diagnostics written by the kernels (tests and tools use them to
+ * check every intermediate of sampler.rs against a CPU restatement).            */
+typedef struct lrs_row_info {
+    int32_t  status;     /* LRS_OK or LRS_E_NAN */
+    uint32_t token;
+    uint32_t path;       /* 0 greedy fast path (sampler.rs:62-70), 1 greedy after penalty
+                            (sampler.rs:104-113), 2 stochastic, 3 stochastic with n == 1 */
+    uint32_t k;          /* effective top-k (sampler.rs:122-126) */
+    uint32_t cutoff;     /* survivors after top-p (sampler.rs:135-146) */
+    uint32_t pos;        /* position of the drawn token in the sorted survivor list */
+    float    max;        /* softmax max over the scaled logits (ops.rs:401-406) */
+    float    sum_exp;    /* softmax sequential f32 sum (ops.rs:408-411) */
+    float    surv_sum;   /* survivor sum (sampler.rs:148-151) */
+    float    r0;         /* next_f32() * sum (sampler.rs:155) */
+    float    prob;       /* probability of the returned token */
+    uint32_t n_cand;     /* candidates examined after the streaming pass (implementation detail) */
+} lrs_row_info;
+
+typedef struct lrs_ctx lrs_ctx;
+
+/* ---- context ---------------------------------------------------------------
+ * Replaces: nothing in the reference holds device state; a context owns the GPU
+ * resources that a sequence of Sampler::sample calls (model.rs:752-771,
+ * server.rs:182-187, main.rs:552-577) would otherwise re-create per call.
+ * max_rows rows of up to max_vocab logits and max_hist history ids per call.     */
+int  lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_hist, lrs_ctx** out);
+int  lrs_destroy(lrs_ctx* ctx);
+const char* lrs_last_error(const lrs_ctx* ctx);
+
+/* ---- PRNG state ----------------------------------------------------------------
+ * Replaces Sampler::new(seed) (sampler.rs:33-37): lrs_seed_state returns seed | 1.
+ * State arrays are host memory, `rows` entries, copied to/from the context.      */
+uint64_t lrs_seed_state(uint64_t seed);
+int  lrs_set_state(lrs_ctx* ctx, const uint64_t* state, uint32_t rows);
+int  lrs_get_state(lrs_ctx* ctx, uint64_t* state, uint32_t rows);
+int  lrs_set_params(lrs_ctx* ctx, const lrs_params* params, uint32_t rows);
+
+/* ---- batched sampling from host buffers ---------------------------------------
+ * Replaces `rows` calls of Sampler::sample (sampler.rs:56) on independent samplers.
+ *   logits   host (or device if logits_on_device) f32[rows][ld], row r = logits + r*ld,
+ *            n = vocab entries used per row (n <= ld, n <= max_vocab)
+ *   hist     host u32[rows][hist_ld]; row r's history is hist[r*hist_ld .. + hist_len[r]]
+ *            (the `recent` slice: prompt ids + generated ids, oldest first)
+ *   out_tokens host u32[rows]; out_probs (nullable) host f32[rows]: probability of the
+ *            returned token (1.0f for greedy rows)
+ * Parameters and PRNG state come from lrs_set_params / lrs_set_state; the state is
+ * advanced exactly as sampler.rs advances it (one next_u64 per stochastic row).
+ * Synchronous: returns after the results are in host memory.                       */
+int  lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t rows,
+                uint32_t n, uint64_t ld, const uint32_t* hist, uint64_t hist_ld,
+                const uint32_t* hist_len, uint32_t* out_tokens, float* out_probs);
+
+/* ---- batched sampling on device buffers (the hot path) -------------------------
+ * Same computation, every pointer a device pointer, enqueued on `stream`
+ * (a cudaStream_t, NULL = legacy default stream), no host synchronisation.
+ * d_params[rows], d_state[rows] (read and advanced in place), d_tokens[rows],
+ * d_probs[rows] (nullable), d_status[rows] (nullable, int32), d_info[rows] (nullable).
+ * Returns LRS_OK once enqueued; row errors are reported through d_status.           */
+int  lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t n, uint64_t ld,
+                       const uint32_t* d_hist, uint64_t hist_ld, const uint32_t* d_hist_len,
+                       const lrs_params* d_params, uint64_t* d_state,
+                       uint32_t* d_tokens, float* d_probs, int32_t* d_status,
+                       lrs_row_info* d_info, void* stream);
+
+/* ---- single-row drop-in (Sampler API) -------------------------------------------
+ * lrs_sampler_new    replaces Sampler::new(seed)               (sampler.rs:33-37)
+ * lrs_sampler_sample replaces Sampler::sample(logits, params, recent) (sampler.rs:56)
+ *                    host slices in, token out; *status (nullable) gets LRS_OK or an error;
+ *                    on error the token is LRS_TOKEN_NONE.
+ * A sampler lazily creates a one-row context on `device` sized to the first call.   */
+typedef struct lrs_sampler lrs_sampler;
+lrs_sampler* lrs_sampler_new(uint64_t seed, int device);
+void         lrs_sampler_free(lrs_sampler* s);
+uint64_t     lrs_sampler_state(const lrs_sampler* s);
+uint32_t     lrs_sampler_sample(lrs_sampler* s, const float* logits, size_t n,
+                                const lrs_params* params, const uint32_t* recent,
+                                size_t recent_len, int* status);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLAMARS_SAMPLER_H */
