@@ -83,6 +83,12 @@ typedef struct lrs_row_info {
     float    r0;         /* next_f32() * sum (sampler.rs:155) */
     float    prob;       /* probability of the returned token */
     uint32_t n_cand;     /* candidates examined after the streaming pass (implementation detail) */
+    uint32_t events;     /* ordered (exact) steps taken by the sum emulation (implementation detail) */
+    uint32_t cycles[8];  /* SM clock cycles (saturating) by phase: 0 max/filter pass, 1 softmax-sum
+                            pass, 2 top-k/top-p/draw, 3 waits for staged tiles in the sum pass,
+                            4 ordered steps in the sum pass, 5 skip-threshold searches,
+                            6 waits in the max pass, 7 sorting (implementation detail) */
+    uint32_t reserved;
 } lrs_row_info;
 
 typedef struct lrs_ctx lrs_ctx;

@@ -95,4 +95,38 @@ LRS_HD uint32_t sat_add(uint32_t a, uint32_t b) {
 }
 
 
+// ------------------------------------------------------------ two-grid tiles ----
+// A tile is classified on two grids at once: channel 0 is the running value's grid
+// at the tile start (unit 2^uu), channel 1 the grid it moves to after one binade step
+// (2^(uu+1) for sums, 2^(uu-1) for the draw's decreasing differences).  A tile whose
+// running value crosses one binade is then finished from one prefix scan per channel;
+// only a second crossing needs a re-classification.
+LRS_HD int channel_uu(int uu, int dir, int c) {
+    if (c == 0) return uu;
+    const int u1 = uu + dir;
+    return u1 < -149 ? -149 : u1;
+}
+
+struct Cls2 {
+    uint32_t inc0, inc1;
+    bool spec0, spec1;  // tie or big on that grid: always an ordered step
+};
+LRS_HD Cls2 classify2(uint32_t vb, int uu, int dir) {
+    const Cls a = classify(vb, channel_uu(uu, dir, 0));
+    const Cls b = classify(vb, channel_uu(uu, dir, 1));
+    return Cls2{a.inc, b.inc, a.tie || a.big, b.tie || b.big};
+}
+
+// Lowest grid count a difference may reach on grid uu before leaving it.
+LRS_HD uint32_t grid_lower(int uu) { return uu == -149 ? 0u : kTwo23; }
+
+// Does the element at inclusive prefix `rel` (increments since the last ordered step,
+// on the current grid) need an ordered step?  a: grid count of the running value at
+// the last ordered step; tq: stop threshold in grid units (sums), +inf if none.
+LRS_HD bool needs_step(int dir, bool spec, uint32_t a, uint32_t rel, uint32_t lower, float tq) {
+    if (spec) return true;
+    if (dir > 0) return a + rel >= kTwo24 || (float)(a + rel) >= tq;
+    return rel >= a - lower;
+}
+
 }  // namespace lrs

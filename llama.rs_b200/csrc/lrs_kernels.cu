@@ -34,6 +34,7 @@ constexpr int kNB = 2048;           // path N buckets of width 1/32 in (max - x)
 constexpr float kBScale = 32.0f;
 constexpr int kSortCap = 4096;      // largest bucket sorted in shared memory
 constexpr float kTopPMargin = 0.002f;
+constexpr int kSerial = 512;        // elements summed one by one at the start of a row or scan
 constexpr unsigned long long kWaitLimit = 1ull << 26;
 
 using SampleArgs = lrs_kernel_args_t;
@@ -53,6 +54,10 @@ struct RowShared {
     uint32_t row;
     uint32_t issued;       // ring loads issued so far (thread 0)
     float vk;              // k-th largest scaled logit at the last compaction
+    uint32_t events;       // ordered steps taken by acc_tile for this row
+    uint32_t ev_base0, ev_base1;  // tile2: prefixes at the last ordered step
+    float xthr;            // pass-2 skip threshold on (penalised) raw logits
+    int xthr_uu;           // grid exponent xthr was computed for
     uint32_t misc[8];
 };
 
@@ -125,8 +130,8 @@ __device__ __forceinline__ int li_of(int i) {  // local position of per-thread s
 
 // Saturating inclusive prefix (in local-position order) of per-thread incs.
 // Returns per-slot inclusive sums in incl[].
-__device__ __forceinline__ void block_incl_scan(const uint32_t (&inc)[kVpt], uint32_t (&incl)[kVpt],
-                                                uint32_t* sh) {
+__device__ __forceinline__ uint32_t block_incl_scan(const uint32_t (&inc)[kVpt], uint32_t (&incl)[kVpt],
+                                                    uint32_t* sh) {
     const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
     uint32_t jtot[4], jexcl[4];
 #pragma unroll
@@ -145,8 +150,11 @@ __device__ __forceinline__ void block_incl_scan(const uint32_t (&inc)[kVpt], uin
     __syncthreads();
     if (l == 0) sh[w] = wt;
     __syncthreads();
-    uint32_t off = 0;
-    for (int i = 0; i < w; ++i) off = sat_add(off, sh[i]);
+    uint32_t off = 0, total = 0;
+    for (int i = 0; i < kWarps; ++i) {
+        if (i < w) off = sat_add(off, sh[i]);
+        total = sat_add(total, sh[i]);
+    }
     uint32_t jb = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -158,6 +166,7 @@ __device__ __forceinline__ void block_incl_scan(const uint32_t (&inc)[kVpt], uin
         }
         jb = sat_add(jb, jtot[j]);
     }
+    return total;
 }
 
 // Exact emulation of a run of sequential f32 operations over one tile of values in
@@ -169,9 +178,9 @@ __device__ __forceinline__ void block_incl_scan(const uint32_t (&inc)[kVpt], uin
 // Positions >= cnt are ignored.  Returns the local stop position or -1 and leaves in
 // s the value after the stop position (or after the tile).
 template <typename Exactify>
-__device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, float& s, float thr,
-                        Exactify exactify, RowShared& sh) {
-    int consumed = -1;
+__device__ __noinline__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, float& s, float thr,
+                        Exactify exactify, RowShared& sh, int start = 0) {
+    int consumed = start - 1;
     float cur = s;
     for (int round = 0;; ++round) {
         const int uu = unit_exp(cur);
@@ -183,7 +192,7 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
         uint32_t ev_local = 0;  // bit i: tie or big
         bool nonzero = false;   // some remaining value is > 0
         uint32_t tot = 0;
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < kVpt; ++i) {
             const int li = li_of(i);
             inc[i] = 0;
@@ -195,8 +204,8 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
                 } else {
                     const Cls lo = classify(vb > 8u ? vb - 8u : 0u, uu);
                     const Cls hi = classify(vb + 8u, uu);
-                    if (lo.inc == hi.inc && !lo.tie && !hi.tie && !lo.big && !hi.big) {
-                        c = lo;
+                    if ((lo.inc == hi.inc && !lo.tie && !hi.tie && !lo.big && !hi.big) || (lo.big && hi.big)) {
+                        c = lo;  // same increment (or big) for every value within the error bound
                     } else {
                         v[i] = exactify(i);
                         exact |= 1u << i;
@@ -227,9 +236,9 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
         }
         // Ordered path: find the first event (tie, big, grid change or stop).
         uint32_t incl[kVpt];
-        block_incl_scan(inc, incl, sh.red);
+        (void)block_incl_scan(inc, incl, sh.red);
         uint32_t first = 0xFFFFFFFFu;
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < kVpt; ++i) {
             const int li = li_of(i);
             if (li < cnt && li > consumed) {
@@ -249,7 +258,7 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
             return -1;
         }
         // The owner of the event performs the exact operation.
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < kVpt; ++i) {
             if ((uint32_t)li_of(i) == first) {
                 const uint32_t excl = incl[i] - inc[i];
@@ -271,6 +280,7 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
                 }
                 sh.fstate = after;
                 sh.stop = stop ? (int)first : -1;
+                sh.events++;
             }
         }
         __syncthreads();
@@ -285,9 +295,136 @@ __device__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt, int dir, flo
     }
 }
 
+// Two-grid tile (see lrs_grid.h): values v in local-position order, positions
+// [start, cnt); grid uu = the running value's grid at the tile start.  Used after a
+// tile's single-grid fast path found an ordered step.  Values whose `exact` bit is clear
+// are approximations within 8 float steps of the exact value; exactify(i) gives the
+// exact value.  Same contract as acc_tile.
+template <typename Exactify>
+__device__ __noinline__ int tile2(float (&v)[kVpt], uint32_t& exact, int start, int cnt, int dir, float& s, float thr,
+                     Exactify exactify, RowShared& sh) {
+    const int uu = unit_exp(s);
+    const int u1 = channel_uu(uu, dir, 1);
+    uint32_t inc0[kVpt], inc1[kVpt];
+    uint32_t sp0 = 0, sp1 = 0;
+#pragma unroll 1
+    for (int i = 0; i < kVpt; ++i) {
+        const int li = li_of(i);
+        inc0[i] = inc1[i] = 0;
+        if (li < cnt && li >= start && v[i] != 0.0f) {  // an exact zero adds nothing anywhere
+            if (!(exact & (1u << i))) {
+                // both grids' increments must be the same for every value within the error bound
+                const uint32_t vb = __float_as_uint(v[i]);
+                const Cls2 lo = classify2(vb > 8u ? vb - 8u : 0u, uu, dir);
+                const Cls2 hi = classify2(vb + 8u, uu, dir);
+                const bool ok0 = (lo.inc0 == hi.inc0 && !lo.spec0 && !hi.spec0) || (lo.inc0 == kTwo23 && hi.inc0 == kTwo23);
+                const bool ok1 = (lo.inc1 == hi.inc1 && !lo.spec1 && !hi.spec1) || (lo.inc1 == kTwo23 && hi.inc1 == kTwo23);
+                if (!ok0 || !ok1) {
+                    v[i] = exactify(i);
+                    exact |= 1u << i;
+                }
+            }
+            const Cls2 c = classify2(__float_as_uint(v[i]), uu, dir);
+            inc0[i] = c.inc0;
+            inc1[i] = c.inc1;
+            if (c.spec0) sp0 |= 1u << i;
+            if (c.spec1) sp1 |= 1u << i;
+        }
+    }
+    uint32_t incl0[kVpt], incl1[kVpt];
+    const uint32_t tot0 = block_incl_scan(inc0, incl0, sh.red);
+    const uint32_t tot1 = block_incl_scan(inc1, incl1, sh.red);
+    int consumed = start - 1;
+    float cur = s;
+    uint32_t base0 = 0, base1 = 0;
+    for (;;) {
+        const int ucur = unit_exp(cur);
+        const int ch = ucur == uu ? 0 : (ucur == u1 ? 1 : -1);
+        if (ch < 0) {  // a second grid change inside the tile
+            s = cur;
+            return acc_tile(v, exact, cnt, dir, s, thr, exactify, sh, consumed + 1);
+        }
+        const uint32_t A = grid_count(cur, ucur);
+        const uint32_t lower = grid_lower(ucur);
+        const float tq = (dir > 0 && thr < __int_as_float(0x7F800000)) ? ldexpf(thr, -ucur) : __int_as_float(0x7F800000);
+        const uint32_t base = ch ? base1 : base0;
+        const uint32_t spm = ch ? sp1 : sp0;
+        uint32_t cand = 0xFFFFFFFFu;
+#pragma unroll 1
+        for (int i = 0; i < kVpt; ++i) {
+            const int li = li_of(i);
+            if (li < cnt && li > consumed && (uint32_t)li < cand) {
+                const uint32_t incl = ch ? incl1[i] : incl0[i];
+                if (needs_step(dir, (spm >> i) & 1u, A, incl - base, lower, tq)) cand = (uint32_t)li;
+            }
+        }
+        const uint32_t first = block_reduce_u32(cand, MinU(), sh.red2);
+        if (first == 0xFFFFFFFFu) {
+            const uint32_t t = (ch ? tot1 : tot0) - base;
+            s = grid_value(ucur, dir > 0 ? A + t : A - t);
+            return -1;
+        }
+#pragma unroll 1
+        for (int i = 0; i < kVpt; ++i) {
+            if ((uint32_t)li_of(i) == first) {
+                const uint32_t incl = ch ? incl1[i] : incl0[i];
+                const uint32_t inc = ch ? inc1[i] : inc0[i];
+                const uint32_t excl = incl - inc - base;
+                const float before = grid_value(ucur, dir > 0 ? A + excl : A - excl);
+                float val = v[i];
+                if (!(exact & (1u << i))) {
+                    // the operation's result must not depend on where in the error bound v lies
+                    const uint32_t vb = __float_as_uint(val);
+                    const float lo = __uint_as_float(vb > 8u ? vb - 8u : 0u), hi = __uint_as_float(vb + 8u);
+                    const float rlo = dir > 0 ? __fadd_rn(before, lo) : __fsub_rn(before, lo);
+                    const float rhi = dir > 0 ? __fadd_rn(before, hi) : __fsub_rn(before, hi);
+                    if (rlo != rhi) {
+                        val = exactify(i);
+                        v[i] = val;
+                        exact |= 1u << i;
+                    }
+                }
+                const float after = dir > 0 ? __fadd_rn(before, val) : __fsub_rn(before, val);
+                const bool stop = dir > 0 ? after >= thr : after <= 0.0f;
+                sh.fstate = after;
+                sh.stop = stop ? (int)first : -1;
+                sh.ev_base0 = incl0[i];
+                sh.ev_base1 = incl1[i];
+                sh.events++;
+            }
+        }
+        __syncthreads();
+        cur = sh.fstate;
+        const int st = sh.stop;
+        base0 = sh.ev_base0;
+        base1 = sh.ev_base1;
+        if (st >= 0) {
+            s = cur;
+            return st;
+        }
+        consumed = (int)first;
+    }
+}
+
+// Exact sequential run over exact values by the calling thread alone (a short list, or
+// the start of the softmax sum where the running value crosses many binades).
+// Returns the stop position or -1 (sampler.rs:137-139, 148-151, 156-158).
+__device__ __forceinline__ int serial_run(const float* vals, int cnt, int dir, float& s, float thr) {
+    float cur = s;
+    for (int i = 0; i < cnt; ++i) {
+        cur = dir > 0 ? __fadd_rn(cur, vals[i]) : __fsub_rn(cur, vals[i]);
+        if (dir > 0 ? cur >= thr : cur <= 0.0f) {
+            s = cur;
+            return i;
+        }
+    }
+    s = cur;
+    return -1;
+}
+
 // All-ascending bitonic sort of n 64-bit keys (n <= cap, cap a power of two >= n is
 // not required: virtual +inf padding).  `keys` in shared or global memory.
-__device__ void bitonic_sort_u64(unsigned long long* keys, uint32_t n) {
+__device__ __noinline__ void bitonic_sort_u64(unsigned long long* keys, uint32_t n) {
     if (n < 2) return;
     uint32_t P = 1;
     while (P < n) P <<= 1;
@@ -319,16 +456,27 @@ __device__ void bitonic_sort_u64(unsigned long long* keys, uint32_t n) {
 }
 
 // k-th largest key (1-based rank kk) among keys[0..cnt) by radix select.
-__device__ uint32_t radix_select_desc(const float* x, uint32_t cnt, uint32_t kk, RowShared& sh) {
+__device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt, uint32_t kk, RowShared& sh) {
     uint32_t prefix = 0;
     for (int round = 0; round < 4; ++round) {
         const int shift = 24 - 8 * round;
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.hist256[i] = 0;
         __syncthreads();
-        for (uint32_t i = threadIdx.x; i < cnt; i += blockDim.x) {
-            const uint32_t key = fkey(x[i]);
-            const bool match = (round == 0) || ((key >> (shift + 8)) == (prefix >> (shift + 8)));
-            if (match) atomicAdd(&sh.hist256[(key >> shift) & 255u], 1u);
+        for (uint32_t i0 = 0; i0 < cnt; i0 += blockDim.x) {
+            const uint32_t i = i0 + threadIdx.x;
+            uint32_t key = 0;
+            bool match = false;
+            if (i < cnt) {
+                key = fkey(x[i]);
+                match = (round == 0) || ((key >> (shift + 8)) == (prefix >> (shift + 8)));
+            }
+            // warp-aggregated increments: candidates share high key bits
+            const unsigned act = __ballot_sync(0xFFFFFFFFu, match);
+            if (match) {
+                const uint32_t bin = (key >> shift) & 255u;
+                const unsigned peers = __match_any_sync(act, bin);
+                if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&sh.hist256[bin], (uint32_t)__popc(peers));
+            }
         }
         __syncthreads();
         if (threadIdx.x == 0) {
@@ -359,7 +507,7 @@ __device__ __forceinline__ float tie_margin(float vk, float m) {
 }
 
 // Compact the path-K candidate buffer to the elements >= (k-th largest - margin).
-__device__ void compact_candidates(float* cx, uint32_t* ci, uint32_t k, float mrun, RowShared& sh) {
+__device__ __noinline__ void compact_candidates(float* cx, uint32_t* ci, uint32_t k, float mrun, RowShared& sh) {
     const uint32_t cnt = min(sh.cand_n, (uint32_t)kKCap);
     if (cnt <= k) return;
     const uint32_t key = radix_select_desc(cx, cnt, k, sh);
@@ -417,6 +565,45 @@ __device__ __forceinline__ void load_sorted_tile(const unsigned long long* keys,
     }
 }
 
+struct NoExact {  // sorted probability tiles are exact already
+    __device__ float operator()(int) const { return 0.0f; }
+};
+
+// Penalise in place the elements of a staged tile (ids [gbase, gbase + cnt)) whose id
+// is in the row's window (sampler.rs:82-102): x > 0 ? x / p : x * p, once per id.
+__device__ __forceinline__ void patch_tile(float* t, uint32_t gbase, uint32_t cnt, const uint32_t* bitmap,
+                                           float penalty) {
+    const uint32_t w0 = gbase >> 5, w1 = (gbase + cnt - 1) >> 5;
+    for (uint32_t w = w0 + threadIdx.x; w <= w1; w += kThreads) {
+        uint32_t bits = bitmap[w];
+        while (bits) {
+            const int b = __ffs(bits) - 1;
+            bits &= bits - 1;
+            const uint32_t gi = (w << 5) + (uint32_t)b;
+            if (gi >= gbase && gi < gbase + cnt) {
+                const float x = t[gi - gbase];
+                t[gi - gbase] = x > 0.0f ? __fdiv_rn(x, penalty) : __fmul_rn(x, penalty);
+            }
+        }
+    }
+}
+
+// The scaled, shifted logit d = fl(fl(x * inv_t) - max) of sampler.rs:117 / ops.rs:409.
+__device__ __forceinline__ float d_of(float x, float inv_t, float mx) { return __fsub_rn(__fmul_rn(x, inv_t), mx); }
+
+// Largest (penalised) raw logit x with d_of(x) < thr, by bisection over the float order
+// (d_of is non-decreasing in x since inv_t >= 0).  -inf if there is none.
+__device__ __noinline__ float raw_threshold(float thr, float inv_t, float mx) {
+    uint32_t lo = fkey(__int_as_float(0xFF800000)), hi = fkey(__int_as_float(0x7F800000));
+    if (!(d_of(fkey_inv(lo), inv_t, mx) < thr)) return __int_as_float(0xFF800000);
+    if (d_of(fkey_inv(hi), inv_t, mx) < thr) return fkey_inv(hi);
+    while (hi - lo > 1) {  // invariant: d(lo) < thr <= d(hi)
+        const uint32_t mid = lo + (hi - lo) / 2;
+        if (d_of(fkey_inv(mid), inv_t, mx) < thr) lo = mid; else hi = mid;
+    }
+    return fkey_inv(lo);
+}
+
 // ------------------------------------------------------------------- the kernel ----
 extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(SampleArgs a) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -424,7 +611,9 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
     __shared__ float wsh[kWarps];
     __shared__ float gvs[kWarps];
     __shared__ uint32_t gis[kWarps];
-    __shared__ float etile[4];
+    __shared__ float red_f[kWarps];
+    __shared__ uint32_t red_u[kWarps];
+    __shared__ __align__(16) float etile[4];
     float* ring = reinterpret_cast<float*>(smem_raw);
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + (size_t)kStages * kChunk * 4);
     unsigned char* area = smem_raw + (size_t)kStages * kChunk * 4 + (size_t)a.bitmap_words * 4;
@@ -482,6 +671,17 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
         inf.r0 = 0.0f;
         inf.prob = 1.0f;
         inf.n_cand = 0;
+        inf.events = 0;
+        for (int q = 0; q < 8; ++q) inf.cycles[q] = 0;
+        inf.reserved = 0;
+        long long t_mark = clock64();
+        auto sat32 = [](long long d) -> uint32_t { return d > 0xFFFFFFFFll ? 0xFFFFFFFFu : (d < 0 ? 0u : (uint32_t)d); };
+        auto lap = [&](uint32_t& field) {
+            const long long now = clock64();
+            field = sat32(now - t_mark);
+            t_mark = now;
+        };
+        long long acc_wait = 0, acc_ord = 0, acc_thr = 0, acc_wait1 = 0, acc_sort = 0, acc_loop = 0, acc_red = 0;
         int32_t status = LRS_OK;
         uint32_t token = 0;
         float prob = 1.0f;
@@ -499,6 +699,10 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
             sh.delta_min = kInf;
             sh.vk = -kInf;
             sh.misc[7] = 0;
+            sh.events = 0;
+            sh.xthr_uu = 1000;
+            sh.misc[5] = 0;
+            sh.misc[6] = 0;
         }
         // penalty set: distinct ids of the window with id < n (sampler.rs:82-102)
         const uint32_t hlen = a.hist_len ? a.hist_len[r] : 0u;
@@ -519,48 +723,44 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 return x > 0.0f ? __fdiv_rn(x, penalty) : __fmul_rn(x, penalty);
             return x;
         };
-        auto xs_of = [&](float x, uint32_t gi) -> float { return __fmul_rn(penal(x, gi), inv_t); };
 
         if (n == 0) goto row_done;  // sampler.rs:57-60
 
         {
             // -------------------------------------------------------- pass 1 ----
+            // greedy: argmax (lowest index among maximal values); stochastic: NaN-aware
+            // max of the scaled logits and, on path K, the streaming top-k filter.
             float bv = -kInf;
             uint32_t bi = 0xFFFFFFFFu;
             float mx = -kInf;
             float theta = -kInf;
-            auto p1_elem = [&](float x, uint32_t gi, bool active) {
+            auto p1_value = [&](float x, uint32_t gi, bool act, bool& hit) {
                 if (greedy) {
-                    if (active) {
-                        const float xp = penal(x, gi);
-                        if (xp > bv || (xp == bv && gi < bi)) {
-                            bv = xp;
-                            bi = gi;
-                        }
+                    if (act && (x > bv || (x == bv && gi < bi))) {
+                        bv = x;
+                        bi = gi;
                     }
+                    hit = false;
                 } else {
-                    float xs = 0.0f;
-                    if (active) {
-                        xs = xs_of(x, gi);
-                        mx = fmax_nan(mx, xs);
-                    }
-                    if (pathK) {
-                        const bool hit = active && xs >= theta;
-                        const unsigned m = __ballot_sync(0xFFFFFFFFu, hit);
-                        if (m) {
-                            const int leader = __ffs(m) - 1;
-                            uint32_t base = 0;
-                            if (lane == leader) base = atomicAdd(&sh.cand_n, (uint32_t)__popc(m));
-                            base = __shfl_sync(0xFFFFFFFFu, base, leader);
-                            if (hit) {
-                                const uint32_t slot = base + __popc(m & ((1u << lane) - 1u));
-                                if (slot < (uint32_t)kKCap) {
-                                    cand_x[slot] = xs;
-                                    cand_i[slot] = gi;
-                                } else {
-                                    sh.cand_over = 1;
-                                }
-                            }
+                    const float xs = __fmul_rn(x, inv_t);
+                    if (act) mx = fmax_nan(mx, xs);
+                    hit = act && xs >= theta;
+                }
+            };
+            auto p1_append = [&](float x, uint32_t gi, bool hit) {
+                const unsigned m = __ballot_sync(0xFFFFFFFFu, hit);
+                if (m) {
+                    const int leader = __ffs(m) - 1;
+                    uint32_t base = 0;
+                    if (lane == leader) base = atomicAdd(&sh.cand_n, (uint32_t)__popc(m));
+                    base = __shfl_sync(0xFFFFFFFFu, base, leader);
+                    if (hit) {
+                        const uint32_t slot = base + __popc(m & ((1u << lane) - 1u));
+                        if (slot < (uint32_t)kKCap) {
+                            cand_x[slot] = __fmul_rn(x, inv_t);
+                            cand_i[slot] = gi;
+                        } else {
+                            sh.cand_over = 1;
                         }
                     }
                 }
@@ -573,26 +773,40 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 float x = 0.0f;
                 if (mine) {
                     gi = (uint32_t)tid < g.head ? (uint32_t)tid : g.head + (uint32_t)g.body + ((uint32_t)tid - g.head);
-                    x = g.row[gi];
+                    x = penal(g.row[gi], gi);
                 }
-                p1_elem(x, gi, mine);
+                bool hit;
+                p1_value(x, gi, mine, hit);
+                if (pathK) p1_append(x, gi, hit);
             }
             __syncthreads();
             for (uint32_t c = 0; c < g.nchunks; ++c) {
                 const int stage = ring_wait(sh, a, seq, timed_out);
-                const float* slot = ring + (size_t)stage * kChunk;
+                float* slot = ring + (size_t)stage * kChunk;
                 const uint32_t cnt = chunk_count(g, c);
                 const uint32_t gbase = g.head + c * kChunk;
+                if (pen_on) {
+                    patch_tile(slot, gbase, cnt, bitmap, penalty);
+                    __syncthreads();
+                }
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int li0 = li_of(j * 4);
                     const bool act = (uint32_t)li0 < cnt;
                     float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (act) q = *reinterpret_cast<const float4*>(slot + li0);
-                    p1_elem(q.x, gbase + li0 + 0, act);
-                    p1_elem(q.y, gbase + li0 + 1, act);
-                    p1_elem(q.z, gbase + li0 + 2, act);
-                    p1_elem(q.w, gbase + li0 + 3, act);
+                    const uint32_t gi = gbase + (uint32_t)li0;
+                    bool h0, h1, h2, h3;
+                    p1_value(q.x, gi + 0, act, h0);
+                    p1_value(q.y, gi + 1, act, h1);
+                    p1_value(q.z, gi + 2, act, h2);
+                    p1_value(q.w, gi + 3, act, h3);
+                    if (pathK && __any_sync(0xFFFFFFFFu, h0 | h1 | h2 | h3)) {
+                        p1_append(q.x, gi + 0, h0);
+                        p1_append(q.y, gi + 1, h1);
+                        p1_append(q.z, gi + 2, h2);
+                        p1_append(q.w, gi + 3, h3);
+                    }
                 }
                 __syncthreads();
                 ++seq;
@@ -601,8 +815,10 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                     if (sh.cand_over) {
                         pathK = false;
                     } else if (sh.cand_n > (uint32_t)(kKCap - kChunk)) {
+                        const long long tc0 = clock64();
                         const float mb = block_max_nan(mx, wsh);
                         compact_candidates(cand_x, cand_i, k, mb, sh);
+                        acc_wait1 += clock64() - tc0;
                         if (sh.cand_n > (uint32_t)(kKCap - kChunk)) pathK = false;
                     }
                     theta = sh.theta;
@@ -638,11 +854,13 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 if (x0 != x0 || ix == 0xFFFFFFFFu) ix = 0;
                 token = ix;
                 prob = 1.0f;
+                lap(inf.cycles[0]);
                 goto row_done;
             }
 
             // ---------------------------------------------- stochastic rows ----
             mx = block_max_nan(mx, wsh);
+            lap(inf.cycles[0]);
             inf.max = mx;
             // NaN scaled logit or infinite max -> NaN probabilities -> the reference
             // panics at sampler.rs:129/132 (n >= 2)
@@ -670,68 +888,202 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                     hcnt[i] = 0;
                     hmass[i] = 0.0f;
                 }
+            // raw threshold of the path-N histogram: elements with d >= -kNB/kBScale
+            const float xhist = (pathN && !bad) ? raw_threshold(-(float)(kNB - 1) / kBScale, inv_t, mx) : kInf;
             __syncthreads();
 
             // -------------------------------------------------------- pass 2 ----
             // exact sequential softmax denominator in index order (ops.rs:408-411)
             float S = 0.0f;
-            auto s_tile = [&](const float* src, uint32_t cnt, uint32_t gbase) {
+            auto count_bucket = [&](float x, bool live) {
+                // path N: warp-aggregated count of the element's (max - x) bucket
+                const bool c = pathN && live && x >= xhist;
+                const unsigned act = __ballot_sync(0xFFFFFFFFu, c);
+                if (c) {
+                    const int b = (int)fminf(-d_of(x, inv_t, mx) * kBScale, (float)(kNB - 1));
+                    const unsigned peers = __match_any_sync(act, b);
+                    if (lane == __ffs(peers) - 1) atomicAdd(&hcnt[b], (uint32_t)__popc(peers));
+                }
+            };
+            // One tile of values src[li], li in [start, cnt) (local positions = index order).
+            auto s_tile = [&](const float* src, uint32_t cnt, uint32_t gbase, uint32_t start) {
+                const int uu = unit_exp(S);
+                if (uu != sh.xthr_uu) {
+                    // elements with e < U/2 add nothing to S at this grid or any later one
+                    const long long t0 = clock64();
+                    __syncthreads();
+                    if (tid == 0) {
+                        sh.xthr = raw_threshold((float)(uu - 1) * 0.69314718f - 0.01f, inv_t, mx);
+                        sh.xthr_uu = uu;
+                    }
+                    __syncthreads();
+                    acc_thr += clock64() - t0;
+                }
+                const float xthr = sh.xthr;
+                const long long t_start = clock64();
+                const float bm = grid_value(uu, kTwo23);                      // magic base 2^23 * U
+                const float halfu = uu > -149 ? ldexpf(1.0f, uu - 1) : 0.0f;  // U / 2
                 float v[kVpt];
-                uint32_t exact = 0;
-                const int uu0 = unit_exp(S);
-                // e < U/2 adds nothing to S now or later in the row (U only grows)
-                const float thr_skip = pathN ? -kInf : (float)(uu0 - 1) * 0.69314718f - 0.01f;
 #pragma unroll
-                for (int i = 0; i < kVpt; ++i) {
-                    const int li = li_of(i);
-                    v[i] = 0.0f;
-                    if ((uint32_t)li < cnt) {
-                        const float dd = __fsub_rn(xs_of(src[li], gbase + li), mx);
-                        if (dd < thr_skip) {
-                            exact |= 1u << i;
-                        } else {
-                            if (dd == 0.0f) {
-                                v[i] = 1.0f;
-                                exact |= 1u << i;
-                            } else {
-                                v[i] = expf(dd);
-                            }
-                            if (pathN) {
-                                const int b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
-                                atomicAdd(&hcnt[b], 1u);
-                                atomicAdd(&hmass[b], v[i]);
-                            }
+                for (int i = 0; i < kVpt; ++i) v[i] = 0.0f;
+                uint32_t exact = 0xFFFFFFFFu;  // bit i clear: v[i] approximates libm's expf
+                float tot = 0.0f;
+                uint32_t nlive = 0;
+                uint32_t flags = 0;  // 1: tie or big element on the current grid
+                uint32_t live = 0;  // bit i: slot i is above the skip threshold
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int li0 = li_of(j * 4);
+                    float4 q = make_float4(-kInf, -kInf, -kInf, -kInf);
+                    if ((uint32_t)li0 < cnt && (uint32_t)li0 >= start) {  // start, body cnt: multiples of 4
+                        q = *reinterpret_cast<const float4*>(src + li0);
+                        if ((uint32_t)li0 + 1 >= cnt) q.y = -kInf;  // edge tiles hold < 4 values
+                        if ((uint32_t)li0 + 2 >= cnt) q.z = -kInf;
+                        if ((uint32_t)li0 + 3 >= cnt) q.w = -kInf;
+                    }
+                    if (pathN) {
+                        count_bucket(q.x, q.x != -kInf);
+                        count_bucket(q.y, q.y != -kInf);
+                        count_bucket(q.z, q.z != -kInf);
+                        count_bucket(q.w, q.w != -kInf);
+                    }
+                    live |= (q.x > xthr ? 1u : 0u) << (j * 4);
+                    live |= (q.y > xthr ? 2u : 0u) << (j * 4);
+                    live |= (q.z > xthr ? 4u : 0u) << (j * 4);
+                    live |= (q.w > xthr ? 8u : 0u) << (j * 4);
+                }
+#pragma unroll 1
+                while (live) {
+                    const int i = __ffs(live) - 1;
+                    live &= live - 1;
+                    ++nlive;
+                    const float x = src[li_of(i)];
+                    const float d = d_of(x, inv_t, mx);
+                    float e = d == 0.0f ? 1.0f : expf(d);
+                    bool ex = d == 0.0f;
+                    if (e >= bm) {
+                        flags = 1;  // big: ordered step
+                    } else if (halfu > 0.0f) {
+                        float inc = __fsub_rn(__fadd_rn(bm, e), bm);
+                        float rr = fabsf(__fsub_rn(e, inc));
+                        if (!ex && rr >= halfu - __fmul_rn(e, 4.76837158203125e-07f)) {  // 2^-21 > 2.5 ulp
+                            // near a rounding midpoint: take libm's exact value
+                            e = exact_expf(d, exptab);
+                            ex = true;
+                            inc = __fsub_rn(__fadd_rn(bm, e), bm);
+                            rr = fabsf(__fsub_rn(e, inc));
+                            if (e >= bm) flags = 1;
                         }
+                        if (ex && rr == halfu) flags = 1;  // tie: parity decides
+                        tot = __fadd_rn(tot, inc);
+                    } else {
+                        tot = __fadd_rn(tot, e);  // unit 2^-149: every float below 2^-125 is on the grid
+                    }
+                    v[i] = e;
+                    if (!ex) exact &= ~(1u << i);
+                }
+                const long long t_loop = clock64();
+                acc_loop += t_loop - t_start;
+                if (nlive) atomicAdd(&sh.misc[6], nlive);
+                // one reduction of (sum, flags)
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    tot = __fadd_rn(tot, __shfl_xor_sync(0xFFFFFFFFu, tot, o));
+                    flags |= __shfl_xor_sync(0xFFFFFFFFu, flags, o);
+                }
+                __syncthreads();
+                if (lane == 0) {
+                    red_f[tid >> 5] = tot;
+                    red_u[tid >> 5] = flags;
+                }
+                __syncthreads();
+                float T = red_f[0];
+                uint32_t F = red_u[0];
+                for (int w = 1; w < kWarps; ++w) {
+                    T = __fadd_rn(T, red_f[w]);
+                    F |= red_u[w];
+                }
+                acc_red += clock64() - t_loop;
+                if (!F) {
+                    // every increment is a multiple of U below 2^23 U: the float sum is exact
+                    // whenever the new value stays below the grid's top
+                    const float s2 = __fadd_rn(S, T);
+                    if (s2 < __fadd_rn(bm, bm)) {
+                        S = s2;
+                        return;
                     }
                 }
+                // a grid change, a tie or a big element inside the tile
                 auto exf = [&](int i) -> float {
                     const int li = li_of(i);
-                    return exact_expf(__fsub_rn(xs_of(src[li], gbase + li), mx), exptab);
+                    return exact_expf(d_of(src[li], inv_t, mx), exptab);
                 };
-                acc_tile(v, exact, (int)cnt, +1, S, kInf, exf, sh);
+                const long long t0 = clock64();
+                tile2(v, exact, (int)start, (int)cnt, +1, S, kInf, exf, sh);
+                acc_ord += clock64() - t0;
             };
-            if (!bad && g.head) {
-                if (tid < 4) etile[tid] = tid < (int)g.head ? g.row[tid] : 0.0f;
+            __shared__ float ser[kSerial + 4];
+            // Serial start: the head elements and the first kSerial elements of the first
+            // body tile, where the running sum crosses many binades, are added one by one
+            // by thread 0 after all threads computed their exact exps.
+            auto serial_start = [&](const float* body, uint32_t nbody) {
+                const uint32_t nh = g.head;
+                for (uint32_t q = tid; q < nh + nbody; q += kThreads) {
+                    const float x = q < nh ? penal(g.row[q], q) : body[q - nh];
+                    const float d = d_of(x, inv_t, mx);
+                    ser[q] = d == 0.0f ? 1.0f : exact_expf(d, exptab);
+                }
                 __syncthreads();
-                s_tile(etile, g.head, 0);
+                if (tid == 0) {
+                    float s = 0.0f;
+                    (void)serial_run(ser, (int)(nh + nbody), +1, s, kInf);
+                    sh.fstate = s;
+                }
                 __syncthreads();
-            }
+                S = sh.fstate;
+                __syncthreads();
+            };
+            if (!bad && g.nchunks == 0) serial_start(nullptr, 0);
             for (uint32_t c = 0; c < g.nchunks; ++c) {
+                const long long tw = clock64();
                 const int stage = ring_wait(sh, a, seq, timed_out);
-                const float* slot = ring + (size_t)stage * kChunk;
-                if (!bad) s_tile(slot, chunk_count(g, c), g.head + c * kChunk);
+                acc_wait += clock64() - tw;
+                float* slot = ring + (size_t)stage * kChunk;
+                const uint32_t cnt = chunk_count(g, c);
+                const uint32_t gbase = g.head + c * kChunk;
+                if (!bad) {
+                    if (pen_on) {
+                        patch_tile(slot, gbase, cnt, bitmap, penalty);
+                        __syncthreads();
+                    }
+                    uint32_t start = 0;
+                    if (c == 0) {
+                        start = min(cnt, (uint32_t)kSerial);
+                        serial_start(slot, start);
+                        // serial elements are still counted for the path-N histogram
+                        if (pathN)
+                            for (uint32_t q0 = 0; q0 < start; q0 += kThreads) {
+                                const uint32_t q = q0 + tid;
+                                count_bucket(q < start ? slot[q] : 0.0f, q < start);
+                            }
+                    }
+                    s_tile(slot, cnt, gbase, start);
+                }
                 __syncthreads();
                 ++seq;
                 if (tid == 0) ring_issue(sh, ring, g, first_load, total_loads, seq);
             }
             if (!bad && g.tail) {
                 const uint32_t tb = g.head + (uint32_t)g.body;
-                if (tid < 4) etile[tid] = tid < (int)g.tail ? g.row[tb + tid] : 0.0f;
+                if (tid < 4) etile[tid] = tid < (int)g.tail ? penal(g.row[tb + tid], tb + tid) : 0.0f;
                 __syncthreads();
-                s_tile(etile, g.tail, tb);
+                s_tile(etile, g.tail, tb, 0);
                 __syncthreads();
             }
+            if (!bad && pathN && g.head)  // head elements into the histogram
+                if (tid < 32) count_bucket(tid < (int)g.head ? penal(g.row[tid], tid) : 0.0f, tid < (int)g.head);
             inf.sum_exp = S;
+            lap(inf.cycles[1]);
             if (bad) {
                 status = LRS_E_NAN;
                 token = LRS_TOKEN_NONE;
@@ -743,7 +1095,6 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
             float sum = 0.0f;
             uint32_t cutoff = 0, pos = 0;
             unsigned long long chosen = 0;
-            bool drew = false;
             float rr = 0.0f;
             if (pathK) {
                 // -------------------------------------------------------- path K ----
@@ -754,49 +1105,65 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                     keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | cand_i[i];
                 }
                 __syncthreads();
+                const long long ts = clock64();
                 bitonic_sort_u64(keys, nk);  // (p desc, index asc)
+                acc_sort += clock64() - ts;
                 inf.n_cand = nk;
-                float v[kVpt];
-                uint32_t ex = 0xFFFFFFFFu;
-                load_sorted_tile(keys, k, v);
-                float cum = 0.0f;
-                auto noex = [&](int i) -> float { return v[i]; };
-                int stp = acc_tile(v, ex, (int)k, +1, cum, topp_on ? P.top_p : kInf, noex, sh);
-                cutoff = stp >= 0 ? (uint32_t)stp + 1 : k;  // sampler.rs:135-146
-                sum = cum;                                   // sampler.rs:148-151 (same sequence)
+                for (uint32_t i = tid; i < k; i += kThreads) ser[i] = __uint_as_float(~(uint32_t)(keys[i] >> 32));
+                __syncthreads();
+                if (tid == 0) {
+                    // top-p over the first k (sampler.rs:135-146); the survivor sum is the
+                    // same sequence up to the cutoff (sampler.rs:148-151)
+                    float cum = 0.0f;
+                    const int stp = serial_run(ser, (int)k, +1, cum, topp_on ? P.top_p : kInf);
+                    const uint32_t cut = stp >= 0 ? (uint32_t)stp + 1 : k;
+                    uint32_t ps = 0;
+                    float r0 = 0.0f;
+                    unsigned long long st2 = st;
+                    if (cum > 0.0f) {
+                        r0 = __fmul_rn(next_f32(&st2), cum);  // sampler.rs:155
+                        float r = r0;
+                        const int w = serial_run(ser, (int)cut, -1, r, 0.0f);
+                        ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
+                    }
+                    sh.misc[3] = cut;
+                    sh.misc[4] = ps;
+                    sh.fstate = cum;
+                    sh.vk = r0;
+                }
+                __syncthreads();
+                cutoff = sh.misc[3];
+                pos = sh.misc[4];
+                sum = sh.fstate;
+                rr = sh.vk;
                 if (sum > 0.0f) {
-                    rr = __fmul_rn(next_f32(&st), sum);      // sampler.rs:155
+                    (void)next_f32(&st);
                     inf.r0 = rr;
-                    float w[kVpt];
-                    uint32_t ex2 = 0xFFFFFFFFu;
-                    load_sorted_tile(keys, cutoff, w);
-                    auto noex2 = [&](int i) -> float { return w[i]; };
-                    stp = acc_tile(w, ex2, (int)cutoff, -1, rr, 0.0f, noex2, sh);
-                    pos = stp >= 0 ? (uint32_t)stp : cutoff - 1;  // sampler.rs:156-162
-                    drew = true;
-                } else {
-                    pos = 0;  // sampler.rs:152-154
                 }
                 chosen = keys[pos];
                 __syncthreads();
             } else {
                 // -------------------------------------------------------- path N ----
                 if (tid == 0) {
+                    // bucket limit: enough candidates for k and for top_p (+ margin); the
+                    // mass of bucket b is at least count * exp(-(b+1)/kBScale) / S
                     uint32_t cc = 0;
                     double mass = 0.0;
                     const double target = topp_on ? ((double)P.top_p + kTopPMargin) * (double)S : 1e300;
                     uint32_t b = 0;
-                    for (; b < (uint32_t)kNB; ++b) {
+                    for (; b < (uint32_t)kNB - 1; ++b) {
                         cc += hcnt[b];
-                        mass += (double)hmass[b];
+                        mass += (double)hcnt[b] * exp(-(double)(b + 1) / (double)kBScale);
                         if (cc >= k || mass >= target) break;
                     }
-                    sh.misc[3] = b < (uint32_t)kNB ? b : (uint32_t)(kNB - 1);
+                    sh.misc[3] = b;
                     uint32_t acc = 0;
-                    for (int q = 0; q < kNB; ++q) {
+                    for (int q = 0; q < kNB - 1; ++q) {
                         hoff[q] = acc;
                         acc += hcnt[q];
                     }
+                    hoff[kNB - 1] = acc;
+                    hcnt[kNB - 1] = n - acc;  // everything below the histogram range
                 }
                 __syncthreads();
                 const uint32_t blim = sh.misc[3];
@@ -805,14 +1172,42 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 __syncthreads();
                 // gather exact probabilities of buckets [blo, bhi] into scratch
                 auto gather = [&](uint32_t blo, uint32_t bhi) {
-                    for (uint32_t i = tid; i < n; i += kThreads) {
-                        const float dd = __fsub_rn(xs_of(g.row[i], i), mx);
-                        const int b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
-                        if ((uint32_t)b >= blo && (uint32_t)b <= bhi) {
-                            const float e = exact_expf(dd, exptab);
-                            const float p = __fmul_rn(e, inv);
-                            const uint32_t slot = hoff[b] + atomicAdd(&cursor[b], 1u);
-                            scratch[slot] = ((unsigned long long)(~__float_as_uint(p)) << 32) | i;
+                    const float xlo = raw_threshold(-(float)(bhi + 1) / kBScale, inv_t, mx);
+                    constexpr int kU = 4;  // independent elements per thread in flight
+                    for (uint32_t i0 = 0; i0 < n; i0 += kThreads * kU) {
+                        float xs[kU];
+#pragma unroll
+                        for (int u = 0; u < kU; ++u) {
+                            const uint32_t i = i0 + u * kThreads + tid;
+                            xs[u] = i < n ? g.row[i] : -kInf;
+                        }
+#pragma unroll
+                        for (int u = 0; u < kU; ++u) {
+                            const uint32_t i = i0 + u * kThreads + tid;
+                            bool take = false;
+                            int b = 0;
+                            float dd = 0.0f;
+                            if (i < n) {
+                                const float x = penal(xs[u], i);
+                                if (x > xlo || bhi == (uint32_t)kNB - 1) {
+                                    dd = d_of(x, inv_t, mx);
+                                    b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
+                                    if (!(x >= xhist)) b = kNB - 1;
+                                    take = (uint32_t)b >= blo && (uint32_t)b <= bhi;
+                                }
+                            }
+                            const unsigned act = __ballot_sync(0xFFFFFFFFu, take);
+                            if (take) {
+                                const float e = exact_expf(dd, exptab);
+                                const float pr = __fmul_rn(e, inv);
+                                const unsigned peers = __match_any_sync(act, b);
+                                const int leader = __ffs(peers) - 1;
+                                uint32_t base = 0;
+                                if (lane == leader) base = atomicAdd(&cursor[b], (uint32_t)__popc(peers));
+                                base = __shfl_sync(act, base, leader);
+                                const uint32_t slot = hoff[b] + base + __popc(peers & ((1u << lane) - 1u));
+                                scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
+                            }
                         }
                     }
                     __threadfence_block();
@@ -822,107 +1217,135 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 uint32_t gathered_to = blim;
                 inf.n_cand = hoff[blim] + hcnt[blim];
                 unsigned long long* sbuf = reinterpret_cast<unsigned long long*>(ring);
-                auto sort_bucket = [&](uint32_t b) {
-                    const uint32_t cnt = hcnt[b];
-                    unsigned long long* base = scratch + hoff[b];
-                    if (cnt <= (uint32_t)kSortCap) {
-                        for (uint32_t i = tid; i < cnt; i += kThreads) sbuf[i] = base[i];
-                        __syncthreads();
-                        bitonic_sort_u64(sbuf, cnt);
-                        for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = sbuf[i];
-                    } else {
-                        bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
+                uint32_t sorted_to = 0;  // buckets [0, sorted_to) sorted in scratch
+                // Sort bucket b (gathering more buckets first when b is beyond the gathered
+                // range, doubling the range each time).  Buckets are sorted in order.
+                auto ensure_bucket = [&](uint32_t b) {
+                    while (sorted_to <= b) {
+                        const uint32_t q = sorted_to;
+                        if (q > gathered_to) {
+                            const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
+                            gather(gathered_to + 1, hi);
+                            gathered_to = hi;
+                        }
+                        const uint32_t cnt = hcnt[q];
+                        if (cnt > 1) {
+                            const long long ts = clock64();
+                            unsigned long long* base = scratch + hoff[q];
+                            if (cnt <= (uint32_t)kSortCap) {
+                                for (uint32_t i = tid; i < cnt; i += kThreads) sbuf[i] = base[i];
+                                __syncthreads();
+                                bitonic_sort_u64(sbuf, cnt);
+                                for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = sbuf[i];
+                            } else {
+                                bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
+                            }
+                            __threadfence_block();
+                            __syncthreads();
+                            acc_sort += clock64() - ts;
+                        }
+                        ++sorted_to;
                     }
-                    __threadfence_block();
-                    __syncthreads();
                 };
-                // top-p scan over sorted buckets, capped at k survivors (sampler.rs:122-146)
-                float cum = 0.0f;
-                uint32_t done = 0;
-                bool stopped = false;
-                uint32_t sorted_to = 0;
-                for (uint32_t b = 0; b < (uint32_t)kNB && !stopped && done < k; ++b) {
-                    if (b > gathered_to) {
-                        gather(gathered_to + 1, kNB - 1);
-                        gathered_to = kNB - 1;
-                    }
-                    const uint32_t cnt = hcnt[b];
-                    sorted_to = b + 1;
-                    if (cnt == 0) continue;
-                    sort_bucket(b);
-                    const unsigned long long* base = scratch + hoff[b];
-                    for (uint32_t t0 = 0; t0 < cnt && !stopped && done < k; t0 += kChunk) {
-                        uint32_t tc = min((uint32_t)kChunk, cnt - t0);
-                        if (tc > k - done) tc = k - done;
+                auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(scratch[q] >> 32)); };
+                // Exact sequential run over sorted positions [0, p1) of the candidate sequence
+                // (buckets in order, each sorted when reached): the first kSerial positions
+                // one by one on thread 0, then tiles.  Returns the stop position or -1.
+                auto run = [&](uint32_t p1, int dir, float& s, float thr) -> int {
+                    uint32_t p = 0, b = 0;
+                    uint32_t serial_left = kSerial;
+                    while (p < p1) {
+                        while (b + 1 < (uint32_t)kNB && hoff[b] + hcnt[b] <= p) ++b;
+                        if (dir > 0) {
+                            // Every remaining candidate lies in bucket b or a later one; once
+                            // their probabilities are all below half the sum's grid unit no
+                            // later addition changes the sum (and none is a tie).
+                            const float emax = expf(-(float)b / kBScale) * 1.0001f;
+                            const float pmax = __fmul_rn(emax, inv) * 1.0001f;
+                            const int uu = unit_exp(s);
+                            if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
+                        }
+                        ensure_bucket(b);
+                        const uint32_t seg_end = min(p1, hoff[b] + hcnt[b]);
+                        if (serial_left > 0) {
+                            const uint32_t m = min(seg_end - p, serial_left);
+                            for (uint32_t q = tid; q < m; q += kThreads) ser[q] = pval(p + q);
+                            __syncthreads();
+                            if (tid == 0) {
+                                float s2 = s;
+                                sh.stop = serial_run(ser, (int)m, dir, s2, thr);
+                                sh.fstate = s2;
+                            }
+                            __syncthreads();
+                            s = sh.fstate;
+                            const int st0 = sh.stop;
+                            __syncthreads();
+                            if (st0 >= 0) return (int)p + st0;
+                            p += m;
+                            serial_left -= m;
+                            continue;
+                        }
+                        const uint32_t tc = min((uint32_t)kChunk, seg_end - p);
                         float v[kVpt];
                         uint32_t ex = 0xFFFFFFFFu;
-                        load_sorted_tile(base + t0, tc, v);
-                        auto noex = [&](int i) -> float { return v[i]; };
-                        const int stp = acc_tile(v, ex, (int)tc, +1, cum, topp_on ? P.top_p : kInf, noex, sh);
-                        if (stp >= 0) {
-                            stopped = true;
-                            done += (uint32_t)stp + 1;
-                        } else {
-                            done += tc;
+                        load_sorted_tile(scratch + p, tc, v);
+                        // single-grid fast check
+                        const int uu = unit_exp(s);
+                        const uint32_t A = grid_count(s, uu);
+                        uint32_t t = 0, f = 0;
+#pragma unroll
+                        for (int i = 0; i < kVpt; ++i) {
+                            if ((uint32_t)li_of(i) < tc) {
+                                const Cls c = classify(__float_as_uint(v[i]), uu);
+                                t = sat_add(t, c.inc);
+                                f |= (c.tie || c.big) ? 1u : 0u;
+                            }
                         }
+                        t = block_reduce_u32(t, SatAdd(), sh.red);
+                        f = block_reduce_u32(f, OrOp(), sh.red2);
+                        const float tq = (dir > 0 && thr < kInf) ? ldexpf(thr, -uu) : kInf;
+                        const bool fast = dir > 0 ? (!f && A + t <= kTwo24 - 1u && (float)(A + t) < tq)
+                                                  : (!f && t < A - grid_lower(uu));
+                        if (fast) {
+                            s = grid_value(uu, dir > 0 ? A + t : A - t);
+                        } else {
+                            const int stp = tile2(v, ex, 0, (int)tc, dir, s, thr, NoExact(), sh);
+                            if (stp >= 0) return (int)p + stp;
+                        }
+                        p += tc;
                     }
-                }
-                cutoff = done;
+                    return -1;
+                };
+                // top-p scan capped at k survivors (sampler.rs:122-146)
+                float cum = 0.0f;
+                int stp = run(k, +1, cum, topp_on ? P.top_p : kInf);
+                cutoff = stp >= 0 ? (uint32_t)stp + 1 : k;
                 sum = cum;
                 // draw (sampler.rs:152-162)
                 if (sum > 0.0f) {
                     rr = __fmul_rn(next_f32(&st), sum);
                     inf.r0 = rr;
-                    drew = true;
+                    float r = rr;
+                    stp = run(cutoff, -1, r, 0.0f);
+                    pos = stp >= 0 ? (uint32_t)stp : cutoff - 1;
+                } else {
+                    pos = 0;
                 }
-                uint32_t seen = 0;
-                bool found = false;
-                for (uint32_t b = 0; b < (uint32_t)kNB && !found && seen < cutoff; ++b) {
-                    const uint32_t cnt = hcnt[b];
-                    if (cnt == 0) continue;
-                    if (b >= sorted_to) {
-                        if (b > gathered_to) {
-                            gather(gathered_to + 1, kNB - 1);
-                            gathered_to = kNB - 1;
-                        }
-                        sort_bucket(b);
-                        sorted_to = b + 1;
-                    }
-                    const unsigned long long* base = scratch + hoff[b];
-                    for (uint32_t t0 = 0; t0 < cnt && !found && seen < cutoff; t0 += kChunk) {
-                        uint32_t tc = min((uint32_t)kChunk, cnt - t0);
-                        if (tc > cutoff - seen) tc = cutoff - seen;
-                        if (!drew) {  // sum <= 0: the first survivor (sampler.rs:152-154)
-                            found = true;
-                            pos = 0;
-                            chosen = base[t0];
-                            break;
-                        }
-                        float v[kVpt];
-                        uint32_t ex = 0xFFFFFFFFu;
-                        load_sorted_tile(base + t0, tc, v);
-                        auto noex = [&](int i) -> float { return v[i]; };
-                        const int stp = acc_tile(v, ex, (int)tc, -1, rr, 0.0f, noex, sh);
-                        if (stp >= 0) {
-                            found = true;
-                            pos = seen + (uint32_t)stp;
-                            chosen = base[t0 + stp];
-                        } else {
-                            chosen = base[t0 + tc - 1];
-                            seen += tc;
-                        }
-                    }
+                {
+                    uint32_t b = 0;
+                    while (b + 1 < (uint32_t)kNB && hoff[b] + hcnt[b] <= pos) ++b;
+                    ensure_bucket(b);
                 }
-                if (!found) pos = cutoff - 1;  // sampler.rs:162: the last survivor
+                chosen = scratch[pos];
                 __syncthreads();
             }
-            (void)drew;
             advance_state = true;
             token = (uint32_t)(chosen & 0xFFFFFFFFu);
             prob = __uint_as_float(~(uint32_t)(chosen >> 32));
             inf.cutoff = cutoff;
             inf.pos = pos;
             inf.surv_sum = sum;
+            lap(inf.cycles[2]);
         }
 
     row_done:
@@ -932,6 +1355,13 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
             inf.status = status;
             inf.token = token;
             inf.prob = prob;
+            inf.events = sh.events;
+            inf.cycles[3] = sat32(acc_wait1);
+            inf.cycles[4] = sat32(acc_ord);
+            inf.cycles[6] = sat32(acc_loop);
+            inf.reserved = sat32(acc_red) / 16u * 0 + sh.misc[5];
+            inf.cycles[5] = sat32(acc_red);
+            inf.cycles[7] = sat32(acc_sort);
             if (status == LRS_OK && advance_state) a.state[r] = st;
             a.tokens[r] = token;
             if (a.probs) a.probs[r] = prob;

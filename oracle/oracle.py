@@ -26,7 +26,8 @@ PARAMS_DTYPE = np.dtype([
 ROW_INFO_FIELDS = [
     ("status", "<i4"), ("token", "<u4"), ("path", "<u4"), ("k", "<u4"), ("cutoff", "<u4"),
     ("pos", "<u4"), ("max", "<f4"), ("sum_exp", "<f4"), ("surv_sum", "<f4"), ("r0", "<f4"),
-    ("prob", "<f4"), ("n_cand", "<u4"),
+    ("prob", "<f4"), ("n_cand", "<u4"), ("events", "<u4"), ("cycles", "<u4", (8,)),
+    ("reserved", "<u4"),
 ]
 INFO_DTYPE = np.dtype(ROW_INFO_FIELDS + [("flags", "<u4"), ("pad", "<u4")])
 

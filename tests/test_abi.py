@@ -41,7 +41,7 @@ def test_seed_state_is_seed_or_one(built_lib):
 
 def test_struct_layouts_match_header():
     assert lrs.PARAMS_DTYPE.itemsize == 24
-    assert lrs.ROW_INFO_DTYPE.itemsize == 48
+    assert lrs.ROW_INFO_DTYPE.itemsize == 88
 
 
 def test_create_without_gpu_returns_status(built_lib):
