@@ -137,6 +137,31 @@ int  lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint3
                        uint32_t* d_tokens, float* d_probs, int32_t* d_status,
                        lrs_row_info* d_info, void* stream);
 
+/* ---- batched sampling without allocation ----------------------------------------
+ * No counterpart in the reference (rust-llama has no GPU path); an addition for callers
+ * that cannot let a library allocate device memory, e.g. a server whose GPU memory is
+ * handed to its own pool at start-up, or a plug-in host that forbids allocations after
+ * initialisation.  Same computation and arguments as lrs_sample_device, without a
+ * context: the kernel's working memory is a fixed set of file-scope device arrays
+ * (LRS_NOALLOC_SCRATCH_BYTES of candidate scratch plus the libm-expf table), held on
+ * each GPU where the library's device code is loaded until the process exits.  Nothing
+ * is allocated by this call, and no per-row diagnostics are written.
+ *   device   the GPU that owns every buffer; the calling thread's current device is
+ *            restored before returning
+ *   n        1 <= n <= LRS_NOALLOC_MAX_VOCAB, otherwise LRS_E_INVALID
+ * The first call on a device sets that device up once (array addresses, table copy):
+ * make it outside any stream capture.  All calls on a device share the arrays, so calls
+ * whose kernels can overlap on the GPU race with each other: issue them on one stream.
+ * Returns LRS_OK once enqueued, LRS_E_INVALID for bad arguments (or a missing or
+ * mismatching libm-expf table), LRS_E_CUDA if a CUDA call failed; row errors go to
+ * d_status as with lrs_sample_device.                                                */
+#define LRS_NOALLOC_SCRATCH_BYTES (32u << 20)
+#define LRS_NOALLOC_MAX_VOCAB     262144u
+int  lrs_sample_device_noalloc(int device, const float* d_logits, uint32_t rows, uint32_t n, uint64_t ld,
+                               const uint32_t* d_hist, uint64_t hist_ld, const uint32_t* d_hist_len,
+                               const lrs_params* d_params, uint64_t* d_state,
+                               uint32_t* d_tokens, float* d_probs, int32_t* d_status, void* stream);
+
 /* ---- single-row drop-in (Sampler API) -------------------------------------------
  * lrs_sampler_new    replaces Sampler::new(seed)               (sampler.rs:33-37)
  * lrs_sampler_sample replaces Sampler::sample(logits, params, recent) (sampler.rs:56)
