@@ -44,7 +44,7 @@ struct lrs_ctx {
     unsigned long long* d_exp_index = nullptr;
     uint2* d_exp_entries = nullptr;
     unsigned long long* d_scratch = nullptr;
-    uint64_t scratch_stride = 0;
+    uint64_t scratch_stride = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0;
     uint32_t scratch_ctas = 0;
     uint32_t* d_counter = nullptr;
     int32_t* d_err = nullptr;
@@ -141,10 +141,7 @@ static int load_exp_table(lrs_ctx* ctx) {
     return LRS_OK;
 }
 
-static size_t dyn_smem_bytes(uint32_t n) {
-    const size_t bitmap_words = (n + 31) / 32;
-    return lrs_kernel_ring_bytes() + bitmap_words * 4 + lrs_kernel_area_bytes();
-}
+static size_t dyn_smem_bytes(uint32_t) { return lrs_kernel_smem_bytes(); }
 
 extern "C" {
 
@@ -225,7 +222,7 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     }
     ctx->ctas_per_sm = occ > 2 ? 2 : occ;
     ctx->scratch_ctas = (uint32_t)(ctx->num_sms * ctx->ctas_per_sm);
-    ctx->scratch_stride = max_vocab;
+    lrs_kernel_scratch_layout(max_vocab, &ctx->scratch_stride, &ctx->bitmap_off, &ctx->tiles_off, &ctx->lanes_off);
     const size_t R = max_rows;
     CKF(cudaMalloc(&ctx->d_params, R * sizeof(lrs_params)));
     CKF(cudaMalloc(&ctx->d_state, R * sizeof(unsigned long long)));
@@ -235,6 +232,7 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     CKF(cudaMalloc(&ctx->d_hist, R * (size_t)(max_hist ? max_hist : 1) * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_hist_len, R * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
+    CKF(cudaMemset(ctx->d_scratch, 0, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
     CKF(cudaMalloc(&ctx->d_counter, sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_err, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_err, 0, sizeof(int32_t)));
@@ -314,9 +312,11 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.exp_entries = ctx->d_exp_entries;
     args.scratch = ctx->d_scratch;
     args.scratch_stride = ctx->scratch_stride;
+    args.bitmap_off = ctx->bitmap_off;
+    args.tiles_off = ctx->tiles_off;
+    args.lanes_off = ctx->lanes_off;
     args.row_counter = ctx->d_counter;
     args.err_flag = ctx->d_err;
-    args.bitmap_words = (n + 31) / 32;
     uint32_t grid = ctx->scratch_ctas;
     if (grid > rows) grid = rows;
     CK(cudaMemsetAsync(ctx->d_counter, 0, sizeof(uint32_t), s));

@@ -7,16 +7,32 @@
 //   softmax (ops.rs:397-419), top-k (122-132), top-p (135-146), survivor sum (148-151)
 //   and the categorical draw with the row's xorshift64* state (152-162).
 //
-// Structure: a persistent CTA (two per SM) takes rows from a global counter.  A row
-// is streamed through a 3-stage ring of 16 KB bulk copies (TMA engine, mbarrier
-// completion) twice: pass 1 reads it from HBM (L2 evict_last) for the max / argmax
-// and a streaming top-k candidate filter; pass 2 re-reads it from L2 (evict_first)
-// and computes the softmax denominator with the exact sequential-f32 emulation of
-// lrs_device.cuh.  The top-k / top-p / draw phase then works on candidates only:
-//   path K (top_k <= kKMax): candidates from the pass-1 filter, sorted in shared memory;
-//   path N (top_k off or large): candidates bucketed by (max - x) during pass 2,
-//          gathered with exact probabilities into global scratch and sorted bucket by
-//          bucket in shared memory as the top-p scan and the draw reach them.
+// Structure.  A persistent CTA (two per SM) has eight consumer warps and one producer
+// warp.  The producer takes rows from a global counter, passes them to the consumers
+// through a small row queue and streams each row through a ring of 4 KB shared-memory
+// slots with bulk copies (TMA engine; a slot's `full` mbarrier completes on the bytes,
+// its `empty` mbarrier is released by the warp that consumed it): once for pass 1 and,
+// for stochastic rows, once more for pass 2.  A slot holds one tile of 1024 floats;
+// consumer warp w takes tiles w, w+8, w+16, ... and each lane owns a run of 32
+// consecutive elements of the tile.
+//   pass 1  per tile: the max (NaN-propagating), the argmax of greedy rows, the tile's
+//           online-softmax statistics (its max and the sum of exp relative to it) and,
+//           on path K, a per-warp streaming top-k filter.
+//   prep    the row max; from the tile statistics an estimate of the running softmax
+//           sum at every tile start with a proven relative error bound, hence the
+//           lowest binade grid the exact running sum can be on there and a threshold
+//           below which an element cannot change it.  Tiles without a live element are
+//           skipped by pass 2.
+//   pass 2  per lane, the increments of its run on the two grids the running sum can
+//           be on over that run (lrs_grid.h).  The exact running sum is then handed
+//           from tile to tile (a baton in shared memory); each hand-over is one warp
+//           scan of the 32 lane increments, and only a run with a binade crossing, a
+//           tie, an element of half a binade or a missed grid is summed element by
+//           element with hardware f32 adds.
+//   finish  path K (top_k <= kKMax): the filter's candidates sorted in shared memory;
+//           path N: candidates bucketed by (max - x) during pass 2, gathered with exact
+//           probabilities into global scratch and sorted bucket by bucket as the top-p
+//           scan and the draw reach them (sampler.rs:122-162).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -27,44 +43,78 @@
 
 namespace lrs {
 
-constexpr int kKMax = 256;          // path K handles 1 <= k <= kKMax (k < n)
-constexpr int kKCap = 4608;         // path K candidate buffer (entries)
-constexpr int kKSortMax = 2048;     // path K candidates kept after the final compaction
-constexpr int kNB = 2048;           // path N buckets of width 1/32 in (max - x)
+constexpr int kTile = 1024;          // floats per ring slot = one warp tile
+constexpr int kSlots = 12;           // ring depth
+constexpr int kRowQ = 4;             // row queue depth
+constexpr int kBlock = kThreads + 32;  // consumer warps + the producer warp
+constexpr int kKMax = 128;           // path K handles 1 <= k <= kKMax (k < n)
+constexpr int kWCap = 256;           // per-warp path-K candidate buffer (entries)
+constexpr int kKCap = kWarps * kWCap;  // union of the warp buffers
+constexpr int kKSortMax = 2048;      // path K candidates kept after the final compaction
+constexpr int kNB = 2048;            // path N buckets of width 1/32 in (max - x)
 constexpr float kBScale = 32.0f;
-constexpr int kSortCap = 4096;      // largest bucket sorted in shared memory
+constexpr int kSortCap = 4096;       // largest bucket sorted in shared memory
 constexpr float kTopPMargin = 0.002f;
-constexpr int kSerial = 512;        // elements summed one by one at the start of a row or scan
-constexpr unsigned long long kWaitLimit = 1ull << 26;
+constexpr int kSerial = 512;         // elements summed one by one at the start of a scan
+constexpr int kTilesSmem = 256;      // tile records kept in shared memory (larger rows: global)
+constexpr int kUBase = 149;          // skip-threshold table index = grid exponent + kUBase
+constexpr int kNU = 288;
+constexpr uint32_t kSumLive = 1u << 16;   // tile record flags
+constexpr uint32_t kHistLive = 1u << 17;
+constexpr long long kWaitCycles = 1ll << 32;  // bound of every wait (about 2 s)
+constexpr float kLog2e = 1.44269504f;
+
+// dynamic shared memory (bytes)
+constexpr size_t kRingBytes = (size_t)kSlots * kTile * 4;
+constexpr size_t kRegionABytes = (size_t)kNB * 8;     // warp candidate buffers | path-N counts + offsets
+constexpr size_t kRegionBBytes = (size_t)kSortCap * 8;  // warp radix counts | candidates + keys | bucket sort
+constexpr size_t kTTabBytes = (size_t)kTilesSmem * 16;
+constexpr size_t kDynSmem = kRingBytes + kRegionABytes + kRegionBBytes + kTTabBytes;
+static_assert(kRegionABytes >= (size_t)kKCap * 8, "warp candidate buffers");
+static_assert(kRegionBBytes >= (size_t)kKCap * 8 + (size_t)kKSortMax * 8, "candidates and sort keys");
+static_assert(kRegionBBytes >= (size_t)kWarps * 256 * 4, "per-warp radix counts");
+static_assert(kRegionBBytes >= (size_t)kNB * 4, "bucket cursors");
 
 using SampleArgs = lrs_kernel_args_t;
 
 // ---------------------------------------------------------------- shared state ----
 struct RowShared {
-    uint64_t bar[kStages];
+    uint64_t full[kSlots];
+    uint64_t empty[kSlots];
+    uint64_t rq_full[kRowQ];
+    uint64_t rq_empty[kRowQ];
+    uint32_t rq_row[kRowQ];
+    volatile uint32_t abort;   // a wait ran out: every later wait returns at once
+    volatile uint32_t bseq;    // baton: the tile whose chain step may run
+    volatile float bval;       // baton: exact running sum before that tile
     uint32_t red[kWarps + 2];
     uint32_t red2[kWarps + 2];
-    float fstate;          // running exact value broadcast
-    int32_t stop;          // stop position broadcast
+    float fstate;
+    int32_t stop;
     uint32_t cand_n;
     uint32_t cand_over;
     float theta;
     float delta_min;
     uint32_t hist256[256];
-    uint32_t row;
-    uint32_t issued;       // ring loads issued so far (thread 0)
-    float vk;              // k-th largest scaled logit at the last compaction
-    uint32_t events;       // ordered steps taken by acc_tile for this row
-    uint32_t ev_base0, ev_base1;  // tile2: prefixes at the last ordered step
-    float xthr;            // pass-2 skip threshold on (penalised) raw logits
-    int xthr_uu;           // grid exponent xthr was computed for
+    float vk;
+    uint32_t events;
+    uint32_t ev_base0, ev_base1;
     uint32_t misc[8];
+    float wmax[kWarps];
+    float gvs[kWarps];
+    uint32_t gis[kWarps];
+    uint32_t wcnt[kWarps];
+    float wdelta[kWarps];
+    uint32_t wover;
+    float xhist;
+    float xthr[kNU];
+    float ser[kSerial + 4];
+    lrs_row_info info;     // the row's diagnostics, assembled by thread 0
 };
 
 struct Geo {
     const float* row;
-    uint32_t n, head, tail, nchunks;
-    uint64_t body;  // elements in the aligned body
+    uint32_t n, head, tail, nchunks, body;  // body: elements in the 16-byte aligned middle
 };
 
 __device__ __forceinline__ Geo row_geometry(const SampleArgs& a, uint32_t r) {
@@ -75,51 +125,81 @@ __device__ __forceinline__ Geo row_geometry(const SampleArgs& a, uint32_t r) {
     uint32_t head = (uint32_t)(((16u - (uint32_t)(p & 15u)) & 15u) >> 2);
     if (head > g.n) head = g.n;
     g.head = head;
-    g.body = ((uint64_t)(g.n - head) / 4u) * 4u;
-    g.tail = g.n - head - (uint32_t)g.body;
-    g.nchunks = (uint32_t)((g.body + kChunk - 1) / kChunk);
+    g.body = ((g.n - head) / 4u) * 4u;
+    g.tail = g.n - head - g.body;
+    g.nchunks = (g.body + kTile - 1) / kTile;
     return g;
 }
 
 __device__ __forceinline__ uint32_t chunk_count(const Geo& g, uint32_t c) {
-    const uint64_t left = g.body - (uint64_t)c * kChunk;
-    return (uint32_t)(left < (uint64_t)kChunk ? left : (uint64_t)kChunk);
+    const uint32_t left = g.body - c * kTile;
+    return left < (uint32_t)kTile ? left : (uint32_t)kTile;
 }
 
-// ---------------------------------------------------------------- ring pipeline ----
-// Loads of one row are numbered in consumption order: chunk c of pass p is the row's
-// load p * nchunks + c; `first` is the CTA-wide number of the row's first load.  Load q
-// lands in stage q % kStages and completes phase (q / kStages) & 1 of that stage's
-// mbarrier.  Called by thread 0 only; issues while fewer than kStages loads are pending.
-__device__ __forceinline__ void ring_issue(RowShared& s, float* ring, const Geo& g, uint32_t first,
-                                           uint32_t total, uint32_t consumed) {
-    while (s.issued < first + total && s.issued - consumed < (uint32_t)kStages) {
-        const uint32_t local = s.issued - first;
-        const uint32_t pass = local / g.nchunks, c = local % g.nchunks;
-        const uint32_t stage = s.issued % kStages;
-        const uint32_t bytes = chunk_count(g, c) * 4u;
-        const float* src = g.row + g.head + (uint64_t)c * kChunk;
-        fence_proxy_async_smem();
-        mbar_expect_tx(&s.bar[stage], bytes);
-        bulk_load(ring + (size_t)stage * kChunk, src, bytes, &s.bar[stage],
-                  pass == 0 ? policy_evict_last() : policy_evict_first());
-        s.issued++;
-    }
+// Streaming passes over a row: pass 2 exists for stochastic rows with n >= 2
+// (sampler.rs:62 and 104: temperature <= 0 is greedy, NaN is not).
+__device__ __forceinline__ uint32_t row_passes(const lrs_params& P, uint32_t n) {
+    if (n == 0) return 0u;
+    const bool stochastic = !(P.temperature <= 0.0f);
+    return (stochastic && n >= 2) ? 2u : 1u;
 }
 
-// Wait (bounded) until load number q has landed; returns its stage.
-__device__ __forceinline__ int ring_wait(RowShared& s, const SampleArgs& a, uint32_t q, bool& timed_out) {
-    const uint32_t stage = q % kStages;
-    const uint32_t parity = (q / kStages) & 1u;
-    unsigned long long it = 0;
-    while (!mbar_try_wait(&s.bar[stage], parity)) {
-        if (++it > kWaitLimit) {
-            timed_out = true;
-            atomicExch(a.err_flag, LRS_E_TIMEOUT);
-            break;
+// Bounded wait on an mbarrier phase.  On timeout the CTA's abort flag and the sticky
+// error word are set; every later wait then returns false at once, so all warps run
+// their (bounded) loops to the end and leave.
+__device__ __forceinline__ bool wait_bar(RowShared& sh, uint64_t* bar, uint32_t parity, int32_t* err) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (sh.abort) return false;
+        if (clock64() - t0 > kWaitCycles) {
+            sh.abort = 1u;
+            atomicExch(err, LRS_E_TIMEOUT);
+            return false;
         }
     }
-    return (int)stage;
+    return true;
+}
+
+// ------------------------------------------------------------- producer warp ----
+// One thread: takes rows, publishes them in the row queue, and issues the bulk copies
+// of every tile of every pass in the order the consumers take them (load q lands in
+// slot q % kSlots and completes phase (q / kSlots) & 1 of its `full` barrier).
+__device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float* ring) {
+    const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
+    uint32_t q = 0, rqi = 0;
+    for (;;) {
+        const uint32_t qs = rqi % kRowQ, use = rqi / kRowQ;
+        if (use > 0 && !wait_bar(sh, &sh.rq_empty[qs], (use - 1) & 1u, a.err_flag)) break;
+        const uint32_t r = sh.abort ? a.rows : atomicAdd(a.row_counter, 1u);
+        sh.rq_row[qs] = r < a.rows ? r : a.rows;
+        mbar_arrive(&sh.rq_full[qs]);
+        ++rqi;
+        if (r >= a.rows) break;
+        const Geo g = row_geometry(a, r);
+        const uint32_t passes = row_passes(a.params[r], g.n);
+        bool ok = true;
+        for (uint32_t p = 0; p < passes && ok; ++p)
+            for (uint32_t c = 0; c < g.nchunks; ++c) {
+                const uint32_t s = q % kSlots, use2 = q / kSlots;
+                if (use2 > 0 && !wait_bar(sh, &sh.empty[s], (use2 - 1) & 1u, a.err_flag)) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t bytes = chunk_count(g, c) * 4u;
+                mbar_expect_tx(&sh.full[s], bytes);
+                bulk_load(ring + (size_t)s * kTile, g.row + g.head + (size_t)c * kTile, bytes, &sh.full[s],
+                          p == 0 ? pol_keep : pol_drop);
+                ++q;
+            }
+        if (!ok) break;
+    }
+    // Leave no copy in flight behind: wait (bounded, ignoring the abort flag) for the
+    // last kSlots loads to land.
+    for (uint32_t j = q > (uint32_t)kSlots ? q - kSlots : 0u; j < q; ++j) {
+        const long long t0 = clock64();
+        while (!mbar_try_wait(&sh.full[j % kSlots], (j / kSlots) & 1u))
+            if (clock64() - t0 > kWaitCycles) break;
+    }
 }
 
 // --------------------------------------------------------------- block helpers ----
@@ -147,9 +227,9 @@ __device__ __forceinline__ uint32_t block_incl_scan(const uint32_t (&inc)[kVpt],
     uint32_t wt = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) wt = sat_add(wt, jtot[j]);
-    __syncthreads();
+    csync();
     if (l == 0) sh[w] = wt;
-    __syncthreads();
+    csync();
     uint32_t off = 0, total = 0;
     for (int i = 0; i < kWarps; ++i) {
         if (i < w) off = sat_add(off, sh[i]);
@@ -283,10 +363,10 @@ __device__ __noinline__ int acc_tile(float (&v)[kVpt], uint32_t& exact, int cnt,
                 sh.events++;
             }
         }
-        __syncthreads();
+        csync();
         cur = sh.fstate;
         const int st = sh.stop;
-        __syncthreads();
+        csync();
         if (st >= 0) {
             s = cur;
             return st;
@@ -393,7 +473,7 @@ __device__ __noinline__ int tile2(float (&v)[kVpt], uint32_t& exact, int start, 
                 sh.events++;
             }
         }
-        __syncthreads();
+        csync();
         cur = sh.fstate;
         const int st = sh.stop;
         base0 = sh.ev_base0;
@@ -430,7 +510,7 @@ __device__ __noinline__ void bitonic_sort_u64(unsigned long long* keys, uint32_t
     while (P < n) P <<= 1;
     for (uint32_t size = 2; size <= P; size <<= 1) {
         for (uint32_t stride = size >> 1; stride > 0; stride >>= 1) {
-            for (uint32_t t = threadIdx.x; t < P / 2; t += blockDim.x) {
+            for (uint32_t t = threadIdx.x; t < P / 2; t += kThreads) {
                 const uint32_t grp = t / stride, off = t % stride;
                 uint32_t i, j;
                 if (stride == (size >> 1)) {
@@ -450,7 +530,7 @@ __device__ __noinline__ void bitonic_sort_u64(unsigned long long* keys, uint32_t
                     }
                 }
             }
-            __syncthreads();
+            csync();
         }
     }
 }
@@ -460,9 +540,9 @@ __device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt,
     uint32_t prefix = 0;
     for (int round = 0; round < 4; ++round) {
         const int shift = 24 - 8 * round;
-        for (int i = threadIdx.x; i < 256; i += blockDim.x) sh.hist256[i] = 0;
-        __syncthreads();
-        for (uint32_t i0 = 0; i0 < cnt; i0 += blockDim.x) {
+        for (int i = threadIdx.x; i < 256; i += kThreads) sh.hist256[i] = 0;
+        csync();
+        for (uint32_t i0 = 0; i0 < cnt; i0 += kThreads) {
             const uint32_t i = i0 + threadIdx.x;
             uint32_t key = 0;
             bool match = false;
@@ -478,7 +558,7 @@ __device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt,
                 if ((threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&sh.hist256[bin], (uint32_t)__popc(peers));
             }
         }
-        __syncthreads();
+        csync();
         if (threadIdx.x == 0) {
             uint32_t acc = 0;
             int d = 255;
@@ -491,17 +571,17 @@ __device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt,
             sh.misc[1] = (uint32_t)d;
             sh.misc[2] = kk - acc;
         }
-        __syncthreads();
+        csync();
         prefix |= sh.misc[1] << shift;
         kk = sh.misc[2];
-        __syncthreads();
+        csync();
     }
     return prefix;
 }
 
-// Margin below the k-th value inside which probabilities may tie (see DESIGN notes in
-// the host documentation): distinct scaled logits closer than this can round to the
-// same probability.
+// Margin below the k-th value inside which probabilities may tie: distinct scaled
+// logits closer than this can round to the same probability (it is generous by more
+// than a factor of 4 over the rounding steps of d = x - max, exp and p = e * inv).
 __device__ __forceinline__ float tie_margin(float vk, float m) {
     return ldexpf(fabsf(vk) + fabsf(m) + 1.0f, -18);
 }
@@ -527,9 +607,9 @@ __device__ __noinline__ void compact_candidates(float* cx, uint32_t* ci, uint32_
             ++have;
         }
     }
-    __syncthreads();
+    csync();
     if (threadIdx.x == 0) sh.cand_n = 0;
-    __syncthreads();
+    csync();
     uint32_t base = atomicAdd(&sh.cand_n, (uint32_t)have);
     for (int q = 0; q < have; ++q) {
         cx[base + q] = xv[q];
@@ -540,21 +620,9 @@ __device__ __noinline__ void compact_candidates(float* cx, uint32_t* ci, uint32_
         if (delta < sh.delta_min) sh.delta_min = delta;
         sh.vk = vk;
     }
-    __syncthreads();
+    csync();
 }
 
-
-// Block-wide max of a per-thread value (NaN-propagating).
-__device__ __forceinline__ float block_max_nan(float m, float* wsh) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) wsh[threadIdx.x >> 5] = m;
-    __syncthreads();
-    float r = wsh[0];
-    for (int w = 1; w < kWarps; ++w) r = fmax_nan(r, wsh[w]);
-    return r;
-}
 
 // Loads a tile of up to kChunk sorted 64-bit keys (p desc, index asc) as probabilities.
 __device__ __forceinline__ void load_sorted_tile(const unsigned long long* keys, uint32_t cnt, float (&v)[kVpt]) {
@@ -568,25 +636,6 @@ __device__ __forceinline__ void load_sorted_tile(const unsigned long long* keys,
 struct NoExact {  // sorted probability tiles are exact already
     __device__ float operator()(int) const { return 0.0f; }
 };
-
-// Penalise in place the elements of a staged tile (ids [gbase, gbase + cnt)) whose id
-// is in the row's window (sampler.rs:82-102): x > 0 ? x / p : x * p, once per id.
-__device__ __forceinline__ void patch_tile(float* t, uint32_t gbase, uint32_t cnt, const uint32_t* bitmap,
-                                           float penalty) {
-    const uint32_t w0 = gbase >> 5, w1 = (gbase + cnt - 1) >> 5;
-    for (uint32_t w = w0 + threadIdx.x; w <= w1; w += kThreads) {
-        uint32_t bits = bitmap[w];
-        while (bits) {
-            const int b = __ffs(bits) - 1;
-            bits &= bits - 1;
-            const uint32_t gi = (w << 5) + (uint32_t)b;
-            if (gi >= gbase && gi < gbase + cnt) {
-                const float x = t[gi - gbase];
-                t[gi - gbase] = x > 0.0f ? __fdiv_rn(x, penalty) : __fmul_rn(x, penalty);
-            }
-        }
-    }
-}
 
 // The scaled, shifted logit d = fl(fl(x * inv_t) - max) of sampler.rs:117 / ops.rs:409.
 __device__ __forceinline__ float d_of(float x, float inv_t, float mx) { return __fsub_rn(__fmul_rn(x, inv_t), mx); }
@@ -604,44 +653,563 @@ __device__ __noinline__ float raw_threshold(float thr, float inv_t, float mx) {
     return fkey_inv(lo);
 }
 
-// ------------------------------------------------------------------- the kernel ----
-extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(SampleArgs a) {
-    extern __shared__ __align__(128) unsigned char smem_raw[];
-    __shared__ RowShared sh;
-    __shared__ float wsh[kWarps];
-    __shared__ float gvs[kWarps];
-    __shared__ uint32_t gis[kWarps];
-    __shared__ float red_f[kWarps];
-    __shared__ uint32_t red_u[kWarps];
-    __shared__ __align__(16) float etile[4];
-    float* ring = reinterpret_cast<float*>(smem_raw);
-    uint32_t* bitmap = reinterpret_cast<uint32_t*>(smem_raw + (size_t)kStages * kChunk * 4);
-    unsigned char* area = smem_raw + (size_t)kStages * kChunk * 4 + (size_t)a.bitmap_words * 4;
-    float* cand_x = reinterpret_cast<float*>(area);
-    uint32_t* cand_i = reinterpret_cast<uint32_t*>(area + kKCap * 4);
-    uint32_t* hcnt = reinterpret_cast<uint32_t*>(area);            // path N bucket counts
-    float* hmass = reinterpret_cast<float*>(area + kNB * 4);       // path N bucket mass, then cursors
-    uint32_t* hoff = reinterpret_cast<uint32_t*>(area + kNB * 8);  // path N bucket offsets
-    unsigned long long* scratch = a.scratch + (uint64_t)blockIdx.x * a.scratch_stride;
-    const ExpTable exptab{a.exp_index, a.exp_entries};
-    const float kInf = __int_as_float(0x7F800000);
 
+// ------------------------------------------------------------- warp helpers ----
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ float warp_max_nan(float m) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmax_nan(m, __shfl_xor_sync(0xFFFFFFFFu, m, o));
+    return m;
+}
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_incl_scan_f(float v) {
+    const int l = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float t = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (l >= o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ uint32_t warp_incl_scan_plain(uint32_t v) {
+    const int l = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, v, o);
+        if (l >= o) v += t;
+    }
+    return v;
+}
+
+// Register slot i of a lane's run holds run offset run_pos(i): float4 number j = i / 4
+// is read from offset 4 * ((j + lane) & 7), so the eight lanes of a shared-memory
+// phase read eight different bank groups.
+__device__ __forceinline__ uint32_t run_pos(int i, int lane) {
+    return (uint32_t)((((i >> 2) + lane) & 7) * 4 + (i & 3));
+}
+
+// The lane's run of a tile (offsets [32 * lane, 32 * lane + 32)), -inf past nval.
+__device__ __forceinline__ void load_run(const float* slot, int lane, uint32_t nval, float (&v)[32]) {
+    const float ninf = __int_as_float(0xFF800000);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+        float4 q = make_float4(ninf, ninf, ninf, ninf);
+        if (c4 < nval) q = *reinterpret_cast<const float4*>(slot + lane * 32 + c4);
+        v[4 * j + 0] = q.x;
+        v[4 * j + 1] = q.y;
+        v[4 * j + 2] = q.z;
+        v[4 * j + 3] = q.w;
+    }
+}
+
+// Penalty bits of ids [gi0, gi0 + 32) from the row's window bitmap (global, read at L2
+// so that the bits set by this CTA's atomics are seen).
+__device__ __forceinline__ uint32_t lane_bits(const uint32_t* bm, uint32_t gi0) {
+    const uint32_t w = gi0 >> 5, s = gi0 & 31u;
+    const uint32_t lo = __ldcg(bm + w);
+    if (!s) return lo;
+    const uint32_t hi = __ldcg(bm + w + 1);
+    return (lo >> s) | (hi << (32u - s));
+}
+
+// x > 0 ? x / p : x * p (sampler.rs:96-100).
+__device__ __noinline__ float penalise(float x, float p) { return x > 0.0f ? __fdiv_rn(x, p) : __fmul_rn(x, p); }
+
+// Applies the penalty to the register slots whose run offsets have their bit set
+// (rare: a window of W ids touches at most W runs of a row).
+__device__ __forceinline__ void apply_penalty(float (&v)[32], uint32_t bits, int lane, float pen) {
+    while (bits) {
+        const int pos = __ffs(bits) - 1;
+        bits &= bits - 1u;
+        const int slot = ((((pos >> 2) - lane) & 7) << 2) | (pos & 3);
+        float x = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i == slot) x = v[i];
+        x = penalise(x, pen);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+            if (i == slot) v[i] = x;
+    }
+}
+
+// Adds, one after the other, the exponentials held by lanes [lo, lo + cnt) to s; every
+// lane returns the same sum (ops.rs:408-411).  e is CUDA's expf(d), within 2 ulp of
+// exp, unless `exact`; where the rounding of an addition could depend on where libm's
+// value lies within that bound, that lane's exact value (exact_expf(d)) is taken.
+__device__ __noinline__ float warp_serial_add(float s, float e, float d, bool exact, int lo, int cnt,
+                                              const ExpTable& tab) {
+    const int lane = threadIdx.x & 31;
+    const unsigned apx = __ballot_sync(0xFFFFFFFFu, !exact);
+    for (int j = lo; j < lo + cnt; ++j) {
+        float ej = __shfl_sync(0xFFFFFFFFu, e, j);
+        if ((apx >> j) & 1u) {
+            const uint32_t b = __float_as_uint(ej);
+            const float elo = __uint_as_float(b > 4u ? b - 4u : 0u), ehi = __uint_as_float(b + 4u);
+            if (__fadd_rn(s, elo) != __fadd_rn(s, ehi)) {
+                float ex = 0.0f;
+                if (lane == j) ex = exact_expf(d, tab);
+                ej = __shfl_sync(0xFFFFFFFFu, ex, j);
+            }
+        }
+        s = __fadd_rn(s, ej);
+    }
+    return s;
+}
+
+// kk-th largest (1-based) of x[0..cnt) in shared memory, by one warp: radix select on
+// the order-preserving key, 8 bits a round.  hist: 256 words owned by the warp.
+__device__ __noinline__ float warp_kth_desc(const float* x, uint32_t cnt, uint32_t kk, uint32_t* hist) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0;
+    for (int round = 0; round < 4; ++round) {
+        const int shift = 24 - 8 * round;
+        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for (uint32_t i = lane; i < cnt; i += 32) {
+            const uint32_t key = fkey(x[i]);
+            if (round == 0 || (key >> (shift + 8)) == (prefix >> (shift + 8)))
+                atomicAdd(&hist[(key >> shift) & 255u], 1u);
+        }
+        __syncwarp();
+        uint32_t c[8], s = 0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            c[e] = hist[255 - 8 * lane - e];  // digits in descending order
+            s += c[e];
+        }
+        const uint32_t incl = warp_incl_scan_plain(s), excl = incl - s;
+        const unsigned own = __ballot_sync(0xFFFFFFFFu, excl < kk && kk <= incl);
+        uint32_t d = 0, rem = 0;
+        if (excl < kk && kk <= incl) {
+            uint32_t acc = excl;
+            bool found = false;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                if (!found && acc + c[e] >= kk) {
+                    d = (uint32_t)(255 - 8 * lane - e);
+                    rem = kk - acc;
+                    found = true;
+                }
+                acc += c[e];
+            }
+        }
+        const int owner = own ? __ffs(own) - 1 : 0;
+        d = __shfl_sync(0xFFFFFFFFu, d, owner);
+        rem = __shfl_sync(0xFFFFFFFFu, rem, owner);
+        prefix |= d << shift;
+        kk = rem;
+        __syncwarp();
+    }
+    return fkey_inv(prefix);
+}
+
+// Path-K state of one warp's streaming filter.
+struct WState {
+    uint32_t wcnt;  // candidates buffered
+    float theta;    // append threshold
+    float wdelta;   // smallest compaction margin so far
+};
+
+// Raise the warp's threshold to (k-th largest buffered - tie margin) and drop the
+// buffered entries below it (the warp-scope form of compact_candidates).
+__device__ __noinline__ WState warp_compact(float* wx, uint32_t* wi, WState s, uint32_t k, float mrun,
+                                            uint32_t* hist) {
+    const int lane = threadIdx.x & 31;
+    __syncwarp();
+    if (s.wcnt <= k) return s;
+    const float vk = warp_kth_desc(wx, s.wcnt, k, hist);
+    const float delta = tie_margin(vk, mrun);
+    const float th = vk - delta;
+    s.wdelta = fminf(s.wdelta, delta);
+    if (th > s.theta) s.theta = th;
+    uint32_t out = 0;
+    for (uint32_t b = 0; b < s.wcnt; b += 32) {
+        const uint32_t i = b + (uint32_t)lane;
+        const bool keep = i < s.wcnt && wx[i] >= th;
+        const float xv = keep ? wx[i] : 0.0f;
+        const uint32_t iv = keep ? wi[i] : 0u;
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, keep);
+        __syncwarp();
+        if (keep) {
+            const uint32_t p = out + (uint32_t)__popc(m & ((1u << lane) - 1u));
+            wx[p] = xv;
+            wi[p] = iv;
+        }
+        out += (uint32_t)__popc(m);
+        __syncwarp();
+    }
+    s.wcnt = out;
+    return s;
+}
+
+// ------------------------------------------------------------ finish phases ----
+// Row context of the top-k / top-p / draw phase (sampler.rs:122-162).
+struct FinishCtx {
+    Geo g;
+    const float4* tt;               // tile records (max of the scaled logits in .x)
+    unsigned long long* scratch;    // path N: gathered (p, index) keys
+    const uint32_t* bitmap;         // window bitmap
+    uint32_t* hcnt;                 // path N: bucket counts and offsets
+    uint32_t* hoff;
+    uint32_t* cursor;
+    unsigned long long* sbuf;       // path N: bucket sort buffer (aliases cursor)
+    float* cand_x;                  // path K: candidates and sort keys
+    uint32_t* cand_i;
+    unsigned long long* keys;
+    ExpTable exptab;
+    uint32_t k, nk;
+    float mx, inv_t, inv, S, penalty, top_p, xhist;
+    bool pen_on, topp_on;
+    unsigned long long st;          // PRNG state (advanced by the draw)
+    uint32_t cutoff, pos, n_cand;   // results
+    float sum, rr, r0;
+    unsigned long long chosen;
+    long long acc_sort;
+};
+
+// Path K: sort the candidates, then top-p, survivor sum and draw on thread 0.
+__device__ __noinline__ void finish_path_k(RowShared& sh, FinishCtx& f) {
+    const int tid = threadIdx.x;
+    const float kInf = __int_as_float(0x7F800000);
+    for (uint32_t i = tid; i < f.nk; i += kThreads) {
+        const float e = exact_expf(__fsub_rn(f.cand_x[i], f.mx), f.exptab);
+        const float p = __fmul_rn(e, f.inv);
+        f.keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | f.cand_i[i];
+    }
+    csync();
+    const long long ts = clock64();
+    bitonic_sort_u64(f.keys, f.nk);  // (p desc, index asc)
+    f.acc_sort += clock64() - ts;
+    f.n_cand = f.nk;
+    for (uint32_t i = tid; i < f.k; i += kThreads) sh.ser[i] = __uint_as_float(~(uint32_t)(f.keys[i] >> 32));
+    csync();
+    if (tid == 0) {
+        // top-p over the first k (sampler.rs:135-146); the survivor sum is the
+        // same sequence up to the cutoff (sampler.rs:148-151)
+        float cum = 0.0f;
+        const int stp = serial_run(sh.ser, (int)f.k, +1, cum, f.topp_on ? f.top_p : kInf);
+        const uint32_t cut = stp >= 0 ? (uint32_t)stp + 1 : f.k;
+        uint32_t ps = 0;
+        float r0 = 0.0f;
+        unsigned long long st2 = f.st;
+        if (cum > 0.0f) {
+            r0 = __fmul_rn(next_f32(&st2), cum);  // sampler.rs:155
+            float rv = r0;
+            const int w = serial_run(sh.ser, (int)cut, -1, rv, 0.0f);
+            ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
+        }
+        sh.misc[3] = cut;
+        sh.misc[4] = ps;
+        sh.fstate = cum;
+        sh.vk = r0;
+    }
+    csync();
+    f.cutoff = sh.misc[3];
+    f.pos = sh.misc[4];
+    f.sum = sh.fstate;
+    f.rr = sh.vk;
+    if (f.sum > 0.0f) {
+        (void)next_f32(&f.st);
+        f.r0 = f.rr;
+    }
+    f.chosen = f.keys[f.pos];
+    csync();
+}
+
+// Path N: gather bucket by bucket, sort lazily, scan with the exact emulation.
+__device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     const int tid = threadIdx.x;
     const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const float kInf = __int_as_float(0x7F800000);
+    auto penal_g = [&](float x, uint32_t gi) -> float {  // sampler.rs:96-100
+        if (f.pen_on && ((__ldcg(f.bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, f.penalty);
+        return x;
+    };
     if (tid == 0) {
-        for (int i = 0; i < kStages; ++i) mbar_init(&sh.bar[i], 1);
-        fence_barrier_init();
-        sh.issued = 0;
+        // bucket limit: enough candidates for k and for top_p (+ margin); the
+        // mass of bucket b is at least count * exp(-(b+1)/kBScale) / S
+        uint32_t cc = 0;
+        double mass = 0.0;
+        const double target = f.topp_on ? ((double)f.top_p + kTopPMargin) * (double)f.S : 1e300;
+        uint32_t b = 0;
+        for (; b < (uint32_t)kNB - 1; ++b) {
+            cc += f.hcnt[b];
+            mass += (double)f.hcnt[b] * exp(-(double)(b + 1) / (double)kBScale);
+            if (cc >= f.k || mass >= target) break;
+        }
+        sh.misc[3] = b;
+        uint32_t acc = 0;
+        for (int q = 0; q < kNB - 1; ++q) {
+            f.hoff[q] = acc;
+            acc += f.hcnt[q];
+        }
+        f.hoff[kNB - 1] = acc;
+        f.hcnt[kNB - 1] = f.g.n - acc;  // everything below the histogram range
     }
-    for (uint32_t i = tid; i < a.bitmap_words; i += kThreads) bitmap[i] = 0;
-    __syncthreads();
-    uint32_t seq = 0;  // ring loads consumed by this CTA (same value in every thread)
+    csync();
+    const uint32_t blim = sh.misc[3];
+    // gather exact probabilities of buckets [blo, bhi] into scratch; tiles whose
+    // max lies below the range are skipped
+    auto gather = [&](uint32_t blo, uint32_t bhi) {
+        const float xlo = raw_threshold(-(float)(bhi + 1) / kBScale, f.inv_t, f.mx);
+        const bool all = bhi == (uint32_t)kNB - 1;
+        const float dlim = -(float)(bhi + 1) / kBScale;
+        const float xh = f.xhist;
+        for (uint32_t q = blo + tid; q <= bhi; q += kThreads) f.cursor[q] = 0;
+        csync();
+        auto take = [&](uint32_t i, float xr, bool valid) {
+            bool tk = false;
+            int b = 0;
+            float dd = 0.0f;
+            if (valid) {
+                const float x = penal_g(xr, i);
+                if (x > xlo || all) {
+                    dd = d_of(x, f.inv_t, f.mx);
+                    b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
+                    if (!(x >= xh)) b = kNB - 1;
+                    tk = (uint32_t)b >= blo && (uint32_t)b <= bhi;
+                }
+            }
+            const unsigned act = __ballot_sync(0xFFFFFFFFu, tk);
+            if (tk) {
+                const float e = exact_expf(dd, f.exptab);
+                const float pr = __fmul_rn(e, f.inv);
+                const unsigned peers = __match_any_sync(act, b);
+                const int leader = __ffs(peers) - 1;
+                uint32_t base = 0;
+                if (lane == leader) base = atomicAdd(&f.cursor[b], (uint32_t)__popc(peers));
+                base = __shfl_sync(peers, base, leader);
+                const uint32_t slot = f.hoff[b] + base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
+                f.scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
+            }
+        };
+        if (warp == 0) {
+            const uint32_t edges = f.g.head + f.g.tail;
+            const bool mine = (uint32_t)lane < edges;
+            const uint32_t gi =
+                (uint32_t)lane < f.g.head ? (uint32_t)lane : f.g.head + f.g.body + ((uint32_t)lane - f.g.head);
+            take(gi, mine ? f.g.row[gi] : 0.0f, mine);
+        }
+        for (uint32_t t = 0; t < f.g.nchunks; ++t) {
+            if (!all && __fsub_rn(f.tt[t].x, f.mx) < dlim) continue;
+            const uint32_t cnt = chunk_count(f.g, t), tb = f.g.head + t * kTile;
+            constexpr int kU = kTile / kThreads;
+            float xs[kU];
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t i = (uint32_t)(u * kThreads + tid);
+                xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
+            }
+#pragma unroll
+            for (int u = 0; u < kU; ++u) {
+                const uint32_t i = (uint32_t)(u * kThreads + tid);
+                take(tb + i, xs[u], i < cnt);
+            }
+        }
+        __threadfence_block();
+        csync();
+    };
+    gather(0, blim);
+    uint32_t gathered_to = blim;
+    f.n_cand = f.hoff[blim] + f.hcnt[blim];
+    uint32_t sorted_to = 0;  // buckets [0, sorted_to) sorted in scratch
+    // Sort bucket b (gathering more buckets first when b is beyond the gathered
+    // range, doubling the range each time).  Buckets are sorted in order.
+    auto ensure_bucket = [&](uint32_t b) {
+        while (sorted_to <= b) {
+            const uint32_t q = sorted_to;
+            if (q > gathered_to) {
+                const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
+                gather(gathered_to + 1, hi);
+                gathered_to = hi;
+            }
+            const uint32_t cnt = f.hcnt[q];
+            if (cnt > 1) {
+                const long long ts = clock64();
+                unsigned long long* base = f.scratch + f.hoff[q];
+                if (cnt <= (uint32_t)kSortCap) {
+                    for (uint32_t i = tid; i < cnt; i += kThreads) f.sbuf[i] = base[i];
+                    csync();
+                    bitonic_sort_u64(f.sbuf, cnt);
+                    for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
+                } else {
+                    bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
+                }
+                __threadfence_block();
+                csync();
+                f.acc_sort += clock64() - ts;
+            }
+            ++sorted_to;
+        }
+    };
+    auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(f.scratch[q] >> 32)); };
+    // Exact sequential run over sorted positions [0, p1) of the candidate sequence
+    // (buckets in order, each sorted when reached): the first kSerial positions
+    // one by one on thread 0, then tiles.  Returns the stop position or -1.
+    auto run = [&](uint32_t p1, int dir, float& s, float thr) -> int {
+        uint32_t p = 0, b = 0;
+        uint32_t serial_left = kSerial;
+        while (p < p1) {
+            while (b + 1 < (uint32_t)kNB && f.hoff[b] + f.hcnt[b] <= p) ++b;
+            if (dir > 0) {
+                // Every remaining candidate lies in bucket b or a later one; once
+                // their probabilities are all below half the sum's grid unit no
+                // later addition changes the sum (and none is a tie).
+                const float emax = expf(-(float)b / kBScale) * 1.0001f;
+                const float pmax = __fmul_rn(emax, f.inv) * 1.0001f;
+                const int uu = unit_exp(s);
+                if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
+            }
+            ensure_bucket(b);
+            const uint32_t seg_end = min(p1, f.hoff[b] + f.hcnt[b]);
+            if (serial_left > 0) {
+                const uint32_t m = min(seg_end - p, serial_left);
+                for (uint32_t q = tid; q < m; q += kThreads) sh.ser[q] = pval(p + q);
+                csync();
+                if (tid == 0) {
+                    float s2 = s;
+                    sh.stop = serial_run(sh.ser, (int)m, dir, s2, thr);
+                    sh.fstate = s2;
+                }
+                csync();
+                s = sh.fstate;
+                const int st0 = sh.stop;
+                csync();
+                if (st0 >= 0) return (int)p + st0;
+                p += m;
+                serial_left -= m;
+                continue;
+            }
+            const uint32_t tc = min((uint32_t)kChunk, seg_end - p);
+            float v[kVpt];
+            uint32_t ex = 0xFFFFFFFFu;
+            load_sorted_tile(f.scratch + p, tc, v);
+            // single-grid fast check
+            const int uu = unit_exp(s);
+            const uint32_t A = grid_count(s, uu);
+            uint32_t t = 0, f = 0;
+#pragma unroll
+            for (int i = 0; i < kVpt; ++i) {
+                if ((uint32_t)li_of(i) < tc) {
+                    const Cls c = classify(__float_as_uint(v[i]), uu);
+                    t = sat_add(t, c.inc);
+                    f |= (c.tie || c.big) ? 1u : 0u;
+                }
+            }
+            t = block_reduce_u32(t, SatAdd(), sh.red);
+            f = block_reduce_u32(f, OrOp(), sh.red2);
+            const float tq = (dir > 0 && thr < kInf) ? ldexpf(thr, -uu) : kInf;
+            const bool fast = dir > 0 ? (!f && A + t <= kTwo24 - 1u && (float)(A + t) < tq)
+                                      : (!f && t < A - grid_lower(uu));
+            if (fast) {
+                s = grid_value(uu, dir > 0 ? A + t : A - t);
+            } else {
+                const int stp = tile2(v, ex, 0, (int)tc, dir, s, thr, NoExact(), sh);
+                if (stp >= 0) return (int)p + stp;
+            }
+            p += tc;
+        }
+        return -1;
+    };
+    // top-p scan capped at k survivors (sampler.rs:122-146)
+    float cum = 0.0f;
+    int stp = run(f.k, +1, cum, f.topp_on ? f.top_p : kInf);
+    f.cutoff = stp >= 0 ? (uint32_t)stp + 1 : f.k;
+    f.sum = cum;
+    // draw (sampler.rs:152-162)
+    if (f.sum > 0.0f) {
+        f.rr = __fmul_rn(next_f32(&f.st), f.sum);
+        f.r0 = f.rr;
+        float rv = f.rr;
+        stp = run(f.cutoff, -1, rv, 0.0f);
+        f.pos = stp >= 0 ? (uint32_t)stp : f.cutoff - 1;
+    } else {
+        f.pos = 0;
+    }
+    {
+        uint32_t b = 0;
+        while (b + 1 < (uint32_t)kNB && f.hoff[b] + f.hcnt[b] <= f.pos) ++b;
+        ensure_bucket(b);
+    }
+    f.chosen = f.scratch[f.pos];
+    csync();
+}
 
+// ------------------------------------------------------------------- the kernel ----
+extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleArgs a) {
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    __shared__ RowShared sh;
+    float* ring = reinterpret_cast<float*>(smem_raw);
+    unsigned char* regA = smem_raw + kRingBytes;
+    unsigned char* regB = regA + kRegionABytes;
+    float4* ttab_s = reinterpret_cast<float4*>(regB + kRegionBBytes);
+    float* wbx = reinterpret_cast<float*>(regA);                                  // pass 1, path K
+    uint32_t* wbi = reinterpret_cast<uint32_t*>(regA + (size_t)kKCap * 4);
+    uint32_t* hcnt = reinterpret_cast<uint32_t*>(regA);                           // pass 2 on, path N
+    uint32_t* hoff = reinterpret_cast<uint32_t*>(regA + (size_t)kNB * 4);
+    uint32_t* whist = reinterpret_cast<uint32_t*>(regB);                          // pass 1, path K
+    float* cand_x = reinterpret_cast<float*>(regB);                               // finish, path K
+    uint32_t* cand_i = reinterpret_cast<uint32_t*>(regB + (size_t)kKCap * 4);
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(regB + (size_t)kKCap * 8);
+    unsigned long long* sbuf = reinterpret_cast<unsigned long long*>(regB);      // finish, path N
+    uint32_t* cursor = reinterpret_cast<uint32_t*>(regB);
+    unsigned long long* scratch = a.scratch + (uint64_t)blockIdx.x * a.scratch_stride;
+    uint32_t* bitmap = reinterpret_cast<uint32_t*>(scratch + a.bitmap_off);
+    float4* ttab_g = reinterpret_cast<float4*>(scratch + a.tiles_off);
+    float* lrec = reinterpret_cast<float*>(scratch + a.lanes_off);  // per tile: 32 lane sums (pass 1)
+    const ExpTable exptab{a.exp_index, a.exp_entries};
+    const float kInf = __int_as_float(0x7F800000);
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+
+    if (tid == 0) {
+        for (int i = 0; i < kSlots; ++i) {
+            mbar_init(&sh.full[i], 1);
+            mbar_init(&sh.empty[i], 1);
+        }
+        for (int i = 0; i < kRowQ; ++i) {
+            mbar_init(&sh.rq_full[i], 1);
+            mbar_init(&sh.rq_empty[i], 1);
+        }
+        sh.abort = 0u;
+        sh.bseq = 0xFFFFFFFFu;
+        fence_barrier_init();
+    }
+    __syncthreads();
+    if (warp == kWarps) {  // the producer warp
+        if (lane == 0) producer(a, sh, ring);
+        return;
+    }
+
+    uint32_t qbase = 0;  // loads of earlier rows (same count in every consumer thread)
+    uint32_t rqi = 0;
     for (;;) {
-        if (tid == 0) sh.row = atomicAdd(a.row_counter, 1u);
-        __syncthreads();
-        const uint32_t r = sh.row;
-        __syncthreads();
+        if (tid == 0) {
+            const uint32_t qs = rqi % kRowQ;
+            uint32_t rr = a.rows;
+            if (wait_bar(sh, &sh.rq_full[qs], (rqi / kRowQ) & 1u, a.err_flag)) rr = sh.rq_row[qs];
+            mbar_arrive(&sh.rq_empty[qs]);
+            sh.misc[0] = rr;
+        }
+        ++rqi;
+        csync();
+        const uint32_t r = sh.misc[0];
         if (r >= a.rows) break;
 
         const lrs_params P = a.params[r];
@@ -657,53 +1225,42 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
         const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;           // sampler.rs:136
         bool pathK = stochastic && n >= 2 && k < n && k <= (uint32_t)kKMax;
         unsigned long long st = a.state[r];
+        const uint32_t passes = row_passes(P, n);
+        const uint32_t q1 = qbase, q2 = qbase + g.nchunks;  // load numbers of tile 0 of each pass
+        qbase += passes * g.nchunks;
+        float4* const tt = g.nchunks <= (uint32_t)kTilesSmem ? ttab_s : ttab_g;
 
-        lrs_row_info inf;
-        inf.status = LRS_OK;
-        inf.token = 0;
-        inf.path = greedy ? (fast_greedy ? 0u : 1u) : (n == 1 ? 3u : 2u);
-        inf.k = k;
-        inf.cutoff = 0;
-        inf.pos = 0;
-        inf.max = 0.0f;
-        inf.sum_exp = 0.0f;
-        inf.surv_sum = 0.0f;
-        inf.r0 = 0.0f;
-        inf.prob = 1.0f;
-        inf.n_cand = 0;
-        inf.events = 0;
-        for (int q = 0; q < 8; ++q) inf.cycles[q] = 0;
-        inf.reserved = 0;
+        lrs_row_info& inf = sh.info;  // written by thread 0 only
+        if (tid == 0) {
+            inf.status = LRS_OK;
+            inf.token = 0;
+            inf.path = greedy ? (fast_greedy ? 0u : 1u) : (n == 1 ? 3u : 2u);
+            inf.k = k;
+            inf.cutoff = 0;
+            inf.pos = 0;
+            inf.max = 0.0f;
+            inf.sum_exp = 0.0f;
+            inf.surv_sum = 0.0f;
+            inf.r0 = 0.0f;
+            inf.prob = 1.0f;
+            inf.n_cand = 0;
+            inf.events = 0;
+            for (int q = 0; q < 8; ++q) inf.cycles[q] = 0;
+            inf.reserved = 0;
+        }
         long long t_mark = clock64();
         auto sat32 = [](long long d) -> uint32_t { return d > 0xFFFFFFFFll ? 0xFFFFFFFFu : (d < 0 ? 0u : (uint32_t)d); };
-        auto lap = [&](uint32_t& field) {
+        auto lap = [&](int q) {
             const long long now = clock64();
-            field = sat32(now - t_mark);
+            if (tid == 0) inf.cycles[q] = sat32(now - t_mark);
             t_mark = now;
         };
-        long long acc_wait = 0, acc_ord = 0, acc_thr = 0, acc_wait1 = 0, acc_sort = 0, acc_loop = 0, acc_red = 0;
+        long long acc_full = 0, acc_baton = 0, acc_chain = 0, acc_sort = 0;
         int32_t status = LRS_OK;
         uint32_t token = 0;
         float prob = 1.0f;
-        bool timed_out = false;
         bool advance_state = false;
 
-        const bool need_pass2 = stochastic && n >= 2;
-        const uint32_t total_loads = n == 0 ? 0u : g.nchunks * (need_pass2 ? 2u : 1u);
-        const uint32_t first_load = seq;
-        if (tid == 0) {
-            ring_issue(sh, ring, g, first_load, total_loads, seq);
-            sh.cand_n = 0;
-            sh.cand_over = 0;
-            sh.theta = -kInf;
-            sh.delta_min = kInf;
-            sh.vk = -kInf;
-            sh.misc[7] = 0;
-            sh.events = 0;
-            sh.xthr_uu = 1000;
-            sh.misc[5] = 0;
-            sh.misc[6] = 0;
-        }
         // penalty set: distinct ids of the window with id < n (sampler.rs:82-102)
         const uint32_t hlen = a.hist_len ? a.hist_len[r] : 0u;
         const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
@@ -715,120 +1272,172 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 if (t < n) atomicOr(&bitmap[t >> 5], 1u << (t & 31));
             }
         }
-        __syncthreads();
+        if (tid == 0) {
+            sh.cand_n = 0;
+            sh.cand_over = 0;
+            sh.theta = -kInf;
+            sh.delta_min = kInf;
+            sh.vk = -kInf;
+            sh.misc[7] = 0;
+            sh.events = 0;
+            sh.wover = 0;
+        }
+        csync();
 
         const float inv_t = stochastic ? __fdiv_rn(1.0f, temperature) : 1.0f;  // sampler.rs:115
-        auto penal = [&](float x, uint32_t gi) -> float {                     // sampler.rs:96-100
-            if (pen_on && ((bitmap[gi >> 5] >> (gi & 31)) & 1u))
-                return x > 0.0f ? __fdiv_rn(x, penalty) : __fmul_rn(x, penalty);
+        auto penal_g = [&](float x, uint32_t gi) -> float {                   // sampler.rs:96-100
+            if (pen_on && ((__ldcg(bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, penalty);
             return x;
+        };
+
+        // penalty bits of this lane's run of tile t (loaded one tile ahead of use)
+        auto tile_bits = [&](uint32_t t) -> uint32_t {
+            const uint32_t c = chunk_count(g, t), o = (uint32_t)lane * 32u;
+            const uint32_t nv = o < c ? min(32u, c - o) : 0u;
+            if (!pen_on || !nv) return 0u;
+            return lane_bits(bitmap, g.head + t * kTile + o) & (nv >= 32u ? 0xFFFFFFFFu : ((1u << nv) - 1u));
         };
 
         if (n == 0) goto row_done;  // sampler.rs:57-60
 
         {
             // -------------------------------------------------------- pass 1 ----
-            // greedy: argmax (lowest index among maximal values); stochastic: NaN-aware
-            // max of the scaled logits and, on path K, the streaming top-k filter.
-            float bv = -kInf;
+            float m_w = -kInf;          // warp: running max of the scaled logits
+            float bv = -kInf;           // lane: greedy best value and index
             uint32_t bi = 0xFFFFFFFFu;
-            float mx = -kInf;
-            float theta = -kInf;
-            auto p1_value = [&](float x, uint32_t gi, bool act, bool& hit) {
+            WState ws{0u, -kInf, kInf};  // warp: path-K filter
+            bool kact = pathK;          // warp: still filtering
+            float* wx = wbx + warp * kWCap;
+            uint32_t* wi = wbi + warp * kWCap;
+            uint32_t* wh = whist + warp * 256;
+
+            // Appends the hits among 4 values of each lane (bit c of hm: value xc, index gi0 + c),
+            // compacting the warp buffer when they would not fit; mlane: the lane's running max
+            // in the current tile (the margin needs the max of everything seen).  Warp-uniform call.
+            auto append4 = [&](uint32_t hm, float x0, float x1, float x2, float x3, uint32_t gi0, float mlane) {
+                uint32_t nh = (uint32_t)__popc(hm);
+                uint32_t incl = warp_incl_scan_plain(nh);
+                uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+                if (ws.wcnt + tot > (uint32_t)kWCap) {
+                    ws = warp_compact(wx, wi, ws, k, fmax_nan(m_w, warp_max_nan(mlane)), wh);
+                    hm &= (x0 >= ws.theta ? 1u : 0u) | (x1 >= ws.theta ? 2u : 0u) | (x2 >= ws.theta ? 4u : 0u) |
+                          (x3 >= ws.theta ? 8u : 0u);
+                    nh = (uint32_t)__popc(hm);
+                    incl = warp_incl_scan_plain(nh);
+                    tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+                    if (ws.wcnt + tot > (uint32_t)kWCap) {  // ties fill the buffer: path N takes the row
+                        kact = false;
+                        if (lane == 0) sh.wover = 1u;
+                        return;
+                    }
+                }
+                uint32_t p = ws.wcnt + incl - nh;
+                if (hm & 1u) { wx[p] = x0; wi[p] = gi0; ++p; }
+                if (hm & 2u) { wx[p] = x1; wi[p] = gi0 + 1u; ++p; }
+                if (hm & 4u) { wx[p] = x2; wi[p] = gi0 + 2u; ++p; }
+                if (hm & 8u) { wx[p] = x3; wi[p] = gi0 + 3u; }
+                ws.wcnt += tot;
+            };
+
+            // unaligned head and tail elements (at most 3 + 3), plain loads, warp 0
+            if (warp == 0) {
+                const uint32_t edges = g.head + g.tail;
+                const bool mine = (uint32_t)lane < edges;
+                uint32_t gi = 0;
+                float x = -kInf;
+                if (mine) {
+                    gi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+                    x = penal_g(g.row[gi], gi);
+                }
                 if (greedy) {
-                    if (act && (x > bv || (x == bv && gi < bi))) {
+                    if (mine && (x > bv || (x == bv && gi < bi))) {
                         bv = x;
                         bi = gi;
                     }
-                    hit = false;
                 } else {
                     const float xs = __fmul_rn(x, inv_t);
-                    if (act) mx = fmax_nan(mx, xs);
-                    hit = act && xs >= theta;
-                }
-            };
-            auto p1_append = [&](float x, uint32_t gi, bool hit) {
-                const unsigned m = __ballot_sync(0xFFFFFFFFu, hit);
-                if (m) {
-                    const int leader = __ffs(m) - 1;
-                    uint32_t base = 0;
-                    if (lane == leader) base = atomicAdd(&sh.cand_n, (uint32_t)__popc(m));
-                    base = __shfl_sync(0xFFFFFFFFu, base, leader);
-                    if (hit) {
-                        const uint32_t slot = base + __popc(m & ((1u << lane) - 1u));
-                        if (slot < (uint32_t)kKCap) {
-                            cand_x[slot] = __fmul_rn(x, inv_t);
-                            cand_i[slot] = gi;
-                        } else {
-                            sh.cand_over = 1;
-                        }
+                    m_w = fmax_nan(m_w, warp_max_nan(mine ? xs : -kInf));
+                    if (kact) {
+                        const bool hit = mine && xs >= ws.theta;
+                        if (__any_sync(0xFFFFFFFFu, hit)) append4(hit ? 1u : 0u, xs, 0.0f, 0.0f, 0.0f, gi, -kInf);
                     }
                 }
-            };
-            // unaligned head and tail elements, plain loads, warp 0
-            if (tid < 32) {
-                const uint32_t edges = g.head + g.tail;
-                const bool mine = (uint32_t)tid < edges;
-                uint32_t gi = 0;
-                float x = 0.0f;
-                if (mine) {
-                    gi = (uint32_t)tid < g.head ? (uint32_t)tid : g.head + (uint32_t)g.body + ((uint32_t)tid - g.head);
-                    x = penal(g.row[gi], gi);
-                }
-                bool hit;
-                p1_value(x, gi, mine, hit);
-                if (pathK) p1_append(x, gi, hit);
             }
-            __syncthreads();
-            for (uint32_t c = 0; c < g.nchunks; ++c) {
-                const int stage = ring_wait(sh, a, seq, timed_out);
-                float* slot = ring + (size_t)stage * kChunk;
-                const uint32_t cnt = chunk_count(g, c);
-                const uint32_t gbase = g.head + c * kChunk;
-                if (pen_on) {
-                    patch_tile(slot, gbase, cnt, bitmap, penalty);
-                    __syncthreads();
-                }
+            uint32_t bits_nx = (uint32_t)warp < g.nchunks ? tile_bits((uint32_t)warp) : 0u;
+            for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
+                const uint32_t qq = q1 + t, s = qq % kSlots;
+                const uint32_t cnt = chunk_count(g, t);
+                const uint32_t tb = g.head + t * kTile;
+                const uint32_t l0 = (uint32_t)lane * 32u;
+                const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
+                const uint32_t bits = bits_nx;
+                if (t + kWarps < g.nchunks) bits_nx = tile_bits(t + kWarps);
+                const long long tw = clock64();
+                wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                acc_full += clock64() - tw;
+                const float* slot = ring + (size_t)s * kTile + l0;
+                float ml = -kInf, sl = 0.0f;  // lane: running max and sum of exp relative to it
+#pragma unroll 2
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                    const bool gv = c4 < nval;
+                    float4 q = make_float4(-kInf, -kInf, -kInf, -kInf);
+                    if (gv) q = *reinterpret_cast<const float4*>(slot + c4);
+                    float x[4] = {q.x, q.y, q.z, q.w};
+                    const uint32_t pb = (bits >> c4) & 15u;
+                    if (pb) {
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int li0 = li_of(j * 4);
-                    const bool act = (uint32_t)li0 < cnt;
-                    float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
-                    if (act) q = *reinterpret_cast<const float4*>(slot + li0);
-                    const uint32_t gi = gbase + (uint32_t)li0;
-                    bool h0, h1, h2, h3;
-                    p1_value(q.x, gi + 0, act, h0);
-                    p1_value(q.y, gi + 1, act, h1);
-                    p1_value(q.z, gi + 2, act, h2);
-                    p1_value(q.w, gi + 3, act, h3);
-                    if (pathK && __any_sync(0xFFFFFFFFu, h0 | h1 | h2 | h3)) {
-                        p1_append(q.x, gi + 0, h0);
-                        p1_append(q.y, gi + 1, h1);
-                        p1_append(q.z, gi + 2, h2);
-                        p1_append(q.w, gi + 3, h3);
+                        for (int c = 0; c < 4; ++c)
+                            if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
+                    }
+                    const uint32_t gi0 = tb + l0 + c4;
+                    if (greedy) {
+                        // lowest index among the maximal non-NaN values (strict '>' from index 0)
+                        if (gv) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                if (x[c] > bv || (x[c] == bv && gi0 + c < bi)) {
+                                    bv = x[c];
+                                    bi = gi0 + c;
+                                }
+                        }
+                        continue;
+                    }
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) x[c] = gv ? __fmul_rn(x[c], inv_t) : -kInf;
+                    const float mn = fmax_nan(ml, fmax_nan(fmax_nan(x[0], x[1]), fmax_nan(x[2], x[3])));
+                    if (mn != ml) {  // (a NaN makes the row panic; its sums do not matter)
+                        if (ml != -kInf) sl = __fmul_rn(sl, ex2_approx(__fmul_rn(__fsub_rn(ml, mn), kLog2e)));
+                        ml = mn;
+                    }
+                    if (ml != -kInf) {
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) sl += ex2_approx(__fmul_rn(__fsub_rn(x[c], ml), kLog2e));
+                    }
+                    if (kact) {
+                        uint32_t hm = 0;
+                        if (gv) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                if (x[c] >= ws.theta) hm |= 1u << c;
+                        }
+                        if (__any_sync(0xFFFFFFFFu, hm != 0u)) append4(hm, x[0], x[1], x[2], x[3], gi0, ml);
                     }
                 }
-                __syncthreads();
-                ++seq;
-                if (tid == 0) ring_issue(sh, ring, g, first_load, total_loads, seq);
-                if (pathK) {
-                    if (sh.cand_over) {
-                        pathK = false;
-                    } else if (sh.cand_n > (uint32_t)(kKCap - kChunk)) {
-                        const long long tc0 = clock64();
-                        const float mb = block_max_nan(mx, wsh);
-                        compact_candidates(cand_x, cand_i, k, mb, sh);
-                        acc_wait1 += clock64() - tc0;
-                        if (sh.cand_n > (uint32_t)(kKCap - kChunk)) pathK = false;
-                    }
-                    theta = sh.theta;
-                    __syncthreads();
-                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&sh.empty[s]);
+                if (greedy) continue;
+                // tile statistics: max, and per lane its sum of exp relative to the tile max
+                const float mt = warp_max_nan(ml);
+                m_w = fmax_nan(m_w, mt);
+                const float cl = (ml == -kInf || mt != mt)
+                                     ? 0.0f
+                                     : __fmul_rn(sl, ex2_approx(__fmul_rn(__fsub_rn(ml, mt), kLog2e)));
+                lrec[t * 32u + (uint32_t)lane] = cl;
+                const float tot = warp_sum_f(cl);
+                if (lane == 0) tt[t] = make_float4(mt, tot, 0.0f, 0.0f);
             }
-
             if (greedy) {
-                // lowest index among the maximal non-NaN values; NaN at index 0 -> 0
-                // (sampler.rs:62-70 and 104-113: strict '>' scanning up from index 0)
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) {
                     const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
@@ -839,29 +1448,37 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                     }
                 }
                 if (lane == 0) {
-                    gvs[tid >> 5] = bv;
-                    gis[tid >> 5] = bi;
+                    sh.gvs[warp] = bv;
+                    sh.gis[warp] = bi;
                 }
-                __syncthreads();
-                float b = gvs[0];
-                uint32_t ix = gis[0];
+            } else if (lane == 0) {
+                sh.wmax[warp] = m_w;
+                sh.wcnt[warp] = ws.wcnt;
+                sh.wdelta[warp] = ws.wdelta;
+            }
+            csync();
+            lap(0);
+
+            if (greedy) {
+                // sampler.rs:62-70 and 104-113; NaN at index 0 -> 0
+                float b = sh.gvs[0];
+                uint32_t ix = sh.gis[0];
                 for (int w = 1; w < kWarps; ++w)
-                    if (gvs[w] > b || (gvs[w] == b && gis[w] < ix)) {
-                        b = gvs[w];
-                        ix = gis[w];
+                    if (sh.gvs[w] > b || (sh.gvs[w] == b && sh.gis[w] < ix)) {
+                        b = sh.gvs[w];
+                        ix = sh.gis[w];
                     }
-                const float x0 = penal(g.row[0], 0);
+                const float x0 = penal_g(g.row[0], 0);
                 if (x0 != x0 || ix == 0xFFFFFFFFu) ix = 0;
                 token = ix;
                 prob = 1.0f;
-                lap(inf.cycles[0]);
                 goto row_done;
             }
 
             // ---------------------------------------------- stochastic rows ----
-            mx = block_max_nan(mx, wsh);
-            lap(inf.cycles[0]);
-            inf.max = mx;
+            float mx = sh.wmax[0];
+            for (int w = 1; w < kWarps; ++w) mx = fmax_nan(mx, sh.wmax[w]);
+            if (tid == 0) inf.max = mx;
             // NaN scaled logit or infinite max -> NaN probabilities -> the reference
             // panics at sampler.rs:129/132 (n >= 2)
             const bool bad = (mx != mx) || (fabsf(mx) == kInf);
@@ -874,216 +1491,363 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
                 goto row_done;
             }
             if (pathK && !bad) {
-                compact_candidates(cand_x, cand_i, k, mx, sh);
-                if (sh.cand_over || sh.cand_n > (uint32_t)kKSortMax) pathK = false;
-                // candidates dropped at earlier compactions must lie below every
-                // probability tie of the final k-th value
-                if (pathK && sh.delta_min < kInf && tie_margin(sh.vk, mx) > 4.0f * sh.delta_min) pathK = false;
-                __syncthreads();
+                if (sh.wover) {
+                    pathK = false;
+                } else {
+                    // the union of the warp buffers, then the final compaction against the row max
+                    uint32_t off = 0, tot = 0;
+                    for (int w = 0; w < kWarps; ++w) {
+                        if (w < warp) off += sh.wcnt[w];
+                        tot += sh.wcnt[w];
+                    }
+                    const uint32_t mine = sh.wcnt[warp];
+                    for (uint32_t i = (uint32_t)lane; i < mine; i += 32) {
+                        cand_x[off + i] = wx[i];
+                        cand_i[off + i] = wi[i];
+                    }
+                    if (tid == 0) {
+                        float dm = kInf;
+                        for (int w = 0; w < kWarps; ++w) dm = fminf(dm, sh.wdelta[w]);
+                        sh.cand_n = tot;
+                        sh.delta_min = dm;
+                    }
+                    csync();
+                    compact_candidates(cand_x, cand_i, k, mx, sh);
+                    if (sh.cand_over || sh.cand_n > (uint32_t)kKSortMax) pathK = false;
+                    // candidates dropped by earlier compactions must lie below every
+                    // probability tie of the final k-th value
+                    if (pathK && sh.delta_min < kInf && tie_margin(sh.vk, mx) > 4.0f * sh.delta_min) pathK = false;
+                    csync();
+                }
             }
             const uint32_t nk = sh.cand_n;
             const bool pathN = !pathK;
-            if (pathN && !bad)
-                for (int i = tid; i < kNB; i += kThreads) {
-                    hcnt[i] = 0;
-                    hmass[i] = 0.0f;
+
+            // ---------------------------------------------------------- prep ----
+            if (!bad) {
+                if (pathN)
+                    for (int i = tid; i < kNB; i += kThreads) hcnt[i] = 0;
+                if (warp == 0) {
+                    // the unaligned head elements open the sequential sum (ops.rs:408-411)
+                    float eh = 0.0f, dh = 0.0f;
+                    bool exh = true;
+                    if ((uint32_t)lane < g.head) {
+                        dh = d_of(penal_g(g.row[lane], lane), inv_t, mx);
+                        exh = dh == 0.0f;
+                        eh = exh ? 1.0f : expf(dh);
+                    }
+                    const float s0 = warp_serial_add(0.0f, eh, dh, exh, 0, (int)g.head, exptab);
+                    // Running-sum estimate P at every tile start from the tile statistics.
+                    // The exact sequential sum there, S, satisfies S >= P (1 - delta) with
+                    // delta = i 2^-23 + 2^-13 (i elements before the tile): each of the i
+                    // roundings moves it by at most 2^-24 S, and P's own error (approximate exp
+                    // of arguments rounded once, f32 summation) is below 2^-14.  So the grid of
+                    // S is at least ulo = grid(P (1 - delta)) over the whole tile, and an
+                    // element with d < (ulo - 1) ln 2 - 0.01 adds exactly nothing.
+                    float run = s0;
+                    int umin = 0x7FFFFFFF, umax = -0x7FFFFFFF;
+                    const float hist_lim = -(float)(kNB - 1) / kBScale;
+                    for (uint32_t base = 0; base < g.nchunks; base += 32) {
+                        const uint32_t t = base + (uint32_t)lane;
+                        const bool in = t < g.nchunks;
+                        float4 rec = in ? tt[t] : make_float4(-kInf, 0.0f, 0.0f, 0.0f);
+                        float c = 0.0f;
+                        if (in && rec.x != -kInf)
+                            c = __fmul_rn(rec.y, ex2_approx(__fmul_rn(__fsub_rn(rec.x, mx), 1.44269504f)));
+                        const float incl = warp_incl_scan_f(c);
+                        float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                        if (lane == 0) excl = 0.0f;
+                        const float pt = __fadd_rn(run, excl);
+                        run = __fadd_rn(run, __shfl_sync(0xFFFFFFFFu, incl, 31));
+                        const float dl = __fmaf_rn((float)(g.head + t * kTile), 1.1920929e-07f, 1.2207031e-04f);
+                        const int ulo = unit_exp(__fmul_rn(pt, __fsub_rn(1.0f, dl)));
+                        const float dmax = __fsub_rn(rec.x, mx);
+                        const float thr = __fsub_rn(__fmul_rn((float)(ulo - 1), 0.69314718f), 0.01f);
+                        const bool sum_live = in && dmax >= thr;
+                        const bool hist_live = in && pathN && dmax >= hist_lim;
+                        if (in) {
+                            rec.y = pt;
+                            rec.z = __uint_as_float((uint32_t)(ulo + 256) | (sum_live ? kSumLive : 0u) |
+                                                    (hist_live ? kHistLive : 0u));
+                            tt[t] = rec;
+                        }
+                        if (sum_live) {
+                            umin = min(umin, ulo);
+                            umax = max(umax, ulo);
+                        }
+                    }
+                    // next sum-live tile after each tile (the baton's route)
+                    uint32_t carry = g.nchunks;
+                    if (g.nchunks) {
+                        for (int base = (int)((g.nchunks - 1) & ~31u); base >= 0; base -= 32) {
+                            const uint32_t t = (uint32_t)base + (uint32_t)lane;
+                            const bool in = t < g.nchunks;
+                            const uint32_t fl = in ? __float_as_uint(tt[t].z) : 0u;
+                            const unsigned m = __ballot_sync(0xFFFFFFFFu, (fl & kSumLive) != 0u);
+                            const unsigned above = lane == 31 ? 0u : (m & (0xFFFFFFFFu << (lane + 1)));
+                            const uint32_t nxt = above ? (uint32_t)base + (uint32_t)(__ffs(above) - 1) : carry;
+                            if (in) tt[t].w = __uint_as_float(nxt);
+                            if (m) carry = (uint32_t)base + (uint32_t)(__ffs(m) - 1);
+                        }
+                    }
+                    umin = __reduce_min_sync(0xFFFFFFFFu, umin);
+                    umax = __reduce_max_sync(0xFFFFFFFFu, umax);
+                    for (int u = umin + lane; u <= umax; u += 32)
+                        sh.xthr[u + kUBase] =
+                            raw_threshold(__fsub_rn(__fmul_rn((float)(u - 1), 0.69314718f), 0.01f), inv_t, mx);
+                    if (lane == 0) {
+                        sh.xhist = pathN ? raw_threshold(hist_lim, inv_t, mx) : kInf;
+                        sh.bval = s0;
+                        __threadfence_block();
+                        sh.bseq = carry;  // first sum-live tile
+                    }
                 }
-            // raw threshold of the path-N histogram: elements with d >= -kNB/kBScale
-            const float xhist = (pathN && !bad) ? raw_threshold(-(float)(kNB - 1) / kBScale, inv_t, mx) : kInf;
-            __syncthreads();
+                csync();
+            }
+            lap(1);
 
             // -------------------------------------------------------- pass 2 ----
             // exact sequential softmax denominator in index order (ops.rs:408-411)
             float S = 0.0f;
-            auto count_bucket = [&](float x, bool live) {
-                // path N: warp-aggregated count of the element's (max - x) bucket
-                const bool c = pathN && live && x >= xhist;
-                const unsigned act = __ballot_sync(0xFFFFFFFFu, c);
-                if (c) {
-                    const int b = (int)fminf(-d_of(x, inv_t, mx) * kBScale, (float)(kNB - 1));
-                    const unsigned peers = __match_any_sync(act, b);
-                    if (lane == __ffs(peers) - 1) atomicAdd(&hcnt[b], (uint32_t)__popc(peers));
+            {
+                const float xhist = sh.xhist;
+                uint32_t bits_nx = 0;
+                float lr_nx = 0.0f;
+                if ((uint32_t)warp < g.nchunks) {
+                    bits_nx = tile_bits((uint32_t)warp);
+                    lr_nx = __ldcg(lrec + (uint32_t)warp * 32u + (uint32_t)lane);
                 }
-            };
-            // One tile of values src[li], li in [start, cnt) (local positions = index order).
-            auto s_tile = [&](const float* src, uint32_t cnt, uint32_t gbase, uint32_t start) {
-                const int uu = unit_exp(S);
-                if (uu != sh.xthr_uu) {
-                    // elements with e < U/2 add nothing to S at this grid or any later one
-                    const long long t0 = clock64();
-                    __syncthreads();
-                    if (tid == 0) {
-                        sh.xthr = raw_threshold((float)(uu - 1) * 0.69314718f - 0.01f, inv_t, mx);
-                        sh.xthr_uu = uu;
+                for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
+                    const uint32_t qq = q2 + t, s = qq % kSlots;
+                    const float4 rec = bad ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : tt[t];
+                    const uint32_t bits = bits_nx;  // this tile's penalty bits and lane sums
+                    const float lr = lr_nx;
+                    if (t + kWarps < g.nchunks) {
+                        bits_nx = tile_bits(t + kWarps);
+                        lr_nx = __ldcg(lrec + (t + kWarps) * 32u + (uint32_t)lane);
                     }
-                    __syncthreads();
-                    acc_thr += clock64() - t0;
-                }
-                const float xthr = sh.xthr;
-                const long long t_start = clock64();
-                const float bm = grid_value(uu, kTwo23);                      // magic base 2^23 * U
-                const float halfu = uu > -149 ? ldexpf(1.0f, uu - 1) : 0.0f;  // U / 2
-                float v[kVpt];
+                    const uint32_t fl = __float_as_uint(rec.z);
+                    const uint32_t cnt = chunk_count(g, t);
+                    const uint32_t tb = g.head + t * kTile;
+                    const uint32_t l0 = (uint32_t)lane * 32u;
+                    const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
+                    if (!(fl & (kSumLive | kHistLive))) {  // nothing in this tile can matter
+                        wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sh.empty[s]);
+                        continue;
+                    }
+                    const bool sum_live = (fl & kSumLive) != 0u;
+                    const int ulo = (int)(fl & 0xFFFFu) - 256;
+                    const float xthr = sum_live ? sh.xthr[ulo + kUBase] : kInf;
+                    const bool hl = pathN && (fl & kHistLive) != 0u;
+                    const float xlow = hl ? fminf(xthr, xhist) : xthr;
+                    // The running sum at the start of this lane's run is within a factor
+                    // (1 +- delta) of its estimate, so it lies on grid u0 or u0 + 1.
+                    int u0 = ulo;
+                    if (sum_live) {
+                        const float incl = warp_incl_scan_f(lr);
+                        float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                        if (lane == 0) excl = 0.0f;
+                        const float scale = ex2_approx(__fmul_rn(__fsub_rn(rec.x, mx), kLog2e));
+                        const float pl = __fadd_rn(rec.y, __fmul_rn(excl, scale));
+                        const float dl = __fmaf_rn((float)(tb + l0), 1.1920929e-07f, 1.2207031e-04f);
+                        u0 = max(unit_exp(__fmul_rn(pl, __fsub_rn(1.0f, dl))), ulo);
+                    }
+                    const float bm0 = grid_value(u0, kTwo23), bm1 = __fadd_rn(bm0, bm0);
+                    const float h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
+                    const float h1 = ldexpf(1.0f, u0);
+                    const long long tw = clock64();
+                    wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                    acc_full += clock64() - tw;
+                    const float* slot = ring + (size_t)s * kTile;
+                    const long long tc = clock64();
+                    // bucket counts (path N); the run's increments on both grids (exact sums)
+                    float s0 = 0.0f, s1 = 0.0f;
+                    bool sp0 = false, sp1 = false, live = false;  // sp: a tie or big element on that grid
+#pragma unroll 2
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                        if (c4 >= nval) continue;
+                        const float4 q = *reinterpret_cast<const float4*>(slot + l0 + c4);
+                        float x[4] = {q.x, q.y, q.z, q.w};
+                        const uint32_t pb = (bits >> c4) & 15u;
+                        if (pb) {
 #pragma unroll
-                for (int i = 0; i < kVpt; ++i) v[i] = 0.0f;
-                uint32_t exact = 0xFFFFFFFFu;  // bit i clear: v[i] approximates libm's expf
-                float tot = 0.0f;
-                uint32_t nlive = 0;
-                uint32_t flags = 0;  // 1: tie or big element on the current grid
-                uint32_t live = 0;  // bit i: slot i is above the skip threshold
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int li0 = li_of(j * 4);
-                    float4 q = make_float4(-kInf, -kInf, -kInf, -kInf);
-                    if ((uint32_t)li0 < cnt && (uint32_t)li0 >= start) {  // start, body cnt: multiples of 4
-                        q = *reinterpret_cast<const float4*>(src + li0);
-                        if ((uint32_t)li0 + 1 >= cnt) q.y = -kInf;  // edge tiles hold < 4 values
-                        if ((uint32_t)li0 + 2 >= cnt) q.z = -kInf;
-                        if ((uint32_t)li0 + 3 >= cnt) q.w = -kInf;
-                    }
-                    if (pathN) {
-                        count_bucket(q.x, q.x != -kInf);
-                        count_bucket(q.y, q.y != -kInf);
-                        count_bucket(q.z, q.z != -kInf);
-                        count_bucket(q.w, q.w != -kInf);
-                    }
-                    live |= (q.x > xthr ? 1u : 0u) << (j * 4);
-                    live |= (q.y > xthr ? 2u : 0u) << (j * 4);
-                    live |= (q.z > xthr ? 4u : 0u) << (j * 4);
-                    live |= (q.w > xthr ? 8u : 0u) << (j * 4);
-                }
-#pragma unroll 1
-                while (live) {
-                    const int i = __ffs(live) - 1;
-                    live &= live - 1;
-                    ++nlive;
-                    const float x = src[li_of(i)];
-                    const float d = d_of(x, inv_t, mx);
-                    float e = d == 0.0f ? 1.0f : expf(d);
-                    bool ex = d == 0.0f;
-                    if (e >= bm) {
-                        flags = 1;  // big: ordered step
-                    } else if (halfu > 0.0f) {
-                        float inc = __fsub_rn(__fadd_rn(bm, e), bm);
-                        float rr = fabsf(__fsub_rn(e, inc));
-                        if (!ex && rr >= halfu - __fmul_rn(e, 4.76837158203125e-07f)) {  // 2^-21 > 2.5 ulp
-                            // near a rounding midpoint: take libm's exact value
-                            e = exact_expf(d, exptab);
-                            ex = true;
-                            inc = __fsub_rn(__fadd_rn(bm, e), bm);
-                            rr = fabsf(__fsub_rn(e, inc));
-                            if (e >= bm) flags = 1;
+                            for (int c = 0; c < 4; ++c)
+                                if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
                         }
-                        if (ex && rr == halfu) flags = 1;  // tie: parity decides
-                        tot = __fadd_rn(tot, inc);
-                    } else {
-                        tot = __fadd_rn(tot, e);  // unit 2^-149: every float below 2^-125 is on the grid
-                    }
-                    v[i] = e;
-                    if (!ex) exact &= ~(1u << i);
-                }
-                const long long t_loop = clock64();
-                acc_loop += t_loop - t_start;
-                if (nlive) atomicAdd(&sh.misc[6], nlive);
-                // one reduction of (sum, flags)
 #pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    tot = __fadd_rn(tot, __shfl_xor_sync(0xFFFFFFFFu, tot, o));
-                    flags |= __shfl_xor_sync(0xFFFFFFFFu, flags, o);
-                }
-                __syncthreads();
-                if (lane == 0) {
-                    red_f[tid >> 5] = tot;
-                    red_u[tid >> 5] = flags;
-                }
-                __syncthreads();
-                float T = red_f[0];
-                uint32_t F = red_u[0];
-                for (int w = 1; w < kWarps; ++w) {
-                    T = __fadd_rn(T, red_f[w]);
-                    F |= red_u[w];
-                }
-                acc_red += clock64() - t_loop;
-                if (!F) {
-                    // every increment is a multiple of U below 2^23 U: the float sum is exact
-                    // whenever the new value stays below the grid's top
-                    const float s2 = __fadd_rn(S, T);
-                    if (s2 < __fadd_rn(bm, bm)) {
-                        S = s2;
-                        return;
-                    }
-                }
-                // a grid change, a tie or a big element inside the tile
-                auto exf = [&](int i) -> float {
-                    const int li = li_of(i);
-                    return exact_expf(d_of(src[li], inv_t, mx), exptab);
-                };
-                const long long t0 = clock64();
-                tile2(v, exact, (int)start, (int)cnt, +1, S, kInf, exf, sh);
-                acc_ord += clock64() - t0;
-            };
-            __shared__ float ser[kSerial + 4];
-            // Serial start: the head elements and the first kSerial elements of the first
-            // body tile, where the running sum crosses many binades, are added one by one
-            // by thread 0 after all threads computed their exact exps.
-            auto serial_start = [&](const float* body, uint32_t nbody) {
-                const uint32_t nh = g.head;
-                for (uint32_t q = tid; q < nh + nbody; q += kThreads) {
-                    const float x = q < nh ? penal(g.row[q], q) : body[q - nh];
-                    const float d = d_of(x, inv_t, mx);
-                    ser[q] = d == 0.0f ? 1.0f : exact_expf(d, exptab);
-                }
-                __syncthreads();
-                if (tid == 0) {
-                    float s = 0.0f;
-                    (void)serial_run(ser, (int)(nh + nbody), +1, s, kInf);
-                    sh.fstate = s;
-                }
-                __syncthreads();
-                S = sh.fstate;
-                __syncthreads();
-            };
-            if (!bad && g.nchunks == 0) serial_start(nullptr, 0);
-            for (uint32_t c = 0; c < g.nchunks; ++c) {
-                const long long tw = clock64();
-                const int stage = ring_wait(sh, a, seq, timed_out);
-                acc_wait += clock64() - tw;
-                float* slot = ring + (size_t)stage * kChunk;
-                const uint32_t cnt = chunk_count(g, c);
-                const uint32_t gbase = g.head + c * kChunk;
-                if (!bad) {
-                    if (pen_on) {
-                        patch_tile(slot, gbase, cnt, bitmap, penalty);
-                        __syncthreads();
-                    }
-                    uint32_t start = 0;
-                    if (c == 0) {
-                        start = min(cnt, (uint32_t)kSerial);
-                        serial_start(slot, start);
-                        // serial elements are still counted for the path-N histogram
-                        if (pathN)
-                            for (uint32_t q0 = 0; q0 < start; q0 += kThreads) {
-                                const uint32_t q = q0 + tid;
-                                count_bucket(q < start ? slot[q] : 0.0f, q < start);
+                        for (int c = 0; c < 4; ++c) {
+                            if (!(x[c] > xlow)) continue;
+                            const float d = d_of(x[c], inv_t, mx);
+                            if (hl && x[c] > xhist) atomicAdd(&hcnt[(int)fminf(-d * kBScale, (float)(kNB - 1))], 1u);
+                            if (!(x[c] > xthr)) continue;
+                            live = true;
+                            bool ex = d == 0.0f;
+                            float e = ex ? 1.0f : expf(d);
+                            float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
+                            float i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
+                            if (!ex) {
+                                // CUDA's expf is within 2 ulp of exp: take libm's value wherever that
+                                // error could change an increment, a tie or a big element
+                                const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e
+                                const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
+                                                 fabsf(__fsub_rn(e, bm1)) <= tol ||
+                                                 (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
+                                                 (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
+                                if (amb) {
+                                    e = exact_expf(d, exptab);
+                                    ex = true;
+                                    i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
+                                    i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
+                                }
                             }
+                            if (e >= bm0) {
+                                sp0 = true;
+                            } else {
+                                s0 += i0;
+                                if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) sp0 = true;
+                            }
+                            if (e >= bm1) {
+                                sp1 = true;
+                            } else {
+                                s1 += i1;
+                                if (ex && fabsf(__fsub_rn(e, i1)) == h1) sp1 = true;
+                            }
+                        }
                     }
-                    s_tile(slot, cnt, gbase, start);
+                    if (sum_live) {
+                        // multiples of U summed in f32 are exact below 2^24 U; at or above it the
+                        // run leaves the grid anyway (saturated count)
+                        const uint32_t c0 = s0 >= __fadd_rn(bm0, bm0) ? kSat : (uint32_t)ldexpf(s0, -u0);
+                        const uint32_t c1 = s1 >= __fadd_rn(bm1, bm1) ? kSat : (uint32_t)ldexpf(s1, -(u0 + 1));
+                        // tile totals for the common case: every run classified on the same grids
+                        const unsigned lm = __ballot_sync(0xFFFFFFFFu, live);
+                        const int u0w = __shfl_sync(0xFFFFFFFFu, u0, lm ? __ffs(lm) - 1 : 0);
+                        const bool uni = __all_sync(0xFFFFFFFFu, !live || u0 == u0w);
+                        const uint32_t t0 = warp_reduce(live ? c0 : 0u, SatAdd());
+                        const uint32_t t1 = warp_reduce(live ? c1 : 0u, SatAdd());
+                        const bool any0 = __any_sync(0xFFFFFFFFu, live && sp0);
+                        const bool any1 = __any_sync(0xFFFFFFFFu, live && sp1);
+                        // ---- chain step: wait for the exact sum before this tile
+                        const long long tb0 = clock64();
+                        float Sx = 0.0f;
+                        if (lane == 0) {
+                            const long long t0 = clock64();
+                            while (sh.bseq != t) {
+                                if (sh.abort) break;
+                                if (clock64() - t0 > kWaitCycles) {
+                                    sh.abort = 1u;
+                                    atomicExch(a.err_flag, LRS_E_TIMEOUT);
+                                    break;
+                                }
+                                __nanosleep(20);
+                            }
+                            __threadfence_block();
+                            Sx = sh.bval;
+                        }
+                        Sx = __shfl_sync(0xFFFFFFFFu, Sx, 0);
+                        const long long tb1 = clock64();
+                        if (unit_exp(Sx) < ulo && lane == 0) sh.misc[7] = 1u;  // estimate bound broken
+                        bool done = lm == 0u;
+                        if (!done && uni) {
+                            const int u = unit_exp(Sx);
+                            const uint32_t A = grid_count(Sx, u);
+                            if (u == u0w && !any0 && A + t0 < kTwo24) {
+                                Sx = grid_value(u, A + t0);
+                                done = true;
+                            } else if (u == u0w + 1 && !any1 && A + t1 < kTwo24) {
+                                Sx = grid_value(u, A + t1);
+                                done = true;
+                            }
+                        }
+                        uint32_t p = 0;
+                        for (int guard = 0; guard <= 32 && !done; ++guard) {
+                            const int u = unit_exp(Sx);
+                            const uint32_t A = grid_count(Sx, u);
+                            const bool act = (uint32_t)lane >= p && live;
+                            uint32_t inc = 0;
+                            bool ev = false;
+                            if (act) {
+                                if (u == u0) {
+                                    inc = c0;
+                                    ev = sp0;
+                                } else if (u == u0 + 1) {
+                                    inc = c1;
+                                    ev = sp1;
+                                } else {
+                                    ev = true;  // the run starts on a grid it was not classified for
+                                }
+                            }
+                            const uint32_t incl_i = warp_incl_scan(inc);
+                            uint32_t excl_i = __shfl_up_sync(0xFFFFFFFFu, incl_i, 1);
+                            if (lane == 0) excl_i = 0u;  // (not incl - inc: a lane count may saturate)
+                            ev = ev || (act && A + incl_i >= kTwo24);
+                            const unsigned m = __ballot_sync(0xFFFFFFFFu, ev);
+                            if (!m) {
+                                Sx = grid_value(u, A + __shfl_sync(0xFFFFFFFFu, incl_i, 31));
+                                break;
+                            }
+                            // runs before L on the grid, then run L element by element
+                            const int L = __ffs(m) - 1;
+                            const uint32_t exL = __shfl_sync(0xFFFFFFFFu, excl_i, L);
+                            Sx = grid_value(u, A + exL);
+                            const uint32_t bL = __shfl_sync(0xFFFFFFFFu, bits, L);
+                            const uint32_t pos = (uint32_t)L * 32u + (uint32_t)lane;
+                            float e = 0.0f, de = 0.0f;
+                            bool exe = true;
+                            if (pos < cnt) {
+                                float xv = slot[pos];
+                                if ((bL >> lane) & 1u) xv = penalise(xv, penalty);
+                                if (xv > xthr) {  // (at or below: adds exactly nothing on this grid)
+                                    de = d_of(xv, inv_t, mx);
+                                    exe = de == 0.0f;
+                                    e = exe ? 1.0f : expf(de);
+                                }
+                            }
+                            Sx = warp_serial_add(Sx, e, de, exe, 0, 32, exptab);
+                            if (lane == 0) atomicAdd(&sh.events, 1u);
+                            p = (uint32_t)L + 1u;
+                            if (p >= 32u) break;
+                        }
+                        if (lane == 0) {
+                            sh.bval = Sx;
+                            __threadfence_block();
+                            sh.bseq = __float_as_uint(rec.w);
+                        }
+                        acc_baton += tb1 - tb0;
+                        acc_chain += clock64() - tb1 + (tb0 - tc);
+                    }
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.empty[s]);
                 }
-                __syncthreads();
-                ++seq;
-                if (tid == 0) ring_issue(sh, ring, g, first_load, total_loads, seq);
+                csync();
+                if (!bad && warp == 0) {
+                    // the unaligned tail elements close the sum; head and tail into the buckets
+                    const uint32_t edges = g.head + g.tail;
+                    float et = 0.0f, dt = 0.0f, xe = -kInf;
+                    bool ext = true;
+                    if ((uint32_t)lane < edges) {
+                        const uint32_t gi =
+                            (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+                        xe = penal_g(g.row[gi], gi);
+                        if ((uint32_t)lane >= g.head) {
+                            dt = d_of(xe, inv_t, mx);
+                            ext = dt == 0.0f;
+                            et = ext ? 1.0f : expf(dt);
+                        }
+                    }
+                    const float Sx = warp_serial_add(sh.bval, et, dt, ext, (int)g.head, (int)g.tail, exptab);
+                    if (pathN && xe > xhist)
+                        atomicAdd(&hcnt[(int)fminf(-d_of(xe, inv_t, mx) * kBScale, (float)(kNB - 1))], 1u);
+                    if (lane == 0) sh.fstate = Sx;
+                }
+                csync();
+                S = sh.fstate;
             }
-            if (!bad && g.tail) {
-                const uint32_t tb = g.head + (uint32_t)g.body;
-                if (tid < 4) etile[tid] = tid < (int)g.tail ? penal(g.row[tb + tid], tb + tid) : 0.0f;
-                __syncthreads();
-                s_tile(etile, g.tail, tb, 0);
-                __syncthreads();
-            }
-            if (!bad && pathN && g.head)  // head elements into the histogram
-                if (tid < 32) count_bucket(tid < (int)g.head ? penal(g.row[tid], tid) : 0.0f, tid < (int)g.head);
-            inf.sum_exp = S;
-            lap(inf.cycles[1]);
+            if (tid == 0) inf.sum_exp = S;
+            lap(2);
             if (bad) {
                 status = LRS_E_NAN;
                 token = LRS_TOKEN_NONE;
@@ -1092,275 +1856,70 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
             }
 
             const float inv = __fdiv_rn(1.0f, S);  // ops.rs:413
-            float sum = 0.0f;
-            uint32_t cutoff = 0, pos = 0;
-            unsigned long long chosen = 0;
-            float rr = 0.0f;
-            if (pathK) {
-                // -------------------------------------------------------- path K ----
-                unsigned long long* keys = reinterpret_cast<unsigned long long*>(ring);
-                for (uint32_t i = tid; i < nk; i += kThreads) {
-                    const float e = exact_expf(__fsub_rn(cand_x[i], mx), exptab);
-                    const float p = __fmul_rn(e, inv);
-                    keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | cand_i[i];
-                }
-                __syncthreads();
-                const long long ts = clock64();
-                bitonic_sort_u64(keys, nk);  // (p desc, index asc)
-                acc_sort += clock64() - ts;
-                inf.n_cand = nk;
-                for (uint32_t i = tid; i < k; i += kThreads) ser[i] = __uint_as_float(~(uint32_t)(keys[i] >> 32));
-                __syncthreads();
-                if (tid == 0) {
-                    // top-p over the first k (sampler.rs:135-146); the survivor sum is the
-                    // same sequence up to the cutoff (sampler.rs:148-151)
-                    float cum = 0.0f;
-                    const int stp = serial_run(ser, (int)k, +1, cum, topp_on ? P.top_p : kInf);
-                    const uint32_t cut = stp >= 0 ? (uint32_t)stp + 1 : k;
-                    uint32_t ps = 0;
-                    float r0 = 0.0f;
-                    unsigned long long st2 = st;
-                    if (cum > 0.0f) {
-                        r0 = __fmul_rn(next_f32(&st2), cum);  // sampler.rs:155
-                        float r = r0;
-                        const int w = serial_run(ser, (int)cut, -1, r, 0.0f);
-                        ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
-                    }
-                    sh.misc[3] = cut;
-                    sh.misc[4] = ps;
-                    sh.fstate = cum;
-                    sh.vk = r0;
-                }
-                __syncthreads();
-                cutoff = sh.misc[3];
-                pos = sh.misc[4];
-                sum = sh.fstate;
-                rr = sh.vk;
-                if (sum > 0.0f) {
-                    (void)next_f32(&st);
-                    inf.r0 = rr;
-                }
-                chosen = keys[pos];
-                __syncthreads();
-            } else {
-                // -------------------------------------------------------- path N ----
-                if (tid == 0) {
-                    // bucket limit: enough candidates for k and for top_p (+ margin); the
-                    // mass of bucket b is at least count * exp(-(b+1)/kBScale) / S
-                    uint32_t cc = 0;
-                    double mass = 0.0;
-                    const double target = topp_on ? ((double)P.top_p + kTopPMargin) * (double)S : 1e300;
-                    uint32_t b = 0;
-                    for (; b < (uint32_t)kNB - 1; ++b) {
-                        cc += hcnt[b];
-                        mass += (double)hcnt[b] * exp(-(double)(b + 1) / (double)kBScale);
-                        if (cc >= k || mass >= target) break;
-                    }
-                    sh.misc[3] = b;
-                    uint32_t acc = 0;
-                    for (int q = 0; q < kNB - 1; ++q) {
-                        hoff[q] = acc;
-                        acc += hcnt[q];
-                    }
-                    hoff[kNB - 1] = acc;
-                    hcnt[kNB - 1] = n - acc;  // everything below the histogram range
-                }
-                __syncthreads();
-                const uint32_t blim = sh.misc[3];
-                uint32_t* cursor = reinterpret_cast<uint32_t*>(hmass);
-                for (int q = tid; q < kNB; q += kThreads) cursor[q] = 0;
-                __syncthreads();
-                // gather exact probabilities of buckets [blo, bhi] into scratch
-                auto gather = [&](uint32_t blo, uint32_t bhi) {
-                    const float xlo = raw_threshold(-(float)(bhi + 1) / kBScale, inv_t, mx);
-                    constexpr int kU = 4;  // independent elements per thread in flight
-                    for (uint32_t i0 = 0; i0 < n; i0 += kThreads * kU) {
-                        float xs[kU];
-#pragma unroll
-                        for (int u = 0; u < kU; ++u) {
-                            const uint32_t i = i0 + u * kThreads + tid;
-                            xs[u] = i < n ? g.row[i] : -kInf;
-                        }
-#pragma unroll
-                        for (int u = 0; u < kU; ++u) {
-                            const uint32_t i = i0 + u * kThreads + tid;
-                            bool take = false;
-                            int b = 0;
-                            float dd = 0.0f;
-                            if (i < n) {
-                                const float x = penal(xs[u], i);
-                                if (x > xlo || bhi == (uint32_t)kNB - 1) {
-                                    dd = d_of(x, inv_t, mx);
-                                    b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
-                                    if (!(x >= xhist)) b = kNB - 1;
-                                    take = (uint32_t)b >= blo && (uint32_t)b <= bhi;
-                                }
-                            }
-                            const unsigned act = __ballot_sync(0xFFFFFFFFu, take);
-                            if (take) {
-                                const float e = exact_expf(dd, exptab);
-                                const float pr = __fmul_rn(e, inv);
-                                const unsigned peers = __match_any_sync(act, b);
-                                const int leader = __ffs(peers) - 1;
-                                uint32_t base = 0;
-                                if (lane == leader) base = atomicAdd(&cursor[b], (uint32_t)__popc(peers));
-                                base = __shfl_sync(act, base, leader);
-                                const uint32_t slot = hoff[b] + base + __popc(peers & ((1u << lane) - 1u));
-                                scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
-                            }
-                        }
-                    }
-                    __threadfence_block();
-                    __syncthreads();
-                };
-                gather(0, blim);
-                uint32_t gathered_to = blim;
-                inf.n_cand = hoff[blim] + hcnt[blim];
-                unsigned long long* sbuf = reinterpret_cast<unsigned long long*>(ring);
-                uint32_t sorted_to = 0;  // buckets [0, sorted_to) sorted in scratch
-                // Sort bucket b (gathering more buckets first when b is beyond the gathered
-                // range, doubling the range each time).  Buckets are sorted in order.
-                auto ensure_bucket = [&](uint32_t b) {
-                    while (sorted_to <= b) {
-                        const uint32_t q = sorted_to;
-                        if (q > gathered_to) {
-                            const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
-                            gather(gathered_to + 1, hi);
-                            gathered_to = hi;
-                        }
-                        const uint32_t cnt = hcnt[q];
-                        if (cnt > 1) {
-                            const long long ts = clock64();
-                            unsigned long long* base = scratch + hoff[q];
-                            if (cnt <= (uint32_t)kSortCap) {
-                                for (uint32_t i = tid; i < cnt; i += kThreads) sbuf[i] = base[i];
-                                __syncthreads();
-                                bitonic_sort_u64(sbuf, cnt);
-                                for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = sbuf[i];
-                            } else {
-                                bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
-                            }
-                            __threadfence_block();
-                            __syncthreads();
-                            acc_sort += clock64() - ts;
-                        }
-                        ++sorted_to;
-                    }
-                };
-                auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(scratch[q] >> 32)); };
-                // Exact sequential run over sorted positions [0, p1) of the candidate sequence
-                // (buckets in order, each sorted when reached): the first kSerial positions
-                // one by one on thread 0, then tiles.  Returns the stop position or -1.
-                auto run = [&](uint32_t p1, int dir, float& s, float thr) -> int {
-                    uint32_t p = 0, b = 0;
-                    uint32_t serial_left = kSerial;
-                    while (p < p1) {
-                        while (b + 1 < (uint32_t)kNB && hoff[b] + hcnt[b] <= p) ++b;
-                        if (dir > 0) {
-                            // Every remaining candidate lies in bucket b or a later one; once
-                            // their probabilities are all below half the sum's grid unit no
-                            // later addition changes the sum (and none is a tie).
-                            const float emax = expf(-(float)b / kBScale) * 1.0001f;
-                            const float pmax = __fmul_rn(emax, inv) * 1.0001f;
-                            const int uu = unit_exp(s);
-                            if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
-                        }
-                        ensure_bucket(b);
-                        const uint32_t seg_end = min(p1, hoff[b] + hcnt[b]);
-                        if (serial_left > 0) {
-                            const uint32_t m = min(seg_end - p, serial_left);
-                            for (uint32_t q = tid; q < m; q += kThreads) ser[q] = pval(p + q);
-                            __syncthreads();
-                            if (tid == 0) {
-                                float s2 = s;
-                                sh.stop = serial_run(ser, (int)m, dir, s2, thr);
-                                sh.fstate = s2;
-                            }
-                            __syncthreads();
-                            s = sh.fstate;
-                            const int st0 = sh.stop;
-                            __syncthreads();
-                            if (st0 >= 0) return (int)p + st0;
-                            p += m;
-                            serial_left -= m;
-                            continue;
-                        }
-                        const uint32_t tc = min((uint32_t)kChunk, seg_end - p);
-                        float v[kVpt];
-                        uint32_t ex = 0xFFFFFFFFu;
-                        load_sorted_tile(scratch + p, tc, v);
-                        // single-grid fast check
-                        const int uu = unit_exp(s);
-                        const uint32_t A = grid_count(s, uu);
-                        uint32_t t = 0, f = 0;
-#pragma unroll
-                        for (int i = 0; i < kVpt; ++i) {
-                            if ((uint32_t)li_of(i) < tc) {
-                                const Cls c = classify(__float_as_uint(v[i]), uu);
-                                t = sat_add(t, c.inc);
-                                f |= (c.tie || c.big) ? 1u : 0u;
-                            }
-                        }
-                        t = block_reduce_u32(t, SatAdd(), sh.red);
-                        f = block_reduce_u32(f, OrOp(), sh.red2);
-                        const float tq = (dir > 0 && thr < kInf) ? ldexpf(thr, -uu) : kInf;
-                        const bool fast = dir > 0 ? (!f && A + t <= kTwo24 - 1u && (float)(A + t) < tq)
-                                                  : (!f && t < A - grid_lower(uu));
-                        if (fast) {
-                            s = grid_value(uu, dir > 0 ? A + t : A - t);
-                        } else {
-                            const int stp = tile2(v, ex, 0, (int)tc, dir, s, thr, NoExact(), sh);
-                            if (stp >= 0) return (int)p + stp;
-                        }
-                        p += tc;
-                    }
-                    return -1;
-                };
-                // top-p scan capped at k survivors (sampler.rs:122-146)
-                float cum = 0.0f;
-                int stp = run(k, +1, cum, topp_on ? P.top_p : kInf);
-                cutoff = stp >= 0 ? (uint32_t)stp + 1 : k;
-                sum = cum;
-                // draw (sampler.rs:152-162)
-                if (sum > 0.0f) {
-                    rr = __fmul_rn(next_f32(&st), sum);
-                    inf.r0 = rr;
-                    float r = rr;
-                    stp = run(cutoff, -1, r, 0.0f);
-                    pos = stp >= 0 ? (uint32_t)stp : cutoff - 1;
-                } else {
-                    pos = 0;
-                }
-                {
-                    uint32_t b = 0;
-                    while (b + 1 < (uint32_t)kNB && hoff[b] + hcnt[b] <= pos) ++b;
-                    ensure_bucket(b);
-                }
-                chosen = scratch[pos];
-                __syncthreads();
+            FinishCtx fc;
+            fc.g = g;
+            fc.tt = tt;
+            fc.scratch = scratch;
+            fc.bitmap = bitmap;
+            fc.hcnt = hcnt;
+            fc.hoff = hoff;
+            fc.cursor = cursor;
+            fc.sbuf = sbuf;
+            fc.cand_x = cand_x;
+            fc.cand_i = cand_i;
+            fc.keys = keys;
+            fc.exptab = exptab;
+            fc.k = k;
+            fc.nk = nk;
+            fc.mx = mx;
+            fc.inv_t = inv_t;
+            fc.inv = inv;
+            fc.S = S;
+            fc.penalty = penalty;
+            fc.top_p = P.top_p;
+            fc.xhist = sh.xhist;
+            fc.pen_on = pen_on;
+            fc.topp_on = topp_on;
+            fc.st = st;
+            fc.cutoff = fc.pos = fc.n_cand = 0;
+            fc.sum = fc.rr = fc.r0 = 0.0f;
+            fc.chosen = 0;
+            fc.acc_sort = 0;
+            if (pathK)
+                finish_path_k(sh, fc);
+            else
+                finish_path_n(sh, fc);
+            st = fc.st;
+            acc_sort = fc.acc_sort;
+            if (tid == 0) {
+                inf.n_cand = fc.n_cand;
+                inf.r0 = fc.r0;
             }
+            const uint32_t cutoff = fc.cutoff, pos = fc.pos;
+            const float sum = fc.sum;
+            const unsigned long long chosen = fc.chosen;
             advance_state = true;
             token = (uint32_t)(chosen & 0xFFFFFFFFu);
             prob = __uint_as_float(~(uint32_t)(chosen >> 32));
-            inf.cutoff = cutoff;
-            inf.pos = pos;
-            inf.surv_sum = sum;
-            lap(inf.cycles[2]);
+            if (tid == 0) {
+                inf.cutoff = cutoff;
+                inf.pos = pos;
+                inf.surv_sum = sum;
+            }
+            lap(3);
         }
 
     row_done:
         if (sh.misc[7]) status = LRS_E_INTERNAL;
-        if (timed_out) status = LRS_E_TIMEOUT;
+        if (sh.abort) status = LRS_E_TIMEOUT;
         if (tid == 0) {
             inf.status = status;
             inf.token = token;
             inf.prob = prob;
             inf.events = sh.events;
-            inf.cycles[3] = sat32(acc_wait1);
-            inf.cycles[4] = sat32(acc_ord);
-            inf.cycles[6] = sat32(acc_loop);
-            inf.reserved = sat32(acc_red) / 16u * 0 + sh.misc[5];
-            inf.cycles[5] = sat32(acc_red);
+            inf.cycles[4] = sat32(acc_full);
+            inf.cycles[5] = sat32(acc_baton);
+            inf.cycles[6] = sat32(acc_chain);
             inf.cycles[7] = sat32(acc_sort);
             if (status == LRS_OK && advance_state) a.state[r] = st;
             a.tokens[r] = token;
@@ -1372,29 +1931,35 @@ extern "C" __global__ void __launch_bounds__(kThreads, 2) lrs_sample_rows(Sample
         if (pen_on && n > 0)
             for (uint32_t j = hstart + tid; j < hlen; j += kThreads) {
                 const uint32_t t = hrow[j];
-                if (t < n) bitmap[t >> 5] = 0;
+                if (t < n) bitmap[t >> 5] = 0u;
             }
-        __syncthreads();
+        csync();
     }
 }
 
 }  // namespace lrs
 
 // ------------------------------------------------------------------ host side ----
-size_t lrs_kernel_ring_bytes() { return (size_t)lrs::kStages * lrs::kChunk * sizeof(float); }
-size_t lrs_kernel_area_bytes() {
-    const size_t k = (size_t)lrs::kKCap * 8, nb = (size_t)lrs::kNB * 12;
-    return k > nb ? k : nb;
+size_t lrs_kernel_smem_bytes() { return lrs::kDynSmem; }
+int lrs_kernel_block_threads() { return lrs::kBlock; }
+void lrs_kernel_scratch_layout(uint32_t n, uint64_t* stride, uint64_t* bitmap_off, uint64_t* tiles_off,
+                               uint64_t* lanes_off) {
+    const uint64_t words = (uint64_t)(n + 31) / 32 + 2;  // window bitmap (+ read-ahead word)
+    const uint64_t tiles = (uint64_t)n / lrs::kTile + 2;
+    *bitmap_off = n;                                     // [0, n): path-N candidate keys
+    *tiles_off = *bitmap_off + (words + 1) / 2;          // tile records, 16 bytes each
+    *lanes_off = *tiles_off + 2 * tiles;                 // lane sums, 32 floats per tile
+    *stride = (*lanes_off + 16 * tiles + 31) & ~(uint64_t)31;  // 256-byte aligned per CTA
 }
 cudaError_t lrs_kernel_set_smem(size_t bytes) {
     return cudaFuncSetAttribute(lrs::lrs_sample_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 cudaError_t lrs_kernel_occupancy(int* ctas_per_sm, size_t smem) {
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, lrs::lrs_sample_rows, lrs::kThreads, smem);
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(ctas_per_sm, lrs::lrs_sample_rows, lrs::kBlock, smem);
 }
 cudaError_t lrs_kernel_launch(const lrs_kernel_args_t* args, uint32_t grid, size_t smem, cudaStream_t s) {
     cudaError_t e = lrs_kernel_set_smem(smem);
     if (e != cudaSuccess) return e;
-    lrs::lrs_sample_rows<<<grid, lrs::kThreads, smem, s>>>(*args);
+    lrs::lrs_sample_rows<<<grid, lrs::kBlock, smem, s>>>(*args);
     return cudaGetLastError();
 }

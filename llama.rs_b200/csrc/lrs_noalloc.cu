@@ -137,7 +137,8 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
                                          float* d_probs, int32_t* d_status, void* stream) {
     if (device < 0 || device >= kMaxDevices) return LRS_E_INVALID;
     if (rows == 0) return LRS_OK;
-    // The candidate scratch holds n entries of 8 bytes per CTA: at least one CTA must fit.
+    // The per-CTA scratch (n candidate keys, the window bitmap, tile records) of at least
+    // one CTA must fit in the static array.
     if (n == 0 || n > LRS_NOALLOC_MAX_VOCAB) return LRS_E_INVALID;
     if (!d_logits || !d_params || !d_state || !d_tokens) return LRS_E_INVALID;
     if (rows > 1 && ld != 0 && ld < n) return LRS_E_INVALID;
@@ -153,8 +154,9 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
     }
     const DeviceSetup& s = g_setup[device];
     if (rc == LRS_OK) {
-        const size_t smem = lrs_kernel_ring_bytes() + (size_t)((n + 31) / 32) * 4 + lrs_kernel_area_bytes();
-        const uint64_t per_cta = (uint64_t)n;  // scratch entries per CTA
+        const size_t smem = lrs_kernel_smem_bytes();
+        uint64_t per_cta = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0;  // scratch words per CTA and its layout
+        lrs_kernel_scratch_layout(n, &per_cta, &bitmap_off, &tiles_off, &lanes_off);
         uint32_t grid = (uint32_t)(kScratchBytes / 8 / per_cta);
         if (grid > (uint32_t)s.ctas) grid = (uint32_t)s.ctas;
         if (grid > rows) grid = rows;
@@ -177,9 +179,11 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.exp_entries = s.entries;
         args.scratch = s.scratch;
         args.scratch_stride = per_cta;
+        args.bitmap_off = bitmap_off;
+        args.tiles_off = tiles_off;
+        args.lanes_off = lanes_off;
         args.row_counter = s.counter;
         args.err_flag = reinterpret_cast<int32_t*>(s.counter + 1);
-        args.bitmap_words = (n + 31) / 32;
         cudaStream_t st = (cudaStream_t)stream;
         // the row counter and the error word must start at zero on every call
         if (cudaMemsetAsync(s.counter, 0, 2 * sizeof(uint32_t), st) != cudaSuccess)
