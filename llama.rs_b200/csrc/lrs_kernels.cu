@@ -160,6 +160,17 @@ __device__ __forceinline__ bool wait_bar(RowShared& sh, uint64_t* bar, uint32_t 
     return true;
 }
 
+// Bounded wait until load q of the ring has landed.  A parity wait only distinguishes
+// the current phase of an mbarrier from the one before it, and bulk copies may land out
+// of order while warps run tiles apart; so first wait until the slot's previous use
+// (load q - kSlots) was released by its consumer: then the slot's `full` barrier is in
+// the phase of load q and the parity wait is exact.
+__device__ __forceinline__ bool wait_full(RowShared& sh, uint32_t q, int32_t* err) {
+    const uint32_t s = q % kSlots, use = q / kSlots;
+    if (use > 0 && !wait_bar(sh, &sh.empty[s], (use - 1) & 1u, err)) return false;
+    return wait_bar(sh, &sh.full[s], use & 1u, err);
+}
+
 // ------------------------------------------------------------- producer warp ----
 // One thread: takes rows, publishes them in the row queue, and issues the bulk copies
 // of every tile of every pass in the order the consumers take them (load q lands in
@@ -535,6 +546,44 @@ __device__ __noinline__ void bitonic_sort_u64(unsigned long long* keys, uint32_t
     }
 }
 
+// One warp: the digit d of a radix round (256 counts, digit 255 first) holding the kk-th
+// largest key, and kk's rank inside that digit.  Lane l scans digits 255-8l .. 248-8l.
+__device__ __forceinline__ void digit_from_top(const uint32_t* hist, uint32_t kk, uint32_t& d, uint32_t& rem) {
+    const int lane = threadIdx.x & 31;
+    uint32_t c[8], s = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        c[e] = hist[255 - 8 * lane - e];
+        s += c[e];
+    }
+    uint32_t incl = s;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += t;
+    }
+    const uint32_t excl = incl - s;
+    const bool mine = excl < kk && kk <= incl;
+    const unsigned own = __ballot_sync(0xFFFFFFFFu, mine);
+    uint32_t dd = 0, rr = 0;
+    if (mine) {
+        uint32_t acc = excl;
+        bool found = false;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            if (!found && acc + c[e] >= kk) {
+                dd = (uint32_t)(255 - 8 * lane - e);
+                rr = kk - acc;
+                found = true;
+            }
+            acc += c[e];
+        }
+    }
+    const int owner = own ? __ffs(own) - 1 : 0;
+    d = __shfl_sync(0xFFFFFFFFu, dd, owner);
+    rem = __shfl_sync(0xFFFFFFFFu, rr, owner);
+}
+
 // k-th largest key (1-based rank kk) among keys[0..cnt) by radix select.
 __device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt, uint32_t kk, RowShared& sh) {
     uint32_t prefix = 0;
@@ -559,17 +608,13 @@ __device__ __noinline__ uint32_t radix_select_desc(const float* x, uint32_t cnt,
             }
         }
         csync();
-        if (threadIdx.x == 0) {
-            uint32_t acc = 0;
-            int d = 255;
-            for (; d >= 0; --d) {
-                const uint32_t c = sh.hist256[d];
-                if (acc + c >= kk) break;
-                acc += c;
+        if (threadIdx.x < 32) {
+            uint32_t d, rem;
+            digit_from_top(sh.hist256, kk, d, rem);
+            if (threadIdx.x == 0) {
+                sh.misc[1] = d;
+                sh.misc[2] = rem;
             }
-            if (d < 0) d = 0;
-            sh.misc[1] = (uint32_t)d;
-            sh.misc[2] = kk - acc;
         }
         csync();
         prefix |= sh.misc[1] << shift;
@@ -785,31 +830,8 @@ __device__ __noinline__ float warp_kth_desc(const float* x, uint32_t cnt, uint32
                 atomicAdd(&hist[(key >> shift) & 255u], 1u);
         }
         __syncwarp();
-        uint32_t c[8], s = 0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            c[e] = hist[255 - 8 * lane - e];  // digits in descending order
-            s += c[e];
-        }
-        const uint32_t incl = warp_incl_scan_plain(s), excl = incl - s;
-        const unsigned own = __ballot_sync(0xFFFFFFFFu, excl < kk && kk <= incl);
-        uint32_t d = 0, rem = 0;
-        if (excl < kk && kk <= incl) {
-            uint32_t acc = excl;
-            bool found = false;
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-                if (!found && acc + c[e] >= kk) {
-                    d = (uint32_t)(255 - 8 * lane - e);
-                    rem = kk - acc;
-                    found = true;
-                }
-                acc += c[e];
-            }
-        }
-        const int owner = own ? __ffs(own) - 1 : 0;
-        d = __shfl_sync(0xFFFFFFFFu, d, owner);
-        rem = __shfl_sync(0xFFFFFFFFu, rem, owner);
+        uint32_t d, rem;
+        digit_from_top(hist, kk, d, rem);
         prefix |= d << shift;
         kk = rem;
         __syncwarp();
@@ -1373,7 +1395,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const uint32_t bits = bits_nx;
                 if (t + kWarps < g.nchunks) bits_nx = tile_bits(t + kWarps);
                 const long long tw = clock64();
-                wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                wait_full(sh, qq, a.err_flag);
                 acc_full += clock64() - tw;
                 const float* slot = ring + (size_t)s * kTile + l0;
                 float ml = -kInf, sl = 0.0f;  // lane: running max and sum of exp relative to it
@@ -1632,7 +1654,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     const uint32_t l0 = (uint32_t)lane * 32u;
                     const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
                     if (!(fl & (kSumLive | kHistLive))) {  // nothing in this tile can matter
-                        wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                        wait_full(sh, qq, a.err_flag);
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&sh.empty[s]);
                         continue;
@@ -1658,7 +1680,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     const float h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
                     const float h1 = ldexpf(1.0f, u0);
                     const long long tw = clock64();
-                    wait_bar(sh, &sh.full[s], (qq / kSlots) & 1u, a.err_flag);
+                    wait_full(sh, qq, a.err_flag);
                     acc_full += clock64() - tw;
                     const float* slot = ring + (size_t)s * kTile;
                     const long long tc = clock64();
