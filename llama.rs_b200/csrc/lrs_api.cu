@@ -44,7 +44,7 @@ struct lrs_ctx {
     unsigned long long* d_exp_index = nullptr;
     uint2* d_exp_entries = nullptr;
     unsigned long long* d_scratch = nullptr;
-    uint64_t scratch_stride = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0;
+    uint64_t scratch_stride = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0, lists_off = 0;
     uint32_t scratch_ctas = 0;
     uint32_t* d_counter = nullptr;
     int32_t* d_err = nullptr;
@@ -124,13 +124,14 @@ static int load_exp_table(lrs_ctx* ctx) {
         if (!(e == y)) return set_err(ctx, LRS_E_INVALID, "libm expf table %s does not match this libm", path.c_str());
         if (i && ent[i].x <= ent[i - 1].x) return set_err(ctx, LRS_E_INVALID, "libm expf table unsorted");
     }
-    const uint32_t nblocks = ((lrs::kExpDomainHi - 0x80000000u) >> lrs::kExpBlockShift) + 1;
-    std::vector<unsigned long long> index(nblocks, 0ull);
+    const uint32_t nblocks = lrs::kExpBlocks;
+    std::vector<unsigned long long> index(lrs::kExpIndexWords, 0ull);
     size_t j = 0;
     for (uint32_t b = 0; b < nblocks; ++b) {
         const size_t start = j;
         while (j < ent.size() && ((ent[j].x - 0x80000000u) >> lrs::kExpBlockShift) == b) ++j;
-        index[b] = ((unsigned long long)start << 32) | (unsigned long long)(j - start);
+        index[lrs::kExpBitWords + b] = ((unsigned long long)start << 32) | (unsigned long long)(j - start);
+        if (j > start) index[b >> 6] |= 1ull << (b & 63);
     }
     if (j != ent.size()) return set_err(ctx, LRS_E_INVALID, "libm expf table has entries outside its domain");
     CK(cudaMalloc(&ctx->d_exp_index, index.size() * sizeof(unsigned long long)));
@@ -222,7 +223,8 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     }
     ctx->ctas_per_sm = occ > 2 ? 2 : occ;
     ctx->scratch_ctas = (uint32_t)(ctx->num_sms * ctx->ctas_per_sm);
-    lrs_kernel_scratch_layout(max_vocab, &ctx->scratch_stride, &ctx->bitmap_off, &ctx->tiles_off, &ctx->lanes_off);
+    lrs_kernel_scratch_layout(max_vocab, &ctx->scratch_stride, &ctx->bitmap_off, &ctx->tiles_off, &ctx->lanes_off,
+                              &ctx->lists_off);
     const size_t R = max_rows;
     CKF(cudaMalloc(&ctx->d_params, R * sizeof(lrs_params)));
     CKF(cudaMalloc(&ctx->d_state, R * sizeof(unsigned long long)));
@@ -315,6 +317,7 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.bitmap_off = ctx->bitmap_off;
     args.tiles_off = ctx->tiles_off;
     args.lanes_off = ctx->lanes_off;
+    args.lists_off = ctx->lists_off;
     args.row_counter = ctx->d_counter;
     args.err_flag = ctx->d_err;
     uint32_t grid = ctx->scratch_ctas;

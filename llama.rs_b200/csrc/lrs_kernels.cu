@@ -51,12 +51,18 @@ constexpr int kKMax = 128;           // path K handles 1 <= k <= kKMax (k < n)
 constexpr int kWCap = 256;           // per-warp path-K candidate buffer (entries)
 constexpr int kKCap = kWarps * kWCap;  // union of the warp buffers
 constexpr int kKSortMax = 2048;      // path K candidates kept after the final compaction
-constexpr int kNB = 2048;            // path N buckets of width 1/32 in (max - x)
+constexpr int kNB = 580;             // path N buckets of width 1/32 in (max - x); the last is
+                                     // everything below the candidate lists' range (d < -579/32)
 constexpr float kBScale = 32.0f;
 constexpr int kSortCap = 4096;       // largest bucket sorted in shared memory
 constexpr float kTopPMargin = 0.002f;
 constexpr int kSerial = 512;         // elements summed one by one at the start of a scan
 constexpr int kTilesSmem = 256;      // tile records kept in shared memory (larger rows: global)
+constexpr int kMaxTiles = 4096;      // tiles of the longest row (n <= 2^22)
+constexpr int kDense = 256;          // a tile with more candidates is streamed again in pass 2
+constexpr int kRunS = kDense / 32;   // list entries per lane run of a sparse tile
+constexpr uint32_t kDenseMark = 0xFFFFFFFFu;  // TileRec::lcnt of a dense tile
+constexpr uint32_t kNoTag = 0xFFFFFFFFu;
 constexpr int kUBase = 149;          // skip-threshold table index = grid exponent + kUBase
 constexpr int kNU = 288;
 constexpr uint32_t kSumLive = 1u << 16;   // tile record flags
@@ -66,16 +72,29 @@ constexpr float kLog2e = 1.44269504f;
 
 // dynamic shared memory (bytes)
 constexpr size_t kRingBytes = (size_t)kSlots * kTile * 4;
-constexpr size_t kRegionABytes = (size_t)kNB * 8;     // warp candidate buffers | path-N counts + offsets
+constexpr size_t kRegionABytes = (size_t)kWarps * kWCap * 8;  // warp candidate buffers | path-N counts + offsets
 constexpr size_t kRegionBBytes = (size_t)kSortCap * 8;  // warp radix counts | candidates + keys | bucket sort
-constexpr size_t kTTabBytes = (size_t)kTilesSmem * 16;
+constexpr size_t kTTabBytes = (size_t)kTilesSmem * 32;
 constexpr size_t kDynSmem = kRingBytes + kRegionABytes + kRegionBBytes + kTTabBytes;
 static_assert(kRegionABytes >= (size_t)kKCap * 8, "warp candidate buffers");
+static_assert(kRegionABytes >= (size_t)kNB * 8, "bucket counts and offsets");
 static_assert(kRegionBBytes >= (size_t)kKCap * 8 + (size_t)kKSortMax * 8, "candidates and sort keys");
 static_assert(kRegionBBytes >= (size_t)kWarps * 256 * 4, "per-warp radix counts");
 static_assert(kRegionBBytes >= (size_t)kNB * 4, "bucket cursors");
 
 using SampleArgs = lrs_kernel_args_t;
+
+// One tile of a row (32 bytes; shared memory, or per-CTA scratch for long rows).
+struct __align__(16) TileRec {
+    float mt;        // pass 1: max of the tile's scaled logits
+    float pt;        // pass 1: sum of exp relative to mt; prep: estimate of the running sum at the tile
+    uint32_t flags;  // prep: lowest grid exponent + 256 | kSumLive | kHistLive
+    uint32_t next;   // prep: next sum-live tile (the baton's route)
+    uint32_t loff;   // pass 1: first list entry (sparse tiles)
+    uint32_t lcnt;   // pass 1: list entries, or kDenseMark
+    uint32_t rank;   // prep: load number of a dense tile within pass 2
+    uint32_t tag;    // pass 1: the row id once the record is complete (kNoTag before)
+};
 
 // ---------------------------------------------------------------- shared state ----
 struct RowShared {
@@ -110,6 +129,9 @@ struct RowShared {
     float xthr[kNU];
     float ser[kSerial + 4];
     lrs_row_info info;     // the row's diagnostics, assembled by thread 0
+    uint32_t dense[kMaxTiles / 32];  // pass 1: tiles streamed again in pass 2 (read by the producer)
+    volatile uint32_t p1done;        // pass-1 tiles of two-pass rows finished by this CTA (monotone)
+    uint32_t ndense;                 // dense tiles of the current row
 };
 
 struct Geo {
@@ -173,11 +195,21 @@ __device__ __forceinline__ bool wait_full(RowShared& sh, uint32_t q, int32_t* er
 
 // ------------------------------------------------------------- producer warp ----
 // One thread: takes rows, publishes them in the row queue, and issues the bulk copies
-// of every tile of every pass in the order the consumers take them (load q lands in
-// slot q % kSlots and completes phase (q / kSlots) & 1 of its `full` barrier).
+// in the order the consumers take them (load q lands in slot q % kSlots and completes
+// phase (q / kSlots) & 1 of its `full` barrier): every tile for pass 1; then, once the
+// consumers have finished the row's pass 1, the dense tiles again for pass 2.
 __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float* ring) {
     const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
-    uint32_t q = 0, rqi = 0;
+    uint32_t q = 0, rqi = 0, p1target = 0;
+    auto issue = [&](const Geo& g, uint32_t c, uint64_t pol) -> bool {
+        const uint32_t s = q % kSlots, use = q / kSlots;
+        if (use > 0 && !wait_bar(sh, &sh.empty[s], (use - 1) & 1u, a.err_flag)) return false;
+        const uint32_t bytes = chunk_count(g, c) * 4u;
+        mbar_expect_tx(&sh.full[s], bytes);
+        bulk_load(ring + (size_t)s * kTile, g.row + g.head + (size_t)c * kTile, bytes, &sh.full[s], pol);
+        ++q;
+        return true;
+    };
     for (;;) {
         const uint32_t qs = rqi % kRowQ, use = rqi / kRowQ;
         if (use > 0 && !wait_bar(sh, &sh.rq_empty[qs], (use - 1) & 1u, a.err_flag)) break;
@@ -189,20 +221,26 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
         const Geo g = row_geometry(a, r);
         const uint32_t passes = row_passes(a.params[r], g.n);
         bool ok = true;
-        for (uint32_t p = 0; p < passes && ok; ++p)
-            for (uint32_t c = 0; c < g.nchunks; ++c) {
-                const uint32_t s = q % kSlots, use2 = q / kSlots;
-                if (use2 > 0 && !wait_bar(sh, &sh.empty[s], (use2 - 1) & 1u, a.err_flag)) {
-                    ok = false;
+        for (uint32_t c = 0; c < g.nchunks && ok; ++c) ok = issue(g, c, pol_keep);
+        if (!ok) break;
+        if (passes == 2 && g.nchunks) {
+            p1target += g.nchunks;
+            const long long t0 = clock64();
+            while ((int)(sh.p1done - p1target) < 0) {
+                if (sh.abort) break;
+                if (clock64() - t0 > kWaitCycles) {
+                    sh.abort = 1u;
+                    atomicExch(a.err_flag, LRS_E_TIMEOUT);
                     break;
                 }
-                const uint32_t bytes = chunk_count(g, c) * 4u;
-                mbar_expect_tx(&sh.full[s], bytes);
-                bulk_load(ring + (size_t)s * kTile, g.row + g.head + (size_t)c * kTile, bytes, &sh.full[s],
-                          p == 0 ? pol_keep : pol_drop);
-                ++q;
+                __nanosleep(64);
             }
-        if (!ok) break;
+            if (sh.abort) break;
+            __threadfence_block();
+            for (uint32_t c = 0; c < g.nchunks && ok; ++c)
+                if ((sh.dense[c >> 5] >> (c & 31)) & 1u) ok = issue(g, c, pol_drop);
+            if (!ok) break;
+        }
     }
     // Leave no copy in flight behind: wait (bounded, ignoring the abort flag) for the
     // last kSlots loads to land.
@@ -844,6 +882,7 @@ struct WState {
     uint32_t wcnt;  // candidates buffered
     float theta;    // append threshold
     float wdelta;   // smallest compaction margin so far
+    uint32_t over;  // ties overflowed the buffer (path N takes the row)
 };
 
 // Raise the warp's threshold to (k-th largest buffered - tie margin) and drop the
@@ -878,11 +917,105 @@ __device__ __noinline__ WState warp_compact(float* wx, uint32_t* wi, WState s, u
     return s;
 }
 
+// Increments of one element on the two grids a run is classified for (units
+// 2^u0 and 2^(u0+1)): e = libm's expf(d) where CUDA's expf (within 2 ulp) could round
+// differently; a tie or an element of half a binade or more flags the grid.
+struct GridAcc {
+    float s0, s1;  // sums of the rounded increments (multiples of the units)
+    bool sp0, sp1;
+};
+__device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, float h0, float h1, GridAcc& g,
+                                              const ExpTable& tab) {
+    bool ex = d == 0.0f;
+    float e = ex ? 1.0f : expf(d);
+    float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
+    float i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
+    if (!ex) {
+        const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
+        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol || fabsf(__fsub_rn(e, bm1)) <= tol ||
+                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
+                         (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
+        if (amb) {
+            e = exact_expf(d, tab);
+            ex = true;
+            i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
+            i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
+        }
+    }
+    if (e >= bm0) {
+        g.sp0 = true;
+    } else {
+        g.s0 += i0;
+        if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) g.sp0 = true;
+    }
+    if (e >= bm1) {
+        g.sp1 = true;
+    } else {
+        g.s1 += i1;
+        if (ex && fabsf(__fsub_rn(e, i1)) == h1) g.sp1 = true;
+    }
+}
+
+// Path K, one tile: appends this lane's hits (run offsets in hmask, values re-read from
+// the staged run) to the warp buffer in index order, 4 per lane at a time, compacting
+// the buffer when a batch would not fit.  mrun: the max of everything seen so far.
+__device__ __noinline__ WState topk_tile(const float* run, uint32_t hmask, uint32_t bits, float penalty, float inv_t,
+                                        uint32_t gbase, float mrun, uint32_t k, float* wx, uint32_t* wi,
+                                        uint32_t* wh, WState ws) {
+    const int lane = threadIdx.x & 31;
+    while (__any_sync(0xFFFFFFFFu, hmask != 0u)) {
+        float xv[4];
+        uint32_t gv[4], hm = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            xv[c] = 0.0f;
+            gv[c] = 0u;
+            if (hmask) {
+                const int pos = __ffs(hmask) - 1;
+                hmask &= hmask - 1u;
+                float x = run[pos];
+                if ((bits >> pos) & 1u) x = penalise(x, penalty);
+                xv[c] = __fmul_rn(x, inv_t);
+                gv[c] = gbase + (uint32_t)pos;
+                if (xv[c] >= ws.theta) hm |= 1u << c;
+            }
+        }
+        uint32_t nh = (uint32_t)__popc(hm);
+        uint32_t incl = warp_incl_scan_plain(nh);
+        uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+        if (ws.wcnt + tot > (uint32_t)kWCap) {
+            ws = warp_compact(wx, wi, ws, k, mrun, wh);
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if (!(xv[c] >= ws.theta)) hm &= ~(1u << c);
+            nh = (uint32_t)__popc(hm);
+            incl = warp_incl_scan_plain(nh);
+            tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            if (ws.wcnt + tot > (uint32_t)kWCap) {  // ties fill the buffer
+                ws.over = 1u;
+                return ws;
+            }
+        }
+        uint32_t p = ws.wcnt + incl - nh;
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+            if ((hm >> c) & 1u) {
+                wx[p] = xv[c];
+                wi[p] = gv[c];
+                ++p;
+            }
+        ws.wcnt += tot;
+        // hits after a compaction must clear the raised threshold: re-tested next batch
+    }
+    return ws;
+}
+
 // ------------------------------------------------------------ finish phases ----
 // Row context of the top-k / top-p / draw phase (sampler.rs:122-162).
 struct FinishCtx {
     Geo g;
-    const float4* tt;               // tile records (max of the scaled logits in .x)
+    const TileRec* tt;              // tile records
+    const uint2* lists;             // candidate lists of the sparse tiles: (scaled logit, index)
     unsigned long long* scratch;    // path N: gathered (p, index) keys
     const uint32_t* bitmap;         // window bitmap
     uint32_t* hcnt;                 // path N: bucket counts and offsets
@@ -894,7 +1027,7 @@ struct FinishCtx {
     unsigned long long* keys;
     ExpTable exptab;
     uint32_t k, nk;
-    float mx, inv_t, inv, S, penalty, top_p, xhist;
+    float mx, inv_t, inv, S, penalty, top_p, hist_lim;
     bool pen_on, topp_on;
     unsigned long long st;          // PRNG state (advanced by the draw)
     uint32_t cutoff, pos, n_cand;   // results
@@ -971,8 +1104,11 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         uint32_t b = 0;
         for (; b < (uint32_t)kNB - 1; ++b) {
             cc += f.hcnt[b];
-            mass += (double)f.hcnt[b] * exp(-(double)(b + 1) / (double)kBScale);
-            if (cc >= f.k || mass >= target) break;
+            const double eb = exp(-(double)(b + 1) / (double)kBScale);
+            mass += (double)f.hcnt[b] * eb;
+            // past this bucket every probability is below 2^-26: once the top-p sum is at
+            // least 1/2 nothing after it changes the sum (the scan ends there)
+            if (cc >= f.k || mass >= target || eb < 1.4901161193847656e-08 * (double)f.S) break;
         }
         sh.misc[3] = b;
         uint32_t acc = 0;
@@ -988,24 +1124,17 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     // gather exact probabilities of buckets [blo, bhi] into scratch; tiles whose
     // max lies below the range are skipped
     auto gather = [&](uint32_t blo, uint32_t bhi) {
-        const float xlo = raw_threshold(-(float)(bhi + 1) / kBScale, f.inv_t, f.mx);
         const bool all = bhi == (uint32_t)kNB - 1;
         const float dlim = -(float)(bhi + 1) / kBScale;
-        const float xh = f.xhist;
         for (uint32_t q = blo + tid; q <= bhi; q += kThreads) f.cursor[q] = 0;
         csync();
-        auto take = [&](uint32_t i, float xr, bool valid) {
+        // d: the element's d = fl(fl(x * inv_t) - max) (ops.rs:409)
+        auto take = [&](uint32_t i, float dd, bool valid) {
             bool tk = false;
             int b = 0;
-            float dd = 0.0f;
-            if (valid) {
-                const float x = penal_g(xr, i);
-                if (x > xlo || all) {
-                    dd = d_of(x, f.inv_t, f.mx);
-                    b = (int)fminf(-dd * kBScale, (float)(kNB - 1));
-                    if (!(x >= xh)) b = kNB - 1;
-                    tk = (uint32_t)b >= blo && (uint32_t)b <= bhi;
-                }
+            if (valid && (dd >= dlim || all)) {
+                b = dd >= f.hist_lim ? (int)fminf(-dd * kBScale, (float)(kNB - 1)) : kNB - 1;
+                tk = (uint32_t)b >= blo && (uint32_t)b <= bhi;
             }
             const unsigned act = __ballot_sync(0xFFFFFFFFu, tk);
             if (tk) {
@@ -1025,22 +1154,36 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             const bool mine = (uint32_t)lane < edges;
             const uint32_t gi =
                 (uint32_t)lane < f.g.head ? (uint32_t)lane : f.g.head + f.g.body + ((uint32_t)lane - f.g.head);
-            take(gi, mine ? f.g.row[gi] : 0.0f, mine);
+            take(gi, mine ? d_of(penal_g(f.g.row[gi], gi), f.inv_t, f.mx) : 0.0f, mine);
         }
         for (uint32_t t = 0; t < f.g.nchunks; ++t) {
-            if (!all && __fsub_rn(f.tt[t].x, f.mx) < dlim) continue;
-            const uint32_t cnt = chunk_count(f.g, t), tb = f.g.head + t * kTile;
-            constexpr int kU = kTile / kThreads;
-            float xs[kU];
-#pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const uint32_t i = (uint32_t)(u * kThreads + tid);
-                xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
+            const TileRec& R = f.tt[t];
+            if (!all && __fsub_rn(R.mt, f.mx) < dlim) continue;
+            if (!all && R.lcnt != kDenseMark) {
+                // sparse tile: its list holds every element with d >= hist_lim
+                const uint2* ent = f.lists + R.loff;
+                for (uint32_t i0 = 0; i0 < R.lcnt; i0 += kThreads) {
+                    const uint32_t i = i0 + (uint32_t)tid;
+                    uint2 e = make_uint2(0u, 0u);
+                    if (i < R.lcnt) e = __ldcg(ent + i);
+                    take(e.y, __fsub_rn(__uint_as_float(e.x), f.mx), i < R.lcnt);
+                }
+                continue;
             }
+            const uint32_t cnt = chunk_count(f.g, t), tb = f.g.head + t * kTile;
+            constexpr int kU = 4;  // independent loads in flight per thread
+            for (uint32_t i0 = 0; i0 < cnt; i0 += kU * kThreads) {
+                float xs[kU];
 #pragma unroll
-            for (int u = 0; u < kU; ++u) {
-                const uint32_t i = (uint32_t)(u * kThreads + tid);
-                take(tb + i, xs[u], i < cnt);
+                for (int u = 0; u < kU; ++u) {
+                    const uint32_t i = i0 + (uint32_t)(u * kThreads + tid);
+                    xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < kU; ++u) {
+                    const uint32_t i = i0 + (uint32_t)(u * kThreads + tid);
+                    take(tb + i, i < cnt ? d_of(penal_g(xs[u], tb + i), f.inv_t, f.mx) : 0.0f, i < cnt);
+                }
             }
         }
         __threadfence_block();
@@ -1179,7 +1322,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
     float* ring = reinterpret_cast<float*>(smem_raw);
     unsigned char* regA = smem_raw + kRingBytes;
     unsigned char* regB = regA + kRegionABytes;
-    float4* ttab_s = reinterpret_cast<float4*>(regB + kRegionBBytes);
+    TileRec* ttab_s = reinterpret_cast<TileRec*>(regB + kRegionBBytes);
     float* wbx = reinterpret_cast<float*>(regA);                                  // pass 1, path K
     uint32_t* wbi = reinterpret_cast<uint32_t*>(regA + (size_t)kKCap * 4);
     uint32_t* hcnt = reinterpret_cast<uint32_t*>(regA);                           // pass 2 on, path N
@@ -1192,8 +1335,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
     uint32_t* cursor = reinterpret_cast<uint32_t*>(regB);
     unsigned long long* scratch = a.scratch + (uint64_t)blockIdx.x * a.scratch_stride;
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(scratch + a.bitmap_off);
-    float4* ttab_g = reinterpret_cast<float4*>(scratch + a.tiles_off);
+    TileRec* ttab_g = reinterpret_cast<TileRec*>(scratch + a.tiles_off);
     float* lrec = reinterpret_cast<float*>(scratch + a.lanes_off);  // per tile: 32 lane sums (pass 1)
+    uint2* lists = reinterpret_cast<uint2*>(scratch + a.lists_off);  // per warp: sparse tiles' candidates
     const ExpTable exptab{a.exp_index, a.exp_entries};
     const float kInf = __int_as_float(0x7F800000);
     const int tid = threadIdx.x;
@@ -1211,6 +1355,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
         }
         sh.abort = 0u;
         sh.bseq = 0xFFFFFFFFu;
+        sh.p1done = 0u;
         fence_barrier_init();
     }
     __syncthreads();
@@ -1248,9 +1393,10 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
         bool pathK = stochastic && n >= 2 && k < n && k <= (uint32_t)kKMax;
         unsigned long long st = a.state[r];
         const uint32_t passes = row_passes(P, n);
-        const uint32_t q1 = qbase, q2 = qbase + g.nchunks;  // load numbers of tile 0 of each pass
-        qbase += passes * g.nchunks;
-        float4* const tt = g.nchunks <= (uint32_t)kTilesSmem ? ttab_s : ttab_g;
+        const bool lists_on = passes == 2;  // candidate lists and dense tiles for pass 2
+        const uint32_t q1 = qbase, q2 = qbase + g.nchunks;  // load numbers of pass 1 / pass 2 tile 0
+        qbase += g.nchunks;                                  // (+ the dense tiles, after the prep)
+        TileRec* const tt = g.nchunks <= (uint32_t)kTilesSmem ? ttab_s : ttab_g;
 
         lrs_row_info& inf = sh.info;  // written by thread 0 only
         if (tid == 0) {
@@ -1294,6 +1440,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 if (t < n) atomicOr(&bitmap[t >> 5], 1u << (t & 31));
             }
         }
+        if (lists_on)
+            for (uint32_t t = tid; t < g.nchunks; t += kThreads) tt[t].tag = kNoTag;
         if (tid == 0) {
             sh.cand_n = 0;
             sh.cand_over = 0;
@@ -1303,6 +1451,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             sh.misc[7] = 0;
             sh.events = 0;
             sh.wover = 0;
+            sh.ndense = 0;
         }
         csync();
 
@@ -1311,7 +1460,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             if (pen_on && ((__ldcg(bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, penalty);
             return x;
         };
-
         // penalty bits of this lane's run of tile t (loaded one tile ahead of use)
         auto tile_bits = [&](uint32_t t) -> uint32_t {
             const uint32_t c = chunk_count(g, t), o = (uint32_t)lane * 32u;
@@ -1324,42 +1472,26 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
 
         {
             // -------------------------------------------------------- pass 1 ----
-            float m_w = -kInf;          // warp: running max of the scaled logits
+            float m_w = -kInf;          // warp: running max of the scaled logits (its own tiles)
             float bv = -kInf;           // lane: greedy best value and index
             uint32_t bi = 0xFFFFFFFFu;
-            WState ws{0u, -kInf, kInf};  // warp: path-K filter
+            WState ws{0u, -kInf, kInf, 0u};  // warp: path-K filter
             bool kact = pathK;          // warp: still filtering
             float* wx = wbx + warp * kWCap;
             uint32_t* wi = wbi + warp * kWCap;
             uint32_t* wh = whist + warp * 256;
-
-            // Appends the hits among 4 values of each lane (bit c of hm: value xc, index gi0 + c),
-            // compacting the warp buffer when they would not fit; mlane: the lane's running max
-            // in the current tile (the margin needs the max of everything seen).  Warp-uniform call.
-            auto append4 = [&](uint32_t hm, float x0, float x1, float x2, float x3, uint32_t gi0, float mlane) {
-                uint32_t nh = (uint32_t)__popc(hm);
-                uint32_t incl = warp_incl_scan_plain(nh);
-                uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
-                if (ws.wcnt + tot > (uint32_t)kWCap) {
-                    ws = warp_compact(wx, wi, ws, k, fmax_nan(m_w, warp_max_nan(mlane)), wh);
-                    hm &= (x0 >= ws.theta ? 1u : 0u) | (x1 >= ws.theta ? 2u : 0u) | (x2 >= ws.theta ? 4u : 0u) |
-                          (x3 >= ws.theta ? 8u : 0u);
-                    nh = (uint32_t)__popc(hm);
-                    incl = warp_incl_scan_plain(nh);
-                    tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
-                    if (ws.wcnt + tot > (uint32_t)kWCap) {  // ties fill the buffer: path N takes the row
-                        kact = false;
-                        if (lane == 0) sh.wover = 1u;
-                        return;
-                    }
-                }
-                uint32_t p = ws.wcnt + incl - nh;
-                if (hm & 1u) { wx[p] = x0; wi[p] = gi0; ++p; }
-                if (hm & 2u) { wx[p] = x1; wi[p] = gi0 + 1u; ++p; }
-                if (hm & 4u) { wx[p] = x2; wi[p] = gi0 + 2u; ++p; }
-                if (hm & 8u) { wx[p] = x3; wi[p] = gi0 + 3u; }
-                ws.wcnt += tot;
-            };
+            // Candidate lists.  S, the exact sum before an element, is at least the exp of the
+            // largest d before its tile, e_mp; the prep's grid bound for the tile is then at
+            // least grid(e_mp) - 1 (rows of n <= 2^21: delta < 1/4), so an element with
+            // d < d_mp - 26 ln 2 - 0.01 adds exactly nothing.  A scaled logit more than
+            // theta = 18.1 (+ rounding slack) below a lower bound of the prefix max is such an
+            // element, and its d < -18.0999 lies below the path-N bucket range as well.
+            const float theta_c = g.n <= (1u << 21) ? 18.1f : 18.8f;
+            const uint32_t capw = ((g.nchunks + kWarps - 1) / kWarps) * kDense;
+            uint2* wlist = lists + (size_t)warp * capw;
+            uint32_t woff = 0;   // warp: entries written to its list
+            uint32_t front = 0;  // tiles [0, front) folded into gpm
+            float gpm = -kInf;   // max over tiles [0, front) (published by any warp)
 
             // unaligned head and tail elements (at most 3 + 3), plain loads, warp 0
             if (warp == 0) {
@@ -1379,9 +1511,15 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 } else {
                     const float xs = __fmul_rn(x, inv_t);
                     m_w = fmax_nan(m_w, warp_max_nan(mine ? xs : -kInf));
-                    if (kact) {
+                    if (kact) {  // at most 6 entries: the buffer is empty
                         const bool hit = mine && xs >= ws.theta;
-                        if (__any_sync(0xFFFFFFFFu, hit)) append4(hit ? 1u : 0u, xs, 0.0f, 0.0f, 0.0f, gi, -kInf);
+                        const unsigned hb = __ballot_sync(0xFFFFFFFFu, hit);
+                        if (hit) {
+                            const uint32_t p = (uint32_t)__popc(hb & ((1u << lane) - 1u));
+                            wx[p] = xs;
+                            wi[p] = gi;
+                        }
+                        ws.wcnt = (uint32_t)__popc(hb);
                     }
                 }
             }
@@ -1394,11 +1532,25 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
                 const uint32_t bits = bits_nx;
                 if (t + kWarps < g.nchunks) bits_nx = tile_bits(t + kWarps);
+                // candidate threshold from a lower bound of the max before this tile
+                float cthr = -kInf;
+                if (lists_on) {
+                    while (front < t) {
+                        if (*reinterpret_cast<volatile uint32_t*>(&tt[front].tag) != r) break;
+                        __threadfence_block();
+                        gpm = fmax_nan(gpm, tt[front].mt);
+                        ++front;
+                    }
+                    const float mp = fmax_nan(m_w, gpm);
+                    cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
+                }
                 const long long tw = clock64();
                 wait_full(sh, qq, a.err_flag);
                 acc_full += clock64() - tw;
                 const float* slot = ring + (size_t)s * kTile + l0;
-                float ml = -kInf, sl = 0.0f;  // lane: running max and sum of exp relative to it
+                float ml = -kInf;                // lane: max of its scaled logits
+                uint32_t cmask = 0, hmask = 0;   // lane: candidate / top-k hit run offsets
+                const float theta = kact ? ws.theta : kInf;
 #pragma unroll 2
                 for (int j = 0; j < 8; ++j) {
                     const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
@@ -1412,9 +1564,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         for (int c = 0; c < 4; ++c)
                             if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
                     }
-                    const uint32_t gi0 = tb + l0 + c4;
                     if (greedy) {
                         // lowest index among the maximal non-NaN values (strict '>' from index 0)
+                        const uint32_t gi0 = tb + l0 + c4;
                         if (gv) {
 #pragma unroll
                             for (int c = 0; c < 4; ++c)
@@ -1425,39 +1577,75 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         }
                         continue;
                     }
+                    if (gv) {
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) x[c] = gv ? __fmul_rn(x[c], inv_t) : -kInf;
-                    const float mn = fmax_nan(ml, fmax_nan(fmax_nan(x[0], x[1]), fmax_nan(x[2], x[3])));
-                    if (mn != ml) {  // (a NaN makes the row panic; its sums do not matter)
-                        if (ml != -kInf) sl = __fmul_rn(sl, ex2_approx(__fmul_rn(__fsub_rn(ml, mn), kLog2e)));
-                        ml = mn;
-                    }
-                    if (ml != -kInf) {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c) sl += ex2_approx(__fmul_rn(__fsub_rn(x[c], ml), kLog2e));
-                    }
-                    if (kact) {
-                        uint32_t hm = 0;
-                        if (gv) {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c)
-                                if (x[c] >= ws.theta) hm |= 1u << c;
+                        for (int c = 0; c < 4; ++c) {
+                            const float xs = __fmul_rn(x[c], inv_t);
+                            ml = fmax_nan(ml, xs);
+                            if (xs >= cthr) cmask |= 1u << (c4 + c);
+                            if (xs >= theta) hmask |= 1u << (c4 + c);
                         }
-                        if (__any_sync(0xFFFFFFFFu, hm != 0u)) append4(hm, x[0], x[1], x[2], x[3], gi0, ml);
+                    }
+                }
+                if (greedy) {
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&sh.empty[s]);
+                    continue;
+                }
+                const float mt = warp_max_nan(ml);
+                // path K: the tile's hits join the warp's buffer
+                if (kact && __any_sync(0xFFFFFFFFu, hmask != 0u)) {
+                    ws = topk_tile(slot, hmask, bits, penalty, inv_t, tb + l0, fmax_nan(m_w, mt), k, wx, wi, wh, ws);
+                    if (ws.over) {
+                        kact = false;
+                        if (lane == 0) sh.wover = 1u;
+                    }
+                }
+                // The candidates: their exp relative to the lane max (the estimate leaves
+                // out the rest, each below 2^-26 of the prefix max's term: the estimate
+                // only gets smaller, which keeps its bound), and for a sparse tile the list.
+                const uint32_t nc = (uint32_t)__popc(cmask);
+                const uint32_t cinc = warp_incl_scan_plain(nc);
+                const uint32_t ncand = __shfl_sync(0xFFFFFFFFu, cinc, 31);
+                const bool dense = ncand > (uint32_t)kDense;
+                float sl = 0.0f;
+                {
+                    uint32_t p = woff + cinc - nc;
+                    uint32_t m = cmask;
+                    while (m) {
+                        const int pos = __ffs(m) - 1;
+                        m &= m - 1u;
+                        float xv = slot[pos];
+                        if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
+                        const float xs = __fmul_rn(xv, inv_t);
+                        sl += ex2_approx(__fmul_rn(__fsub_rn(xs, ml), kLog2e));
+                        if (!dense) wlist[p++] = make_uint2(__float_as_uint(xs), tb + l0 + (uint32_t)pos);
                     }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&sh.empty[s]);
-                if (greedy) continue;
-                // tile statistics: max, and per lane its sum of exp relative to the tile max
-                const float mt = warp_max_nan(ml);
-                m_w = fmax_nan(m_w, mt);
-                const float cl = (ml == -kInf || mt != mt)
+                // tile statistics: max, and per lane its candidates' exp sum relative to the tile max
+                const float cl = (ml == -kInf || mt != mt || sl == 0.0f)
                                      ? 0.0f
                                      : __fmul_rn(sl, ex2_approx(__fmul_rn(__fsub_rn(ml, mt), kLog2e)));
                 lrec[t * 32u + (uint32_t)lane] = cl;
                 const float tot = warp_sum_f(cl);
-                if (lane == 0) tt[t] = make_float4(mt, tot, 0.0f, 0.0f);
+                if (lane == 0) {
+                    TileRec& R = tt[t];
+                    R.mt = mt;
+                    R.pt = tot;
+                    R.loff = (uint32_t)warp * capw + woff;
+                    R.lcnt = dense ? kDenseMark : ncand;
+                    if (dense)
+                        atomicOr(&sh.dense[t >> 5], 1u << (t & 31));
+                    else
+                        atomicAnd(&sh.dense[t >> 5], ~(1u << (t & 31)));
+                    __threadfence_block();
+                    *reinterpret_cast<volatile uint32_t*>(&R.tag) = r;
+                    atomicAdd(const_cast<uint32_t*>(&sh.p1done), 1u);
+                }
+                if (!dense) woff += ncand;
+                m_w = fmax_nan(m_w, mt);
             }
             if (greedy) {
 #pragma unroll
@@ -1544,88 +1732,103 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             }
             const uint32_t nk = sh.cand_n;
             const bool pathN = !pathK;
+            const float hist_lim = -(float)(kNB - 1) / kBScale;
 
             // ---------------------------------------------------------- prep ----
-            if (!bad) {
-                if (pathN)
-                    for (int i = tid; i < kNB; i += kThreads) hcnt[i] = 0;
-                if (warp == 0) {
-                    // the unaligned head elements open the sequential sum (ops.rs:408-411)
-                    float eh = 0.0f, dh = 0.0f;
-                    bool exh = true;
-                    if ((uint32_t)lane < g.head) {
-                        dh = d_of(penal_g(g.row[lane], lane), inv_t, mx);
-                        exh = dh == 0.0f;
-                        eh = exh ? 1.0f : expf(dh);
+            if (pathN && !bad)
+                for (int i = tid; i < kNB; i += kThreads) hcnt[i] = 0;
+            if (warp == 0) {
+                // pass-2 load numbers of the dense tiles (the producer streams them in order)
+                uint32_t dn_acc = 0;
+                for (uint32_t base = 0; base < g.nchunks; base += 32) {
+                    const uint32_t t = base + (uint32_t)lane;
+                    const bool dn = t < g.nchunks && tt[t].lcnt == kDenseMark;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, dn);
+                    if (dn) tt[t].rank = dn_acc + (uint32_t)__popc(m & ((1u << lane) - 1u));
+                    dn_acc += (uint32_t)__popc(m);
+                }
+                if (lane == 0) sh.ndense = dn_acc;
+            }
+            if (!bad && warp == 0) {
+                // the unaligned head elements open the sequential sum (ops.rs:408-411)
+                float eh = 0.0f, dh = 0.0f;
+                bool exh = true;
+                if ((uint32_t)lane < g.head) {
+                    dh = d_of(penal_g(g.row[lane], lane), inv_t, mx);
+                    exh = dh == 0.0f;
+                    eh = exh ? 1.0f : expf(dh);
+                }
+                const float s0 = warp_serial_add(0.0f, eh, dh, exh, 0, (int)g.head, exptab);
+                // Running-sum estimate P at every tile start from the tile statistics.
+                // The exact sequential sum there, S, satisfies S >= P (1 - delta) with
+                // delta = i 2^-23 + 2^-13 (i elements before the tile): each of the i
+                // roundings moves it by at most 2^-24 S, and P's own error (approximate exp
+                // of arguments rounded once, f32 summation) is below 2^-14.  So the grid of
+                // S is at least ulo = grid(P (1 - delta)) over the whole tile, and an
+                // element with d < (ulo - 1) ln 2 - 0.01 adds exactly nothing.
+                float run = s0;
+                int umin = 0x7FFFFFFF, umax = -0x7FFFFFFF;
+                for (uint32_t base = 0; base < g.nchunks; base += 32) {
+                    const uint32_t t = base + (uint32_t)lane;
+                    const bool in = t < g.nchunks;
+                    float mt = -kInf, pt = 0.0f;
+                    uint32_t lcnt = 0;
+                    if (in) {
+                        mt = tt[t].mt;
+                        pt = tt[t].pt;
+                        lcnt = tt[t].lcnt;
                     }
-                    const float s0 = warp_serial_add(0.0f, eh, dh, exh, 0, (int)g.head, exptab);
-                    // Running-sum estimate P at every tile start from the tile statistics.
-                    // The exact sequential sum there, S, satisfies S >= P (1 - delta) with
-                    // delta = i 2^-23 + 2^-13 (i elements before the tile): each of the i
-                    // roundings moves it by at most 2^-24 S, and P's own error (approximate exp
-                    // of arguments rounded once, f32 summation) is below 2^-14.  So the grid of
-                    // S is at least ulo = grid(P (1 - delta)) over the whole tile, and an
-                    // element with d < (ulo - 1) ln 2 - 0.01 adds exactly nothing.
-                    float run = s0;
-                    int umin = 0x7FFFFFFF, umax = -0x7FFFFFFF;
-                    const float hist_lim = -(float)(kNB - 1) / kBScale;
-                    for (uint32_t base = 0; base < g.nchunks; base += 32) {
-                        const uint32_t t = base + (uint32_t)lane;
-                        const bool in = t < g.nchunks;
-                        float4 rec = in ? tt[t] : make_float4(-kInf, 0.0f, 0.0f, 0.0f);
-                        float c = 0.0f;
-                        if (in && rec.x != -kInf)
-                            c = __fmul_rn(rec.y, ex2_approx(__fmul_rn(__fsub_rn(rec.x, mx), 1.44269504f)));
-                        const float incl = warp_incl_scan_f(c);
-                        float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-                        if (lane == 0) excl = 0.0f;
-                        const float pt = __fadd_rn(run, excl);
-                        run = __fadd_rn(run, __shfl_sync(0xFFFFFFFFu, incl, 31));
-                        const float dl = __fmaf_rn((float)(g.head + t * kTile), 1.1920929e-07f, 1.2207031e-04f);
-                        const int ulo = unit_exp(__fmul_rn(pt, __fsub_rn(1.0f, dl)));
-                        const float dmax = __fsub_rn(rec.x, mx);
-                        const float thr = __fsub_rn(__fmul_rn((float)(ulo - 1), 0.69314718f), 0.01f);
-                        const bool sum_live = in && dmax >= thr;
-                        const bool hist_live = in && pathN && dmax >= hist_lim;
-                        if (in) {
-                            rec.y = pt;
-                            rec.z = __uint_as_float((uint32_t)(ulo + 256) | (sum_live ? kSumLive : 0u) |
-                                                    (hist_live ? kHistLive : 0u));
-                            tt[t] = rec;
-                        }
-                        if (sum_live) {
-                            umin = min(umin, ulo);
-                            umax = max(umax, ulo);
-                        }
+                    float c = 0.0f;
+                    if (in && mt != -kInf) c = __fmul_rn(pt, ex2_approx(__fmul_rn(__fsub_rn(mt, mx), kLog2e)));
+                    const float incl = warp_incl_scan_f(c);
+                    float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                    if (lane == 0) excl = 0.0f;
+                    const float ptile = __fadd_rn(run, excl);
+                    run = __fadd_rn(run, __shfl_sync(0xFFFFFFFFu, incl, 31));
+                    const float dl = __fmaf_rn((float)(g.head + t * kTile), 1.1920929e-07f, 1.2207031e-04f);
+                    const int ulo = unit_exp(__fmul_rn(ptile, __fsub_rn(1.0f, dl)));
+                    const float dmax = __fsub_rn(mt, mx);
+                    const float thr = __fsub_rn(__fmul_rn((float)(ulo - 1), 0.69314718f), 0.01f);
+                    const bool has = lcnt != 0u;  // a sparse tile without candidates adds nothing
+                    const bool sum_live = in && has && dmax >= thr;
+                    const bool hist_live = in && has && pathN && dmax >= hist_lim;
+                    if (in) {
+                        tt[t].pt = ptile;
+                        tt[t].flags = (uint32_t)(ulo + 256) | (sum_live ? kSumLive : 0u) | (hist_live ? kHistLive : 0u);
                     }
-                    // next sum-live tile after each tile (the baton's route)
-                    uint32_t carry = g.nchunks;
-                    if (g.nchunks) {
-                        for (int base = (int)((g.nchunks - 1) & ~31u); base >= 0; base -= 32) {
-                            const uint32_t t = (uint32_t)base + (uint32_t)lane;
-                            const bool in = t < g.nchunks;
-                            const uint32_t fl = in ? __float_as_uint(tt[t].z) : 0u;
-                            const unsigned m = __ballot_sync(0xFFFFFFFFu, (fl & kSumLive) != 0u);
-                            const unsigned above = lane == 31 ? 0u : (m & (0xFFFFFFFFu << (lane + 1)));
-                            const uint32_t nxt = above ? (uint32_t)base + (uint32_t)(__ffs(above) - 1) : carry;
-                            if (in) tt[t].w = __uint_as_float(nxt);
-                            if (m) carry = (uint32_t)base + (uint32_t)(__ffs(m) - 1);
-                        }
-                    }
-                    umin = __reduce_min_sync(0xFFFFFFFFu, umin);
-                    umax = __reduce_max_sync(0xFFFFFFFFu, umax);
-                    for (int u = umin + lane; u <= umax; u += 32)
-                        sh.xthr[u + kUBase] =
-                            raw_threshold(__fsub_rn(__fmul_rn((float)(u - 1), 0.69314718f), 0.01f), inv_t, mx);
-                    if (lane == 0) {
-                        sh.xhist = pathN ? raw_threshold(hist_lim, inv_t, mx) : kInf;
-                        sh.bval = s0;
-                        __threadfence_block();
-                        sh.bseq = carry;  // first sum-live tile
+                    if (sum_live) {
+                        umin = min(umin, ulo);
+                        umax = max(umax, ulo);
                     }
                 }
-                csync();
+                // next sum-live tile after each tile (the baton's route)
+                uint32_t carry = g.nchunks;
+                if (g.nchunks) {
+                    for (int base = (int)((g.nchunks - 1) & ~31u); base >= 0; base -= 32) {
+                        const uint32_t t = (uint32_t)base + (uint32_t)lane;
+                        const bool in = t < g.nchunks;
+                        const uint32_t fl = in ? tt[t].flags : 0u;
+                        const unsigned m = __ballot_sync(0xFFFFFFFFu, (fl & kSumLive) != 0u);
+                        const unsigned above = lane == 31 ? 0u : (m & (0xFFFFFFFFu << (lane + 1)));
+                        const uint32_t nxt = above ? (uint32_t)base + (uint32_t)(__ffs(above) - 1) : carry;
+                        if (in) tt[t].next = nxt;
+                        if (m) carry = (uint32_t)base + (uint32_t)(__ffs(m) - 1);
+                    }
+                }
+                umin = __reduce_min_sync(0xFFFFFFFFu, umin);
+                umax = __reduce_max_sync(0xFFFFFFFFu, umax);
+                for (int u = umin + lane; u <= umax; u += 32)
+                    sh.xthr[u + kUBase] =
+                        raw_threshold(__fsub_rn(__fmul_rn((float)(u - 1), 0.69314718f), 0.01f), inv_t, mx);
+                if (lane == 0) {
+                    sh.xhist = pathN ? raw_threshold(hist_lim, inv_t, mx) : kInf;
+                    sh.bval = s0;
+                    __threadfence_block();
+                    sh.bseq = carry;  // first sum-live tile
+                }
             }
+            csync();
+            qbase += sh.ndense;
             lap(1);
 
             // -------------------------------------------------------- pass 2 ----
@@ -1635,131 +1838,160 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const float xhist = sh.xhist;
                 uint32_t bits_nx = 0;
                 float lr_nx = 0.0f;
-                if ((uint32_t)warp < g.nchunks) {
-                    bits_nx = tile_bits((uint32_t)warp);
-                    lr_nx = __ldcg(lrec + (uint32_t)warp * 32u + (uint32_t)lane);
-                }
+                float xs_nx[kRunS];      // next sparse tile: this lane's list entries (scaled logits)
+                uint32_t i0_nx = 0;      // and the index of its first entry
+                // loads of tile t's per-lane inputs, issued one tile ahead of their use
+                auto prefetch = [&](uint32_t t) {
+                    bits_nx = tile_bits(t);
+                    lr_nx = __ldcg(lrec + t * 32u + (uint32_t)lane);
+                    const uint32_t lc = tt[t].lcnt, e0 = (uint32_t)lane * kRunS;
+                    const bool want = !bad && lc != kDenseMark && (tt[t].flags & (kSumLive | kHistLive));
+                    const uint2* en = lists + tt[t].loff;
+#pragma unroll
+                    for (int i = 0; i < kRunS; ++i)
+                        xs_nx[i] = (want && e0 + (uint32_t)i < lc) ? __uint_as_float(__ldcg(&en[e0 + i].x)) : -kInf;
+                    i0_nx = (want && e0 < lc) ? __ldcg(&en[e0].y) : 0u;
+                };
+                if ((uint32_t)warp < g.nchunks) prefetch((uint32_t)warp);
                 for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
-                    const uint32_t qq = q2 + t, s = qq % kSlots;
-                    const float4 rec = bad ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : tt[t];
-                    const uint32_t bits = bits_nx;  // this tile's penalty bits and lane sums
+                    const bool dense = tt[t].lcnt == kDenseMark;
+                    const uint32_t fl = bad ? 0u : tt[t].flags;
+                    const uint32_t bits = bits_nx;  // this tile's penalty bits, lane sums, list entries
                     const float lr = lr_nx;
-                    if (t + kWarps < g.nchunks) {
-                        bits_nx = tile_bits(t + kWarps);
-                        lr_nx = __ldcg(lrec + (t + kWarps) * 32u + (uint32_t)lane);
-                    }
-                    const uint32_t fl = __float_as_uint(rec.z);
+                    float xsv[kRunS];
+#pragma unroll
+                    for (int i = 0; i < kRunS; ++i) xsv[i] = xs_nx[i];
+                    const uint32_t i0v = i0_nx;
+                    if (t + kWarps < g.nchunks) prefetch(t + kWarps);
+                    const bool sum_live = (fl & kSumLive) != 0u;
+                    const bool hl = pathN && (fl & kHistLive) != 0u;
+                    if (!dense && !sum_live && !hl) continue;  // nothing in this tile can matter
                     const uint32_t cnt = chunk_count(g, t);
                     const uint32_t tb = g.head + t * kTile;
                     const uint32_t l0 = (uint32_t)lane * 32u;
-                    const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
-                    if (!(fl & (kSumLive | kHistLive))) {  // nothing in this tile can matter
-                        wait_full(sh, qq, a.err_flag);
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&sh.empty[s]);
-                        continue;
-                    }
-                    const bool sum_live = (fl & kSumLive) != 0u;
                     const int ulo = (int)(fl & 0xFFFFu) - 256;
+                    const float thr_d = __fsub_rn(__fmul_rn((float)(ulo - 1), 0.69314718f), 0.01f);
                     const float xthr = sum_live ? sh.xthr[ulo + kUBase] : kInf;
-                    const bool hl = pathN && (fl & kHistLive) != 0u;
-                    const float xlow = hl ? fminf(xthr, xhist) : xthr;
-                    // The running sum at the start of this lane's run is within a factor
-                    // (1 +- delta) of its estimate, so it lies on grid u0 or u0 + 1.
-                    int u0 = ulo;
-                    if (sum_live) {
-                        const float incl = warp_incl_scan_f(lr);
-                        float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
-                        if (lane == 0) excl = 0.0f;
-                        const float scale = ex2_approx(__fmul_rn(__fsub_rn(rec.x, mx), kLog2e));
-                        const float pl = __fadd_rn(rec.y, __fmul_rn(excl, scale));
-                        const float dl = __fmaf_rn((float)(tb + l0), 1.1920929e-07f, 1.2207031e-04f);
-                        u0 = max(unit_exp(__fmul_rn(pl, __fsub_rn(1.0f, dl))), ulo);
+                    const float ptile = tt[t].pt;
+                    const uint32_t lcnt = dense ? 0u : tt[t].lcnt;
+                    const uint2* ent = lists + (dense ? 0u : tt[t].loff);
+                    uint32_t s = 0;
+                    const float* slot = ring;
+                    if (dense) {
+                        const uint32_t qq = q2 + tt[t].rank;
+                        s = qq % kSlots;
+                        slot = ring + (size_t)s * kTile;
+                        const long long tw = clock64();
+                        wait_full(sh, qq, a.err_flag);
+                        acc_full += clock64() - tw;
                     }
-                    const float bm0 = grid_value(u0, kTwo23), bm1 = __fadd_rn(bm0, bm0);
-                    const float h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
-                    const float h1 = ldexpf(1.0f, u0);
-                    const long long tw = clock64();
-                    wait_full(sh, qq, a.err_flag);
-                    acc_full += clock64() - tw;
-                    const float* slot = ring + (size_t)s * kTile;
                     const long long tc = clock64();
-                    // bucket counts (path N); the run's increments on both grids (exact sums)
-                    float s0 = 0.0f, s1 = 0.0f;
-                    bool sp0 = false, sp1 = false, live = false;  // sp: a tie or big element on that grid
-#pragma unroll 2
-                    for (int j = 0; j < 8; ++j) {
-                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
-                        if (c4 >= nval) continue;
-                        const float4 q = *reinterpret_cast<const float4*>(slot + l0 + c4);
-                        float x[4] = {q.x, q.y, q.z, q.w};
-                        const uint32_t pb = (bits >> c4) & 15u;
-                        if (pb) {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c)
-                                if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
+                    // ---- this lane's run: its grid estimate and its increments on two grids
+                    GridAcc acc{0.0f, 0.0f, false, false};
+                    bool live = false;
+                    int u0 = ulo;
+                    float bm0 = 0.0f, bm1 = 0.0f, h0 = 0.0f, h1 = 0.0f;
+                    auto set_grids = [&](float pl, uint32_t first_index) {
+                        const float dl = __fmaf_rn((float)first_index, 1.1920929e-07f, 1.2207031e-04f);
+                        u0 = max(unit_exp(__fmul_rn(pl, __fsub_rn(1.0f, dl))), ulo);
+                        bm0 = grid_value(u0, kTwo23);
+                        bm1 = __fadd_rn(bm0, bm0);
+                        h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
+                        h1 = ldexpf(1.0f, u0);
+                    };
+                    if (dense) {
+                        // run = 32 consecutive elements of the staged tile
+                        const uint32_t nval = l0 < cnt ? min(32u, cnt - l0) : 0u;
+                        if (sum_live) {
+                            // the running sum at the run start is within (1 +- delta) of its
+                            // estimate, so it lies on grid u0 or u0 + 1
+                            const float incl = warp_incl_scan_f(lr);
+                            float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                            if (lane == 0) excl = 0.0f;
+                            const float scale = ex2_approx(__fmul_rn(__fsub_rn(tt[t].mt, mx), kLog2e));
+                            set_grids(__fadd_rn(ptile, __fmul_rn(excl, scale)), tb + l0);
                         }
+                        uint32_t lmask = 0;  // live run offsets
+                        const float xlow = hl ? fminf(xthr, xhist) : xthr;
+#pragma unroll 2
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                            if (c4 >= nval) continue;
+                            const float4 q = *reinterpret_cast<const float4*>(slot + l0 + c4);
+                            float x[4] = {q.x, q.y, q.z, q.w};
+                            const uint32_t pb = (bits >> c4) & 15u;
+                            if (pb) {
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            if (!(x[c] > xlow)) continue;
-                            const float d = d_of(x[c], inv_t, mx);
-                            if (hl && x[c] > xhist) atomicAdd(&hcnt[(int)fminf(-d * kBScale, (float)(kNB - 1))], 1u);
-                            if (!(x[c] > xthr)) continue;
-                            live = true;
-                            bool ex = d == 0.0f;
-                            float e = ex ? 1.0f : expf(d);
-                            float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
-                            float i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
-                            if (!ex) {
-                                // CUDA's expf is within 2 ulp of exp: take libm's value wherever that
-                                // error could change an increment, a tie or a big element
-                                const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e
-                                const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
-                                                 fabsf(__fsub_rn(e, bm1)) <= tol ||
-                                                 (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
-                                                 (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
-                                if (amb) {
-                                    e = exact_expf(d, exptab);
-                                    ex = true;
-                                    i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
-                                    i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
+                                for (int c = 0; c < 4; ++c)
+                                    if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
+                            }
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                if (!(x[c] > xlow)) continue;
+                                if (hl && x[c] > xhist)
+                                    atomicAdd(&hcnt[(int)fminf(-d_of(x[c], inv_t, mx) * kBScale, (float)(kNB - 1))], 1u);
+                                if (x[c] > xthr) lmask |= 1u << (c4 + c);
+                            }
+                        }
+                        live = lmask != 0u;
+                        while (lmask) {  // the live elements only
+                            const int pos = __ffs(lmask) - 1;
+                            lmask &= lmask - 1u;
+                            float xv = slot[l0 + (uint32_t)pos];
+                            if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
+                            classify_elem(d_of(xv, inv_t, mx), bm0, bm1, h0, h1, acc, exptab);
+                        }
+                    } else {
+                        // run = kRunS consecutive list entries of the sparse tile
+                        const uint32_t e0 = (uint32_t)lane * kRunS;
+                        float dv[kRunS];
+                        float lsum = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < kRunS; ++i) {
+                            dv[i] = -kInf;
+                            if (e0 + (uint32_t)i < lcnt) {
+                                const float d = __fsub_rn(xsv[i], mx);
+                                if (hl && d >= hist_lim) atomicAdd(&hcnt[(int)fminf(-d * kBScale, (float)(kNB - 1))], 1u);
+                                if (sum_live && d >= thr_d) {
+                                    dv[i] = d;
+                                    lsum += ex2_approx(__fmul_rn(d, kLog2e));
                                 }
                             }
-                            if (e >= bm0) {
-                                sp0 = true;
-                            } else {
-                                s0 += i0;
-                                if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) sp0 = true;
-                            }
-                            if (e >= bm1) {
-                                sp1 = true;
-                            } else {
-                                s1 += i1;
-                                if (ex && fabsf(__fsub_rn(e, i1)) == h1) sp1 = true;
-                            }
+                        }
+                        if (sum_live) {
+                            const float incl = warp_incl_scan_f(lsum);
+                            float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+                            if (lane == 0) excl = 0.0f;
+                            set_grids(__fadd_rn(ptile, excl), e0 < lcnt ? i0v : tb);
+#pragma unroll
+                            for (int i = 0; i < kRunS; ++i)
+                                if (dv[i] != -kInf) {
+                                    live = true;
+                                    classify_elem(dv[i], bm0, bm1, h0, h1, acc, exptab);
+                                }
                         }
                     }
                     if (sum_live) {
                         // multiples of U summed in f32 are exact below 2^24 U; at or above it the
                         // run leaves the grid anyway (saturated count)
-                        const uint32_t c0 = s0 >= __fadd_rn(bm0, bm0) ? kSat : (uint32_t)ldexpf(s0, -u0);
-                        const uint32_t c1 = s1 >= __fadd_rn(bm1, bm1) ? kSat : (uint32_t)ldexpf(s1, -(u0 + 1));
+                        const uint32_t c0 = acc.s0 >= __fadd_rn(bm0, bm0) ? kSat : (uint32_t)ldexpf(acc.s0, -u0);
+                        const uint32_t c1 = acc.s1 >= __fadd_rn(bm1, bm1) ? kSat : (uint32_t)ldexpf(acc.s1, -(u0 + 1));
                         // tile totals for the common case: every run classified on the same grids
                         const unsigned lm = __ballot_sync(0xFFFFFFFFu, live);
                         const int u0w = __shfl_sync(0xFFFFFFFFu, u0, lm ? __ffs(lm) - 1 : 0);
                         const bool uni = __all_sync(0xFFFFFFFFu, !live || u0 == u0w);
                         const uint32_t t0 = warp_reduce(live ? c0 : 0u, SatAdd());
                         const uint32_t t1 = warp_reduce(live ? c1 : 0u, SatAdd());
-                        const bool any0 = __any_sync(0xFFFFFFFFu, live && sp0);
-                        const bool any1 = __any_sync(0xFFFFFFFFu, live && sp1);
+                        const bool any0 = __any_sync(0xFFFFFFFFu, live && acc.sp0);
+                        const bool any1 = __any_sync(0xFFFFFFFFu, live && acc.sp1);
                         // ---- chain step: wait for the exact sum before this tile
                         const long long tb0 = clock64();
                         float Sx = 0.0f;
                         if (lane == 0) {
-                            const long long t0 = clock64();
+                            const long long t0w = clock64();
                             while (sh.bseq != t) {
                                 if (sh.abort) break;
-                                if (clock64() - t0 > kWaitCycles) {
+                                if (clock64() - t0w > kWaitCycles) {
                                     sh.abort = 1u;
                                     atomicExch(a.err_flag, LRS_E_TIMEOUT);
                                     break;
@@ -1794,10 +2026,10 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             if (act) {
                                 if (u == u0) {
                                     inc = c0;
-                                    ev = sp0;
+                                    ev = acc.sp0;
                                 } else if (u == u0 + 1) {
                                     inc = c1;
-                                    ev = sp1;
+                                    ev = acc.sp1;
                                 } else {
                                     ev = true;  // the run starts on a grid it was not classified for
                                 }
@@ -1813,22 +2045,36 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             }
                             // runs before L on the grid, then run L element by element
                             const int L = __ffs(m) - 1;
-                            const uint32_t exL = __shfl_sync(0xFFFFFFFFu, excl_i, L);
-                            Sx = grid_value(u, A + exL);
-                            const uint32_t bL = __shfl_sync(0xFFFFFFFFu, bits, L);
-                            const uint32_t pos = (uint32_t)L * 32u + (uint32_t)lane;
+                            Sx = grid_value(u, A + __shfl_sync(0xFFFFFFFFu, excl_i, L));
                             float e = 0.0f, de = 0.0f;
                             bool exe = true;
-                            if (pos < cnt) {
-                                float xv = slot[pos];
-                                if ((bL >> lane) & 1u) xv = penalise(xv, penalty);
-                                if (xv > xthr) {  // (at or below: adds exactly nothing on this grid)
-                                    de = d_of(xv, inv_t, mx);
-                                    exe = de == 0.0f;
-                                    e = exe ? 1.0f : expf(de);
+                            int len;
+                            if (dense) {
+                                const uint32_t bL = __shfl_sync(0xFFFFFFFFu, bits, L);
+                                const uint32_t pos = (uint32_t)L * 32u + (uint32_t)lane;
+                                len = 32;
+                                if (pos < cnt) {
+                                    float xv = slot[pos];
+                                    if ((bL >> lane) & 1u) xv = penalise(xv, penalty);
+                                    if (xv > xthr) {  // (at or below: adds exactly nothing on this grid)
+                                        de = d_of(xv, inv_t, mx);
+                                        exe = de == 0.0f;
+                                        e = exe ? 1.0f : expf(de);
+                                    }
+                                }
+                            } else {
+                                const uint32_t j = (uint32_t)L * kRunS + (uint32_t)lane;
+                                len = kRunS;
+                                if (lane < kRunS && j < lcnt) {
+                                    const float d = __fsub_rn(__uint_as_float(__ldcg(&ent[j].x)), mx);
+                                    if (d >= thr_d) {
+                                        de = d;
+                                        exe = de == 0.0f;
+                                        e = exe ? 1.0f : expf(de);
+                                    }
                                 }
                             }
-                            Sx = warp_serial_add(Sx, e, de, exe, 0, 32, exptab);
+                            Sx = warp_serial_add(Sx, e, de, exe, 0, len, exptab);
                             if (lane == 0) atomicAdd(&sh.events, 1u);
                             p = (uint32_t)L + 1u;
                             if (p >= 32u) break;
@@ -1836,13 +2082,15 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         if (lane == 0) {
                             sh.bval = Sx;
                             __threadfence_block();
-                            sh.bseq = __float_as_uint(rec.w);
+                            sh.bseq = tt[t].next;
                         }
                         acc_baton += tb1 - tb0;
                         acc_chain += clock64() - tb1 + (tb0 - tc);
                     }
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&sh.empty[s]);
+                    if (dense) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&sh.empty[s]);
+                    }
                 }
                 csync();
                 if (!bad && warp == 0) {
@@ -1881,6 +2129,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             FinishCtx fc;
             fc.g = g;
             fc.tt = tt;
+            fc.lists = lists;
             fc.scratch = scratch;
             fc.bitmap = bitmap;
             fc.hcnt = hcnt;
@@ -1899,7 +2148,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             fc.S = S;
             fc.penalty = penalty;
             fc.top_p = P.top_p;
-            fc.xhist = sh.xhist;
+            fc.hist_lim = hist_lim;
             fc.pen_on = pen_on;
             fc.topp_on = topp_on;
             fc.st = st;
@@ -1917,16 +2166,13 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 inf.n_cand = fc.n_cand;
                 inf.r0 = fc.r0;
             }
-            const uint32_t cutoff = fc.cutoff, pos = fc.pos;
-            const float sum = fc.sum;
-            const unsigned long long chosen = fc.chosen;
             advance_state = true;
-            token = (uint32_t)(chosen & 0xFFFFFFFFu);
-            prob = __uint_as_float(~(uint32_t)(chosen >> 32));
+            token = (uint32_t)(fc.chosen & 0xFFFFFFFFu);
+            prob = __uint_as_float(~(uint32_t)(fc.chosen >> 32));
             if (tid == 0) {
-                inf.cutoff = cutoff;
-                inf.pos = pos;
-                inf.surv_sum = sum;
+                inf.cutoff = fc.cutoff;
+                inf.pos = fc.pos;
+                inf.surv_sum = fc.sum;
             }
             lap(3);
         }
@@ -1965,13 +2211,15 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
 size_t lrs_kernel_smem_bytes() { return lrs::kDynSmem; }
 int lrs_kernel_block_threads() { return lrs::kBlock; }
 void lrs_kernel_scratch_layout(uint32_t n, uint64_t* stride, uint64_t* bitmap_off, uint64_t* tiles_off,
-                               uint64_t* lanes_off) {
+                               uint64_t* lanes_off, uint64_t* lists_off) {
     const uint64_t words = (uint64_t)(n + 31) / 32 + 2;  // window bitmap (+ read-ahead word)
     const uint64_t tiles = (uint64_t)n / lrs::kTile + 2;
+    const uint64_t wtiles = (tiles + lrs::kWarps - 1) / lrs::kWarps;  // tiles of one consumer warp
     *bitmap_off = n;                                     // [0, n): path-N candidate keys
-    *tiles_off = *bitmap_off + (words + 1) / 2;          // tile records, 16 bytes each
-    *lanes_off = *tiles_off + 2 * tiles;                 // lane sums, 32 floats per tile
-    *stride = (*lanes_off + 16 * tiles + 31) & ~(uint64_t)31;  // 256-byte aligned per CTA
+    *tiles_off = *bitmap_off + (words + 1) / 2;          // tile records, 32 bytes each
+    *lanes_off = *tiles_off + 4 * tiles;                 // lane sums, 32 floats per tile
+    *lists_off = *lanes_off + 16 * tiles;                // candidate lists, 8 bytes an entry
+    *stride = (*lists_off + (uint64_t)lrs::kWarps * wtiles * lrs::kDense + 31) & ~(uint64_t)31;
 }
 cudaError_t lrs_kernel_set_smem(size_t bytes) {
     return cudaFuncSetAttribute(lrs::lrs_sample_rows, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);

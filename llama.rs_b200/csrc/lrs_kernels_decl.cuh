@@ -28,6 +28,7 @@ struct lrs_kernel_args_t {
     uint64_t bitmap_off;                  // window bitmap (zero between rows)
     uint64_t tiles_off;                   // tile records of rows longer than the shared table
     uint64_t lanes_off;                   // per-tile lane sums
+    uint64_t lists_off;                   // candidate lists of sparse tiles
     uint32_t* row_counter;    // zeroed before each launch
     int32_t* err_flag;        // sticky error word
 };
@@ -35,10 +36,10 @@ struct lrs_kernel_args_t {
 size_t lrs_kernel_smem_bytes();   // dynamic shared memory of a CTA (independent of n)
 int lrs_kernel_block_threads();
 // Per-CTA scratch for rows of up to n entries: stride and the offsets of the window
-// bitmap, the tile records and the lane sums (8-byte words).  The bitmap words must be
+// bitmap, the tile records, the lane sums and the candidate lists (8-byte words).  The bitmap words must be
 // zero before the first launch; every row clears the bits it sets.
 void lrs_kernel_scratch_layout(uint32_t n, uint64_t* stride, uint64_t* bitmap_off, uint64_t* tiles_off,
-                               uint64_t* lanes_off);
+                               uint64_t* lanes_off, uint64_t* lists_off);
 cudaError_t lrs_kernel_set_smem(size_t bytes);
 cudaError_t lrs_kernel_occupancy(int* ctas_per_sm, size_t smem);
 cudaError_t lrs_kernel_launch(const lrs_kernel_args_t* args, uint32_t grid, size_t smem, cudaStream_t s);

@@ -33,12 +33,11 @@ namespace {
 
 constexpr size_t kScratchBytes = (size_t)LRS_NOALLOC_SCRATCH_BYTES;
 constexpr uint32_t kMaxTableEntries = 131072;  // libm exceptions (about 103,000 on glibc 2.39)
-constexpr uint32_t kIndexBlocks = ((lrs::kExpDomainHi - 0x80000000u) >> lrs::kExpBlockShift) + 1;
 constexpr int kMaxDevices = 64;
 
 // The kernel's working memory, one copy per device.
 static __device__ __align__(256) unsigned long long g_scratch[kScratchBytes / 8];
-static __device__ __align__(256) unsigned long long g_exp_index[kIndexBlocks];
+static __device__ __align__(256) unsigned long long g_exp_index[lrs::kExpIndexWords];
 static __device__ __align__(256) uint2 g_exp_entries[kMaxTableEntries + 1];
 static __device__ __align__(256) uint32_t g_counter[2];  // [0] row counter, [1] error word
 
@@ -56,7 +55,7 @@ std::mutex g_setup_lock;
 
 // Host copies of the table, filled once from the file (no heap allocation).
 uint2 h_entries[kMaxTableEntries];
-unsigned long long h_index[kIndexBlocks];
+unsigned long long h_index[lrs::kExpIndexWords];
 uint32_t h_count = 0;
 bool h_loaded = false;
 
@@ -93,10 +92,12 @@ int load_table_once() {
         if (!(expf(x) == y)) return LRS_E_INVALID;
     }
     uint32_t j = 0;
-    for (uint32_t b = 0; b < kIndexBlocks; ++b) {
+    memset(h_index, 0, sizeof h_index);
+    for (uint32_t b = 0; b < lrs::kExpBlocks; ++b) {
         const uint32_t start = j;
         while (j < hdr[0] && ((h_entries[j].x - 0x80000000u) >> lrs::kExpBlockShift) == b) ++j;
-        h_index[b] = ((unsigned long long)start << 32) | (unsigned long long)(j - start);
+        h_index[lrs::kExpBitWords + b] = ((unsigned long long)start << 32) | (unsigned long long)(j - start);
+        if (j > start) h_index[b >> 6] |= 1ull << (b & 63);
     }
     if (j != hdr[0]) return LRS_E_INVALID;
     h_count = hdr[0];
@@ -155,8 +156,8 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
     const DeviceSetup& s = g_setup[device];
     if (rc == LRS_OK) {
         const size_t smem = lrs_kernel_smem_bytes();
-        uint64_t per_cta = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0;  // scratch words per CTA and its layout
-        lrs_kernel_scratch_layout(n, &per_cta, &bitmap_off, &tiles_off, &lanes_off);
+        uint64_t per_cta = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0, lists_off = 0;  // scratch words per CTA and its layout
+        lrs_kernel_scratch_layout(n, &per_cta, &bitmap_off, &tiles_off, &lanes_off, &lists_off);
         uint32_t grid = (uint32_t)(kScratchBytes / 8 / per_cta);
         if (grid > (uint32_t)s.ctas) grid = (uint32_t)s.ctas;
         if (grid > rows) grid = rows;
@@ -182,6 +183,7 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.bitmap_off = bitmap_off;
         args.tiles_off = tiles_off;
         args.lanes_off = lanes_off;
+        args.lists_off = lists_off;
         args.row_counter = s.counter;
         args.err_flag = reinterpret_cast<int32_t*>(s.counter + 1);
         cudaStream_t st = (cudaStream_t)stream;
