@@ -63,6 +63,7 @@ constexpr int kDense = 256;          // a tile with more candidates is streamed 
 constexpr int kRunS = kDense / 32;   // list entries per lane run of a sparse tile
 constexpr uint32_t kDenseMark = 0xFFFFFFFFu;  // TileRec::lcnt of a dense tile
 constexpr uint32_t kNoTag = 0xFFFFFFFFu;
+constexpr uint32_t kApxKey = 0x80000000u;  // path-N key flag: p from CUDA's expf, not yet exact
 constexpr int kUBase = 149;          // skip-threshold table index = grid exponent + kUBase
 constexpr int kNU = 288;
 constexpr uint32_t kSumLive = 1u << 16;   // tile record flags
@@ -132,6 +133,7 @@ struct RowShared {
     uint32_t dense[kMaxTiles / 32];  // pass 1: tiles streamed again in pass 2 (read by the producer)
     volatile uint32_t p1done;        // pass-1 tiles of two-pass rows finished by this CTA (monotone)
     uint32_t ndense;                 // dense tiles of the current row
+    uint32_t bsorted[(kNB + 31) / 32];  // path N: buckets in exact sorted order
 };
 
 struct Geo {
@@ -1095,29 +1097,48 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         if (f.pen_on && ((__ldcg(f.bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, f.penalty);
         return x;
     };
-    if (tid == 0) {
-        // bucket limit: enough candidates for k and for top_p (+ margin); the
-        // mass of bucket b is at least count * exp(-(b+1)/kBScale) / S
-        uint32_t cc = 0;
-        double mass = 0.0;
+    if (warp == 0) {
+        // bucket limit: enough candidates for k and for top_p (+ margin); the mass of
+        // bucket b is at least count * exp(-(b+1)/kBScale) / S.  Past the first bucket
+        // whose probabilities are all below 2^-26 the scan ends (once the top-p sum is at
+        // least 1/2 nothing after it changes the sum).  One warp, 32 buckets a step.
         const double target = f.topp_on ? ((double)f.top_p + kTopPMargin) * (double)f.S : 1e300;
-        uint32_t b = 0;
-        for (; b < (uint32_t)kNB - 1; ++b) {
-            cc += f.hcnt[b];
-            const double eb = exp(-(double)(b + 1) / (double)kBScale);
-            mass += (double)f.hcnt[b] * eb;
-            // past this bucket every probability is below 2^-26: once the top-p sum is at
-            // least 1/2 nothing after it changes the sum (the scan ends there)
-            if (cc >= f.k || mass >= target || eb < 1.4901161193847656e-08 * (double)f.S) break;
+        const double exit_e = 1.4901161193847656e-08 * (double)f.S;
+        double e32 = 1.0;  // exp(-32 k / kBScale) at the start of each 32-bucket step
+        const double elane = exp(-(double)(lane + 1) / (double)kBScale) * (1.0 - 1e-12);  // (low: a lower bound)
+        uint32_t cc = 0, acc = 0, found = (uint32_t)kNB - 1;
+        double mass = 0.0;
+        for (uint32_t base = 0; base < (uint32_t)kNB - 1; base += 32) {
+            const uint32_t b = base + (uint32_t)lane;
+            const bool in = b < (uint32_t)kNB - 1;
+            const uint32_t c = in ? f.hcnt[b] : 0u;
+            const double eb = e32 * elane;
+            // inclusive prefixes of counts and masses over the lanes
+            uint32_t ci = c;
+            double mi = (double)c * eb;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t tc = __shfl_up_sync(0xFFFFFFFFu, ci, o);
+                const double tm = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+                if (lane >= o) {
+                    ci += tc;
+                    mi += tm;
+                }
+            }
+            if (in) f.hoff[b] = acc + ci - c;
+            const bool stop = in && (cc + ci >= f.k || mass + mi >= target || eb < exit_e);
+            const unsigned m = __ballot_sync(0xFFFFFFFFu, stop);
+            if (m && found == (uint32_t)kNB - 1) found = base + (uint32_t)(__ffs(m) - 1);
+            cc += __shfl_sync(0xFFFFFFFFu, ci, 31);
+            acc += __shfl_sync(0xFFFFFFFFu, ci, 31);
+            mass += __shfl_sync(0xFFFFFFFFu, mi, 31);
+            e32 *= __shfl_sync(0xFFFFFFFFu, elane, 31);  // exp(-32/kBScale)
         }
-        sh.misc[3] = b;
-        uint32_t acc = 0;
-        for (int q = 0; q < kNB - 1; ++q) {
-            f.hoff[q] = acc;
-            acc += f.hcnt[q];
+        if (lane == 0) {
+            f.hoff[kNB - 1] = acc;
+            f.hcnt[kNB - 1] = f.g.n - acc;  // everything below the histogram range
+            sh.misc[3] = found;
         }
-        f.hoff[kNB - 1] = acc;
-        f.hcnt[kNB - 1] = f.g.n - acc;  // everything below the histogram range
     }
     csync();
     const uint32_t blim = sh.misc[3];
@@ -1138,7 +1159,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             }
             const unsigned act = __ballot_sync(0xFFFFFFFFu, tk);
             if (tk) {
-                const float e = exact_expf(dd, f.exptab);
+                // CUDA's expf (within 2 ulp): keys are exactified before a bucket is ordered
+                const float e = dd == 0.0f ? 1.0f : expf(dd);
                 const float pr = __fmul_rn(e, f.inv);
                 const unsigned peers = __match_any_sync(act, b);
                 const int leader = __ffs(peers) - 1;
@@ -1146,7 +1168,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 if (lane == leader) base = atomicAdd(&f.cursor[b], (uint32_t)__popc(peers));
                 base = __shfl_sync(peers, base, leader);
                 const uint32_t slot = f.hoff[b] + base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
-                f.scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
+                f.scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i | (dd == 0.0f ? 0u : kApxKey);
             }
         };
         if (warp == 0) {
@@ -1156,14 +1178,14 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 (uint32_t)lane < f.g.head ? (uint32_t)lane : f.g.head + f.g.body + ((uint32_t)lane - f.g.head);
             take(gi, mine ? d_of(penal_g(f.g.row[gi], gi), f.inv_t, f.mx) : 0.0f, mine);
         }
-        for (uint32_t t = 0; t < f.g.nchunks; ++t) {
+        for (uint32_t t = (uint32_t)warp; t < f.g.nchunks; t += kWarps) {  // one tile per warp
             const TileRec& R = f.tt[t];
             if (!all && __fsub_rn(R.mt, f.mx) < dlim) continue;
             if (!all && R.lcnt != kDenseMark) {
                 // sparse tile: its list holds every element with d >= hist_lim
                 const uint2* ent = f.lists + R.loff;
-                for (uint32_t i0 = 0; i0 < R.lcnt; i0 += kThreads) {
-                    const uint32_t i = i0 + (uint32_t)tid;
+                for (uint32_t i0 = 0; i0 < R.lcnt; i0 += 32) {
+                    const uint32_t i = i0 + (uint32_t)lane;
                     uint2 e = make_uint2(0u, 0u);
                     if (i < R.lcnt) e = __ldcg(ent + i);
                     take(e.y, __fsub_rn(__uint_as_float(e.x), f.mx), i < R.lcnt);
@@ -1171,17 +1193,17 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 continue;
             }
             const uint32_t cnt = chunk_count(f.g, t), tb = f.g.head + t * kTile;
-            constexpr int kU = 4;  // independent loads in flight per thread
-            for (uint32_t i0 = 0; i0 < cnt; i0 += kU * kThreads) {
+            constexpr int kU = 8;  // independent loads in flight per lane
+            for (uint32_t i0 = 0; i0 < cnt; i0 += kU * 32) {
                 float xs[kU];
 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
-                    const uint32_t i = i0 + (uint32_t)(u * kThreads + tid);
+                    const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
                     xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
                 }
 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
-                    const uint32_t i = i0 + (uint32_t)(u * kThreads + tid);
+                    const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
                     take(tb + i, i < cnt ? d_of(penal_g(xs[u], tb + i), f.inv_t, f.mx) : 0.0f, i < cnt);
                 }
             }
@@ -1192,45 +1214,76 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     gather(0, blim);
     uint32_t gathered_to = blim;
     f.n_cand = f.hoff[blim] + f.hcnt[blim];
-    uint32_t sorted_to = 0;  // buckets [0, sorted_to) sorted in scratch
-    // Sort bucket b (gathering more buckets first when b is beyond the gathered
-    // range, doubling the range each time).  Buckets are sorted in order.
-    auto ensure_bucket = [&](uint32_t b) {
-        while (sorted_to <= b) {
-            const uint32_t q = sorted_to;
-            if (q > gathered_to) {
-                const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
-                gather(gathered_to + 1, hi);
-                gathered_to = hi;
-            }
-            const uint32_t cnt = f.hcnt[q];
-            if (cnt > 1) {
-                const long long ts = clock64();
-                unsigned long long* base = f.scratch + f.hoff[q];
-                if (cnt <= (uint32_t)kSortCap) {
-                    for (uint32_t i = tid; i < cnt; i += kThreads) f.sbuf[i] = base[i];
-                    csync();
-                    bitonic_sort_u64(f.sbuf, cnt);
-                    for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
-                } else {
-                    bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
-                }
-                __threadfence_block();
-                csync();
-                f.acc_sort += clock64() - ts;
-            }
-            ++sorted_to;
+    for (int q = tid; q < (kNB + 31) / 32; q += kThreads) sh.bsorted[q] = 0u;
+    csync();
+    auto bucket_of = [&](uint32_t pos) -> uint32_t {  // bucket holding sorted position pos
+        uint32_t lo = 0, hi = (uint32_t)kNB - 1;
+        while (lo < hi) {
+            const uint32_t mid = (lo + hi + 1) >> 1;
+            if (f.hoff[mid] <= pos) lo = mid; else hi = mid - 1;
         }
+        return lo;
+    };
+    auto bend = [&](uint32_t q) -> uint32_t { return f.hoff[q] + f.hcnt[q]; };
+    auto ensure_gathered = [&](uint32_t q) {
+        while (q > gathered_to) {
+            const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
+            gather(gathered_to + 1, hi);
+            gathered_to = hi;
+        }
+    };
+    // exact key of element i: p = fl(libm expf(d) * inv) (sampler.rs:129-131, ops.rs:409-416)
+    auto exact_key = [&](uint32_t i) -> unsigned long long {
+        const float d = d_of(penal_g(f.g.row[i], i), f.inv_t, f.mx);
+        const float pr = __fmul_rn(exact_expf(d, f.exptab), f.inv);
+        return ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
+    };
+    // Bucket q in exact (p desc, index asc) order: exact keys, then a bitonic sort.
+    auto ensure_sorted = [&](uint32_t q) {
+        ensure_gathered(q);
+        if ((sh.bsorted[q >> 5] >> (q & 31)) & 1u) return;
+        const long long ts = clock64();
+        const uint32_t cnt = f.hcnt[q];
+        unsigned long long* base = f.scratch + f.hoff[q];
+        for (uint32_t i = tid; i < cnt; i += kThreads) {
+            const unsigned long long kk = base[i];
+            if ((uint32_t)kk & kApxKey) base[i] = exact_key((uint32_t)kk & ~kApxKey);
+        }
+        __threadfence_block();
+        csync();
+        if (cnt > 1) {
+            if (cnt <= (uint32_t)kSortCap) {
+                for (uint32_t i = tid; i < cnt; i += kThreads) f.sbuf[i] = base[i];
+                csync();
+                bitonic_sort_u64(f.sbuf, cnt);
+                for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
+            } else {
+                bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
+            }
+            __threadfence_block();
+        }
+        if (tid == 0) sh.bsorted[q >> 5] |= 1u << (q & 31);
+        csync();
+        f.acc_sort += clock64() - ts;
     };
     auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(f.scratch[q] >> 32)); };
     // Exact sequential run over sorted positions [0, p1) of the candidate sequence
-    // (buckets in order, each sorted when reached): the first kSerial positions
-    // one by one on thread 0, then tiles.  Returns the stop position or -1.
+    // (sampler.rs:137-139 / 148-151 / 156-158).  Buckets are in order; inside a bucket
+    // the order matters only around an ordered step (a binade crossing, a tie, a big
+    // element, the stop), so chunks of whole buckets are summed in storage order on one
+    // grid, and only the bucket holding a chunk's first ordered step is made exact,
+    // sorted and run in order.  The first kSerial positions go one by one on thread 0.
+    // Returns the stop position or -1.
     auto run = [&](uint32_t p1, int dir, float& s, float thr) -> int {
-        uint32_t p = 0, b = 0;
+        if (p1 == 0) return -1;
+        {   // a limit inside a bucket needs that bucket in order
+            const uint32_t q1 = bucket_of(p1 - 1);
+            if (bend(q1) > p1) ensure_sorted(q1);
+        }
+        uint32_t p = 0;
         uint32_t serial_left = kSerial;
         while (p < p1) {
-            while (b + 1 < (uint32_t)kNB && f.hoff[b] + f.hcnt[b] <= p) ++b;
+            const uint32_t b = bucket_of(p);
             if (dir > 0) {
                 // Every remaining candidate lies in bucket b or a later one; once
                 // their probabilities are all below half the sum's grid unit no
@@ -1240,9 +1293,11 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 const int uu = unit_exp(s);
                 if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
             }
-            ensure_bucket(b);
-            const uint32_t seg_end = min(p1, f.hoff[b] + f.hcnt[b]);
+            ensure_gathered(b);
+            const bool b_sorted = (sh.bsorted[b >> 5] >> (b & 31)) & 1u;
             if (serial_left > 0) {
+                ensure_sorted(b);
+                const uint32_t seg_end = min(p1, bend(b));
                 const uint32_t m = min(seg_end - p, serial_left);
                 for (uint32_t q = tid; q < m; q += kThreads) sh.ser[q] = pval(p + q);
                 csync();
@@ -1260,34 +1315,105 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 serial_left -= m;
                 continue;
             }
-            const uint32_t tc = min((uint32_t)kChunk, seg_end - p);
+            // chunk [p, e): whole buckets, or a piece of a sorted bucket (a bucket larger
+            // than a chunk is sorted first)
+            uint32_t e;
+            if (b_sorted || bend(b) - p > (uint32_t)kChunk) {
+                if (!b_sorted) ensure_sorted(b);
+                e = min(min(p1, bend(b)), p + (uint32_t)kChunk);
+            } else {
+                uint32_t q = b;
+                e = bend(b);
+                while (q + 1 < (uint32_t)kNB && q + 1 <= gathered_to && bend(q + 1) <= p1 &&
+                       bend(q + 1) - p <= (uint32_t)kChunk && !((sh.bsorted[(q + 1) >> 5] >> ((q + 1) & 31)) & 1u)) {
+                    ++q;
+                    e = bend(q);
+                }
+                e = min(e, p1);
+            }
+            const uint32_t tc = e - p;
             float v[kVpt];
-            uint32_t ex = 0xFFFFFFFFu;
             load_sorted_tile(f.scratch + p, tc, v);
-            // single-grid fast check
+            // increments on the running value's grid, exact where an approximate key's
+            // error bound could change them
             const int uu = unit_exp(s);
             const uint32_t A = grid_count(s, uu);
-            uint32_t t = 0, f = 0;
-#pragma unroll
+            uint32_t inc[kVpt];
+            uint32_t t = 0, fl = 0, spm = 0;
+#pragma unroll 1
             for (int i = 0; i < kVpt; ++i) {
-                if ((uint32_t)li_of(i) < tc) {
-                    const Cls c = classify(__float_as_uint(v[i]), uu);
+                inc[i] = 0;
+                const int li = li_of(i);
+                if ((uint32_t)li < tc) {
+                    const unsigned long long kk = f.scratch[p + li];
+                    uint32_t vb = __float_as_uint(v[i]);
+                    if ((uint32_t)kk & kApxKey) {
+                        const Cls lo = classify(vb > 8u ? vb - 8u : 0u, uu), hi = classify(vb + 8u, uu);
+                        if (!(lo.inc == hi.inc && !lo.tie && !hi.tie && !lo.big && !hi.big) && !(lo.big && hi.big)) {
+                            const unsigned long long ek = exact_key((uint32_t)kk & ~kApxKey);
+                            f.scratch[p + li] = ek;
+                            v[i] = __uint_as_float(~(uint32_t)(ek >> 32));
+                            vb = __float_as_uint(v[i]);
+                        }
+                    }
+                    const Cls c = classify(vb, uu);
+                    inc[i] = c.inc;
                     t = sat_add(t, c.inc);
-                    f |= (c.tie || c.big) ? 1u : 0u;
+                    if (c.tie || c.big) {
+                        fl = 1u;
+                        spm |= 1u << i;
+                    }
                 }
             }
             t = block_reduce_u32(t, SatAdd(), sh.red);
-            f = block_reduce_u32(f, OrOp(), sh.red2);
+            fl = block_reduce_u32(fl, OrOp(), sh.red2);
             const float tq = (dir > 0 && thr < kInf) ? ldexpf(thr, -uu) : kInf;
-            const bool fast = dir > 0 ? (!f && A + t <= kTwo24 - 1u && (float)(A + t) < tq)
-                                      : (!f && t < A - grid_lower(uu));
+            const bool fast = dir > 0 ? (!fl && A + t <= kTwo24 - 1u && (float)(A + t) < tq)
+                                      : (!fl && t < A - grid_lower(uu));
             if (fast) {
                 s = grid_value(uu, dir > 0 ? A + t : A - t);
-            } else {
-                const int stp = tile2(v, ex, 0, (int)tc, dir, s, thr, NoExact(), sh);
-                if (stp >= 0) return (int)p + stp;
+                p = e;
+                continue;
             }
-            p += tc;
+            // the first ordered step in storage order: its bucket is where the order matters
+            uint32_t incl[kVpt];
+            (void)block_incl_scan(inc, incl, sh.red);
+            uint32_t cand = 0xFFFFFFFFu;
+            const uint32_t lower = grid_lower(uu);
+#pragma unroll 1
+            for (int i = 0; i < kVpt; ++i) {
+                const int li = li_of(i);
+                if ((uint32_t)li < tc && (uint32_t)li < cand &&
+                    needs_step(dir, (spm >> i) & 1u, A, incl[i], lower, tq))
+                    cand = (uint32_t)li;
+            }
+            uint32_t first = block_reduce_u32(cand, MinU(), sh.red2);
+            if (first >= tc) first = 0;  // (cannot happen: then order the chunk's first bucket)
+            const uint32_t qe = bucket_of(p + first);
+            const uint32_t bstart = max(p, f.hoff[qe]);
+            // the buckets before qe in this chunk: summed in any order on this grid
+            if (bstart > p) {
+#pragma unroll 1
+                for (int i = 0; i < kVpt; ++i)
+                    if ((uint32_t)li_of(i) == bstart - p - 1) sh.fstate = grid_value(uu, dir > 0 ? A + incl[i] : A - incl[i]);
+                csync();
+                s = sh.fstate;
+                csync();
+            }
+            ensure_sorted(qe);
+            // bucket qe (from bstart) in exact order
+            uint32_t q0 = bstart;
+            const uint32_t qend = min(p1, bend(qe));
+            while (q0 < qend) {
+                const uint32_t tq2 = min((uint32_t)kChunk, qend - q0);
+                float w[kVpt];
+                uint32_t ex = 0xFFFFFFFFu;
+                load_sorted_tile(f.scratch + q0, tq2, w);
+                const int stp = tile2(w, ex, 0, (int)tq2, dir, s, thr, NoExact(), sh);
+                if (stp >= 0) return (int)q0 + stp;
+                q0 += tq2;
+            }
+            p = qend;
         }
         return -1;
     };
@@ -1306,11 +1432,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     } else {
         f.pos = 0;
     }
-    {
-        uint32_t b = 0;
-        while (b + 1 < (uint32_t)kNB && f.hoff[b] + f.hcnt[b] <= f.pos) ++b;
-        ensure_bucket(b);
-    }
+    ensure_sorted(bucket_of(f.pos));
     f.chosen = f.scratch[f.pos];
     csync();
 }
