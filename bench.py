@@ -14,6 +14,10 @@ e2e        the same metric through the host-buffer entry point (lrs_sample): pin
 roofline   algorithmic bytes (4 * vocab + 4 * window per row) / kernel time vs measured HBM copy bandwidth
 cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of the same rows
 --impl reference  times that CPU restatement alone (all host threads) on the same workload
+--workload vocab_sharded  config 5 instead: 64 x 151,936 rows whose columns are split over the
+           N ranks; a step is the exchange (NCCL all-gather of the shards + row assembly) and
+           the sampling of every row on every rank; reports latency, the exchange's share and
+           a check of the tokens against an unsharded sample
 """
 from __future__ import annotations
 
@@ -149,6 +153,86 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_vocab_sharded(args, world, rank, local):
+    """Config 5: columns split over the ranks, one all-gather per step (lrs.sharded)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import lrs
+    from lrs import sharded
+    from lrs import workloads as W
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    w = W.vocab_sharded()
+    rows, V = w.rows, w.vocab
+    cols = sharded.shard_columns(V, world, rank)
+    vsamp = sharded.VocabShardedSampler(rows, V, w.window, device=local)
+    shard = torch.from_numpy(np.ascontiguousarray(w.logits[:, cols])).to(dev)
+    hist = torch.from_numpy(w.hist.view(np.int32)).to(dev)
+    hlen = torch.from_numpy(w.hist_len.view(np.int32)).to(dev)
+    params = torch.from_numpy(w.params.view(np.uint8)).to(dev)
+    state0 = torch.from_numpy(w.state.view(np.int64)).to(dev)
+    state = state0.clone()
+    tokens = torch.zeros(rows, dtype=torch.int32, device=dev)
+    status = torch.zeros(rows, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    # correctness first: one step from the initial states against an unsharded sample
+    vsamp.sample(shard, params, state, tokens, hist=hist, hist_len=hlen, status=status)
+    torch.cuda.synchronize()
+    ok = None
+    if rank == 0:
+        ref = lrs.BatchSampler(rows, V, w.window, device=local)
+        full = torch.from_numpy(w.logits).to(dev)
+        st2 = state0.clone()
+        tok2 = torch.zeros(rows, dtype=torch.int32, device=dev)
+        ref.sample_device(full, params, st2, tok2, hist=hist, hist_len=hlen)
+        torch.cuda.synchronize()
+        ok = bool(torch.equal(tok2, tokens)) and bool(torch.equal(st2, state)) and int((status != 0).sum()) == 0
+        ref.close()
+    for _ in range(args.warmup):
+        vsamp.sample(shard, params, state, tokens, hist=hist, hist_len=hlen, status=status)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ex = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for i in range(args.steps):
+        ex[i][0].record(stream)
+        vsamp.exchange(shard)
+        ex[i][1].record(stream)
+        vsamp.bs.sample_device(vsamp.full, params, state, tokens, n=V, hist=hist, hist_len=hlen, status=status)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    total_ms = t0.elapsed_time(t1)
+    exch_ms = sum(a.elapsed_time(b) for a, b in ex)
+    if world > 1:
+        tt = torch.tensor([total_ms, exch_ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        total_ms, exch_ms = float(tt[0].item()), float(tt[1].item())
+    if rank == 0:
+        line = {
+            "metric": "config 5 (vocab-sharded) step latency", "value": total_ms / args.steps, "unit": "ms",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"config 5: {rows} x {V} f32 rows, columns split over {world} GPU(s) "
+                                   f"({V // world} each), one all-gather per step, top_k 50, top_p 0.95, temp 0.7",
+                       "parallelism": f"vocabulary over {world} GPU(s)"},
+            "exchange_ms_per_step": exch_ms / args.steps, "exchange_share": exch_ms / total_ms,
+            "tokens_match_unsharded": ok, "gpu_launches": 2 * args.steps,
+        }
+        print(json.dumps(line), flush=True)
+    vsamp.close()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -160,10 +244,14 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--ref-rows", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
+    ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.workload == "vocab_sharded":
+        run_vocab_sharded(args, world, rank, local)
         return
 
     import torch

@@ -162,6 +162,18 @@ int  lrs_sample_device_noalloc(int device, const float* d_logits, uint32_t rows,
                                const lrs_params* d_params, uint64_t* d_state,
                                uint32_t* d_tokens, float* d_probs, int32_t* d_status, void* stream);
 
+/* ---- vocabulary-sharded rows (multi-GPU exchange) -------------------------------
+ * lrs_assemble_shards  the exchange step of vocabulary sharding: G ranks each hold
+ *                      columns [g*shard_n, (g+1)*shard_n) of `rows` rows; after one
+ *                      all-gather (NCCL, rank-major: d_gathered[g][row][col]) this writes
+ *                      the full rows d_out[row][g*shard_n + col] (leading dimension
+ *                      ld_out >= G*shard_n), ready for lrs_sample_device.  It replaces the
+ *                      per-rank logits slice a tensor-parallel LM head would hand to
+ *                      Sampler::sample (model.rs:752-761 calls it with the full vocab).
+ * Enqueued on `stream` (cudaStream_t); returns LRS_OK, LRS_E_INVALID or LRS_E_CUDA.   */
+int  lrs_assemble_shards(const float* d_gathered, uint32_t shards, uint32_t rows, uint32_t shard_n,
+                         float* d_out, uint64_t ld_out, void* stream);
+
 /* ---- single-row drop-in (Sampler API) -------------------------------------------
  * lrs_sampler_new    replaces Sampler::new(seed)               (sampler.rs:33-37)
  * lrs_sampler_sample replaces Sampler::sample(logits, params, recent) (sampler.rs:56)

@@ -144,9 +144,45 @@ static int load_exp_table(lrs_ctx* ctx) {
 
 static size_t dyn_smem_bytes(uint32_t) { return lrs_kernel_smem_bytes(); }
 
+// Rows of vocabulary shards: out[row][g * shard_n + col] = in[g][row][col].  One thread
+// per 4 floats when the widths allow 16-byte accesses, else one per float.
+__global__ void lrs_assemble_kernel(const float* __restrict__ in, uint32_t shards, uint32_t rows, uint32_t shard_n,
+                                    float* __restrict__ out, uint64_t ld_out, bool vec4) {
+    const uint64_t per_row = (uint64_t)shards * shard_n;
+    const uint64_t total = (uint64_t)rows * per_row;
+    const uint64_t step = (uint64_t)gridDim.x * blockDim.x;
+    if (vec4) {
+        for (uint64_t i = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < total; i += step * 4) {
+            const uint64_t row = i / per_row, c = i % per_row;
+            const uint64_t g = c / shard_n, col = c % shard_n;
+            const float4 v = *reinterpret_cast<const float4*>(in + (g * rows + row) * shard_n + col);
+            *reinterpret_cast<float4*>(out + row * ld_out + c) = v;
+        }
+    } else {
+        for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += step) {
+            const uint64_t row = i / per_row, c = i % per_row;
+            const uint64_t g = c / shard_n, col = c % shard_n;
+            out[row * ld_out + c] = in[(g * rows + row) * shard_n + col];
+        }
+    }
+}
+
 extern "C" {
 
 uint64_t lrs_seed_state(uint64_t seed) { return seed | 1ull; }  // sampler.rs:33-37
+
+int lrs_assemble_shards(const float* d_gathered, uint32_t shards, uint32_t rows, uint32_t shard_n, float* d_out,
+                        uint64_t ld_out, void* stream) {
+    if (!d_gathered || !d_out || shards == 0 || rows == 0 || shard_n == 0) return LRS_E_INVALID;
+    if (ld_out < (uint64_t)shards * shard_n) return LRS_E_INVALID;
+    const bool vec4 = shard_n % 4 == 0 && ld_out % 4 == 0 && (uintptr_t)d_gathered % 16 == 0 && (uintptr_t)d_out % 16 == 0;
+    const uint64_t work = (uint64_t)rows * shards * shard_n / (vec4 ? 4 : 1);
+    uint64_t blocks = (work + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    lrs_assemble_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(d_gathered, shards, rows, shard_n, d_out,
+                                                                          ld_out, vec4);
+    return cudaGetLastError() == cudaSuccess ? LRS_OK : LRS_E_CUDA;
+}
 
 const char* lrs_last_error(const lrs_ctx* ctx) {
     return ctx ? ctx->err.c_str() : g_create_error.c_str();

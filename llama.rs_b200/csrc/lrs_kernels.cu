@@ -832,26 +832,14 @@ __device__ __forceinline__ void apply_penalty(float (&v)[32], uint32_t bits, int
 }
 
 // Adds, one after the other, the exponentials held by lanes [lo, lo + cnt) to s; every
-// lane returns the same sum (ops.rs:408-411).  e is CUDA's expf(d), within 2 ulp of
-// exp, unless `exact`; where the rounding of an addition could depend on where libm's
-// value lies within that bound, that lane's exact value (exact_expf(d)) is taken.
+// lane returns the same sum (ops.rs:408-411).  e is CUDA's expf(d) unless `exact`:
+// libm's value (exact_expf(d)) is computed by every such lane at once, before the
+// ordered additions, so one table latency is paid per call, not one per element.
 __device__ __noinline__ float warp_serial_add(float s, float e, float d, bool exact, int lo, int cnt,
                                               const ExpTable& tab) {
     const int lane = threadIdx.x & 31;
-    const unsigned apx = __ballot_sync(0xFFFFFFFFu, !exact);
-    for (int j = lo; j < lo + cnt; ++j) {
-        float ej = __shfl_sync(0xFFFFFFFFu, e, j);
-        if ((apx >> j) & 1u) {
-            const uint32_t b = __float_as_uint(ej);
-            const float elo = __uint_as_float(b > 4u ? b - 4u : 0u), ehi = __uint_as_float(b + 4u);
-            if (__fadd_rn(s, elo) != __fadd_rn(s, ehi)) {
-                float ex = 0.0f;
-                if (lane == j) ex = exact_expf(d, tab);
-                ej = __shfl_sync(0xFFFFFFFFu, ex, j);
-            }
-        }
-        s = __fadd_rn(s, ej);
-    }
+    if (!exact && lane >= lo && lane < lo + cnt) e = exact_expf(d, tab);
+    for (int j = lo; j < lo + cnt; ++j) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e, j));
     return s;
 }
 
@@ -1731,7 +1719,30 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const uint32_t ncand = __shfl_sync(0xFFFFFFFFu, cinc, 31);
                 const bool dense = ncand > (uint32_t)kDense;
                 float sl = 0.0f;
-                {
+                if (dense) {
+                    // many candidates: one predicated pass over the staged run
+                    float sp[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                        if (c4 >= nval) continue;
+                        const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                        float x[4] = {q.x, q.y, q.z, q.w};
+                        const uint32_t pb = (bits >> c4) & 15u;
+                        if (pb) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
+                        }
+                        const uint32_t cb = cmask >> c4;
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const float ev = ex2_approx(__fmul_rn(__fsub_rn(__fmul_rn(x[c], inv_t), ml), kLog2e));
+                            sp[c] += ((cb >> c) & 1u) ? ev : 0.0f;
+                        }
+                    }
+                    sl = (sp[0] + sp[1]) + (sp[2] + sp[3]);
+                } else {
                     uint32_t p = woff + cinc - nc;
                     uint32_t m = cmask;
                     while (m) {
@@ -1741,7 +1752,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
                         const float xs = __fmul_rn(xv, inv_t);
                         sl += ex2_approx(__fmul_rn(__fsub_rn(xs, ml), kLog2e));
-                        if (!dense) wlist[p++] = make_uint2(__float_as_uint(xs), tb + l0 + (uint32_t)pos);
+                        wlist[p++] = make_uint2(__float_as_uint(xs), tb + l0 + (uint32_t)pos);
                     }
                 }
                 __syncwarp();

@@ -43,7 +43,7 @@ ROW_INFO_DTYPE = np.dtype([
 EXPORTS = [
     "lrs_create", "lrs_destroy", "lrs_last_error", "lrs_seed_state", "lrs_set_state", "lrs_get_state",
     "lrs_set_params", "lrs_sample", "lrs_sample_device", "lrs_sampler_new", "lrs_sampler_free",
-    "lrs_sampler_state", "lrs_sampler_sample", "lrs_sample_device_noalloc",
+    "lrs_sampler_state", "lrs_sampler_sample", "lrs_sample_device_noalloc", "lrs_assemble_shards",
 ]
 
 
@@ -85,6 +85,8 @@ def lib() -> ctypes.CDLL:
         L.lrs_sample_device.restype = I
         L.lrs_sample_device_noalloc.argtypes = [I, P, U32, U32, U64, P, U64, P, P, P, P, P, P, P]
         L.lrs_sample_device_noalloc.restype = I
+        L.lrs_assemble_shards.argtypes = [P, U32, U32, U32, P, U64, P]
+        L.lrs_assemble_shards.restype = I
         L.lrs_sampler_new.argtypes = [U64, I]
         L.lrs_sampler_new.restype = P
         L.lrs_sampler_free.argtypes = [P]
