@@ -64,7 +64,7 @@ def profile_traffic(name="lrs_sample_rows_headline.txt"):
 
 class Clocks:
     """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -72,37 +72,61 @@ class Clocks:
         self.index = index
         self.proc = None
         self.path = os.path.join("/tmp", f"lrs_clocks_{os.getpid()}.csv")
+        self.window = None
 
     def start(self):
+        """Starts sampling every 20 ms and waits (up to 3 s) for the first sample."""
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t = time.time()
+        while time.time() - t < 3.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                pass
+            time.sleep(0.01)
+
+    def mark(self, t0, t1):
+        """The timed region's wall-clock bounds (samples outside it are dropped)."""
+        self.window = (t0, t1)
 
     def stop(self):
         if not self.proc:
             return None
+        time.sleep(0.05)
         self.proc.terminate()
         self.proc.wait()
-        sm, mx, reasons = [], 0.0, set()
+        import datetime
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        samples = []
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = max(mx, float(f[2]))
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, float(f[2]), float(f[3]), f[6:10]))
             except ValueError:
                 continue
-            for nm, v in zip(names, f[5:9]):
+        if not samples:
+            return None
+        inside = samples
+        if self.window:
+            lo, hi = self.window
+            inside = [x for x in samples if lo - 0.025 <= x[0] <= hi + 0.025] or samples
+        reasons = set()
+        for _, _, _, flags in inside:
+            for nm, v in zip(names, flags):
                 if v.lower() == "active":
                     reasons.add(nm)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": statistics.median(x[1] for x in inside), "sm_max_mhz": max(x[2] for x in inside),
+                "reasons": sorted(reasons), "samples": len(inside)}
 
 
 def dist_setup(n_gpus):
@@ -298,6 +322,7 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
+    w0 = time.time()
     t0.record(stream)
     for i in range(args.steps):
         ev[i][0].record(stream)
@@ -305,6 +330,7 @@ def main():
         ev[i][1].record(stream)
     t1.record(stream)
     torch.cuda.synchronize()
+    clocks.mark(w0, time.time())
     if pg:
         pg.barrier()
     clk = clocks.stop()
