@@ -7,32 +7,35 @@
 //   softmax (ops.rs:397-419), top-k (122-132), top-p (135-146), survivor sum (148-151)
 //   and the categorical draw with the row's xorshift64* state (152-162).
 //
-// Structure.  A persistent CTA (two per SM) has eight consumer warps and one producer
+// Structure.  A persistent CTA (two per SM) has seven consumer warps and one producer
 // warp.  The producer takes rows from a global counter, passes them to the consumers
 // through a small row queue and streams each row through a ring of 4 KB shared-memory
 // slots with bulk copies (TMA engine; a slot's `full` mbarrier completes on the bytes,
-// its `empty` mbarrier is released by the warp that consumed it): once for pass 1 and,
-// for stochastic rows, once more for pass 2.  A slot holds one tile of 1024 floats;
-// consumer warp w takes tiles w, w+8, w+16, ... and each lane owns a run of 32
-// consecutive elements of the tile.
+// its `empty` mbarrier is released by the warp that consumed it).  A slot holds one tile
+// of 1024 floats; consumer warp w takes tiles w, w+7, w+14, ... and each lane owns a run
+// of 32 consecutive elements of the tile.
 //   pass 1  per tile: the max (NaN-propagating), the argmax of greedy rows, the tile's
-//           online-softmax statistics (its max and the sum of exp relative to it) and,
-//           on path K, a per-warp streaming top-k filter.
+//           online-softmax statistics (its max and the sum of exp relative to it), on
+//           path K a per-warp streaming top-k filter, and the tile's candidate list: the
+//           elements no more than 18.1 below a lower bound of the running max (the only
+//           ones that can change the softmax sum or reach a path-N bucket).  A tile with
+//           more than kDense candidates is marked dense instead.
 //   prep    the row max; from the tile statistics an estimate of the running softmax
 //           sum at every tile start with a proven relative error bound, hence the
 //           lowest binade grid the exact running sum can be on there and a threshold
 //           below which an element cannot change it.  Tiles without a live element are
-//           skipped by pass 2.
+//           skipped by pass 2; the producer streams only the dense tiles again.
 //   pass 2  per lane, the increments of its run on the two grids the running sum can
-//           be on over that run (lrs_grid.h).  The exact running sum is then handed
-//           from tile to tile (a baton in shared memory); each hand-over is one warp
-//           scan of the 32 lane increments, and only a run with a binade crossing, a
-//           tie, an element of half a binade or a missed grid is summed element by
-//           element with hardware f32 adds.
+//           be on over that run (lrs_grid.h), from the staged tile (dense) or from the
+//           candidate list (sparse).  The exact running sum is then handed from tile to
+//           tile (a baton in shared memory); each hand-over is one warp scan of the 32
+//           lane increments, and only a run with a binade crossing, a tie, an element of
+//           half a binade or a missed grid is summed element by element with hardware
+//           f32 adds.
 //   finish  path K (top_k <= kKMax): the filter's candidates sorted in shared memory;
-//           path N: candidates bucketed by (max - x) during pass 2, gathered with exact
-//           probabilities into global scratch and sorted bucket by bucket as the top-p
-//           scan and the draw reach them (sampler.rs:122-162).
+//           path N: candidates bucketed by (max - x) during pass 2, gathered into global
+//           scratch with approximate keys, and made exact and sorted bucket by bucket
+//           only where the top-p scan and the draw need the order (sampler.rs:122-162).
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -1086,16 +1089,44 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         return x;
     };
     if (warp == 0) {
-        // bucket limit: enough candidates for k and for top_p (+ margin); the mass of
-        // bucket b is at least count * exp(-(b+1)/kBScale) / S.  Past the first bucket
-        // whose probabilities are all below 2^-26 the scan ends (once the top-p sum is at
-        // least 1/2 nothing after it changes the sum).  One warp, 32 buckets a step.
+        // Bucket limit: the first bucket through which the gathered candidates are
+        // expected to hold the top-k / top-p survivors (the scan gathers more buckets
+        // when it needs them, so this limit only sizes the first gather).  The mass of
+        // bucket b lies in [count exp(-(b+1)/kBScale), count exp(-b/kBScale)].  Stop at
+        // k candidates, at a lower bound of the head mass of (top_p + margin) S, or
+        // where an upper bound of the mass after the bucket (the elements below the
+        // histogram range included, each below exp(-18)) is at most (1 - top_p -
+        // margin) S.  Past the first bucket whose probabilities are all below 2^-26 the
+        // scan ends (once the top-p sum is at least 1/2 nothing after it changes the
+        // sum).  One warp, 32 buckets a step.
         const double target = f.topp_on ? ((double)f.top_p + kTopPMargin) * (double)f.S : 1e300;
+        const double tail_target = f.topp_on ? (1.0 - (double)f.top_p - kTopPMargin) * (double)f.S : -1.0;
         const double exit_e = 1.4901161193847656e-08 * (double)f.S;
-        double e32 = 1.0;  // exp(-32 k / kBScale) at the start of each 32-bucket step
         const double elane = exp(-(double)(lane + 1) / (double)kBScale) * (1.0 - 1e-12);  // (low: a lower bound)
+        const double ewidth = exp(1.0 / (double)kBScale) * (1.0 + 1e-9);  // upper / lower bound of a bucket
+        const double estep = __shfl_sync(0xFFFFFFFFu, elane, 31);        // exp(-32/kBScale)
+        // upper bound of the whole mass (first sweep)
+        double utot = 0.0;
+        uint32_t ctot = 0;
+        {
+            double e32 = 1.0;
+            for (uint32_t base = 0; base < (uint32_t)kNB - 1; base += 32) {
+                const uint32_t b = base + (uint32_t)lane;
+                const uint32_t c = b < (uint32_t)kNB - 1 ? f.hcnt[b] : 0u;
+                utot += (double)c * e32 * elane * ewidth;
+                ctot += c;
+                e32 *= estep;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                utot += __shfl_xor_sync(0xFFFFFFFFu, utot, o);
+                ctot += __shfl_xor_sync(0xFFFFFFFFu, ctot, o);
+            }
+            utot += (double)(f.g.n - ctot) * 1.5229979744712629e-08;  // exp(-18)
+        }
+        double e32 = 1.0;  // exp(-32 k / kBScale) at the start of each 32-bucket step
         uint32_t cc = 0, acc = 0, found = (uint32_t)kNB - 1;
-        double mass = 0.0;
+        double mass = 0.0, umass = 0.0;
         for (uint32_t base = 0; base < (uint32_t)kNB - 1; base += 32) {
             const uint32_t b = base + (uint32_t)lane;
             const bool in = b < (uint32_t)kNB - 1;
@@ -1114,13 +1145,15 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 }
             }
             if (in) f.hoff[b] = acc + ci - c;
-            const bool stop = in && (cc + ci >= f.k || mass + mi >= target || eb < exit_e);
+            const bool tail_ok = tail_target > 0.0 && utot - (umass + mi * ewidth) <= tail_target;
+            const bool stop = in && (cc + ci >= f.k || mass + mi >= target || tail_ok || eb < exit_e);
             const unsigned m = __ballot_sync(0xFFFFFFFFu, stop);
             if (m && found == (uint32_t)kNB - 1) found = base + (uint32_t)(__ffs(m) - 1);
             cc += __shfl_sync(0xFFFFFFFFu, ci, 31);
             acc += __shfl_sync(0xFFFFFFFFu, ci, 31);
             mass += __shfl_sync(0xFFFFFFFFu, mi, 31);
-            e32 *= __shfl_sync(0xFFFFFFFFu, elane, 31);  // exp(-32/kBScale)
+            umass += __shfl_sync(0xFFFFFFFFu, mi, 31) * ewidth;
+            e32 *= estep;
         }
         if (lane == 0) {
             f.hoff[kNB - 1] = acc;
@@ -1184,15 +1217,20 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             constexpr int kU = 8;  // independent loads in flight per lane
             for (uint32_t i0 = 0; i0 < cnt; i0 += kU * 32) {
                 float xs[kU];
+                uint32_t pw[kU];  // window-bitmap word of each element
 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
                     const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
                     xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
+                    pw[u] = (f.pen_on && i < cnt) ? __ldcg(f.bitmap + ((tb + i) >> 5)) : 0u;
                 }
 #pragma unroll
                 for (int u = 0; u < kU; ++u) {
                     const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
-                    take(tb + i, i < cnt ? d_of(penal_g(xs[u], tb + i), f.inv_t, f.mx) : 0.0f, i < cnt);
+                    const float xv = ((pw[u] >> ((tb + i) & 31)) & 1u) ? penalise(xs[u], f.penalty) : xs[u];
+                    const float dd = i < cnt ? d_of(xv, f.inv_t, f.mx) : -kInf;
+                    if (!all && !__any_sync(0xFFFFFFFFu, dd >= dlim)) continue;
+                    take(tb + i, dd, i < cnt);
                 }
             }
         }
@@ -1254,6 +1292,27 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         csync();
         f.acc_sort += clock64() - ts;
     };
+    auto is_sorted = [&](uint32_t q) -> bool { return (sh.bsorted[q >> 5] >> (q & 31)) & 1u; };
+    // Buckets [qa, qb] (at most kSortCap elements) as one range in exact order: the
+    // buckets ahead of the first ordered steps hold a few candidates each, and one
+    // sort of all of them replaces a sort per bucket.
+    auto sort_range = [&](uint32_t qa, uint32_t qb) {
+        ensure_gathered(qb);
+        const long long ts = clock64();
+        const uint32_t lo = f.hoff[qa], cnt = bend(qb) - lo;
+        unsigned long long* base = f.scratch + lo;
+        for (uint32_t i = tid; i < cnt; i += kThreads) {
+            const unsigned long long kk = base[i];
+            f.sbuf[i] = ((uint32_t)kk & kApxKey) ? exact_key((uint32_t)kk & ~kApxKey) : kk;
+        }
+        csync();
+        bitonic_sort_u64(f.sbuf, cnt);
+        for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
+        __threadfence_block();
+        for (uint32_t q = qa + tid; q <= qb; q += kThreads) atomicOr(&sh.bsorted[q >> 5], 1u << (q & 31));
+        csync();
+        f.acc_sort += clock64() - ts;
+    };
     auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(f.scratch[q] >> 32)); };
     // Exact sequential run over sorted positions [0, p1) of the candidate sequence
     // (sampler.rs:137-139 / 148-151 / 156-158).  Buckets are in order; inside a bucket
@@ -1282,10 +1341,25 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
             }
             ensure_gathered(b);
-            const bool b_sorted = (sh.bsorted[b >> 5] >> (b & 31)) & 1u;
+            const bool b_sorted = is_sorted(b);
             if (serial_left > 0) {
-                ensure_sorted(b);
-                const uint32_t seg_end = min(p1, bend(b));
+                if (!b_sorted) {
+                    // every bucket the serial positions reach, in one sort when they fit
+                    // (gathered buckets only: the run may stop before it needs more)
+                    uint32_t qs = min(bucket_of(min(p1, p + serial_left) - 1u), gathered_to);
+                    while (qs > b && bend(qs) - f.hoff[b] > (uint32_t)kSortCap) --qs;
+                    if (qs > b)
+                        sort_range(b, qs);
+                    else
+                        ensure_sorted(b);
+                }
+                // the sorted stretch from p (whole sorted buckets in a row are in order)
+                uint32_t seg_end = bend(b), q = b;
+                while (q + 1u < (uint32_t)kNB && seg_end < p1 && seg_end - p < serial_left && is_sorted(q + 1u)) {
+                    ++q;
+                    seg_end = bend(q);
+                }
+                seg_end = min(p1, seg_end);
                 const uint32_t m = min(seg_end - p, serial_left);
                 for (uint32_t q = tid; q < m; q += kThreads) sh.ser[q] = pval(p + q);
                 csync();
@@ -1420,7 +1494,46 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     } else {
         f.pos = 0;
     }
-    ensure_sorted(bucket_of(f.pos));
+    // The element at the drawn position.  Buckets split the order by d, so elements of
+    // equal probability (d a few ulp apart) can sit on both sides of a bucket boundary,
+    // each side in index order: such a group is put in index order across the boundary.
+    uint32_t qp = bucket_of(f.pos);
+    ensure_sorted(qp);
+    const uint32_t pk = (uint32_t)(f.scratch[f.pos] >> 32);
+    uint32_t g0 = f.hoff[qp], g1 = bend(qp);
+    while (g0 < f.pos && (uint32_t)(f.scratch[g0] >> 32) != pk) ++g0;   // (sorted: a short scan of
+    while (g1 > f.pos + 1u && (uint32_t)(f.scratch[g1 - 1u] >> 32) != pk) --g1;  // equal keys is rare)
+    bool wide = false;
+    // bucket q holds d in (-(q+1)/kBScale, -q/kBScale], so its probabilities lie in
+    // [P(-(q+1)/kBScale), P(-q/kBScale)] with P(d) = fl(expf(d) inv) monotone: a
+    // neighbour can hold the same probability only if pk reaches that bound
+    auto pbound = [&](uint32_t q) -> float {
+        return __fmul_rn(exact_expf(-(float)q / kBScale, f.exptab), f.inv);
+    };
+    const float pv = __uint_as_float(~pk);
+    const bool look_down = qp > 0u && pv >= pbound(qp);
+    const bool look_up = qp + 1u < (uint32_t)kNB && pv <= pbound(qp + 1u);
+    for (uint32_t q = qp; look_down && g0 == f.hoff[q] && q > 0u;) {  // the group reaches the start of bucket q
+        --q;
+        if (f.hcnt[q] == 0u) continue;
+        ensure_sorted(q);
+        if ((uint32_t)(f.scratch[bend(q) - 1u] >> 32) != pk) break;
+        while (g0 > f.hoff[q] && (uint32_t)(f.scratch[g0 - 1u] >> 32) == pk) --g0;
+        wide = true;
+    }
+    for (uint32_t q = qp; look_up && g1 == bend(q) && q + 1u < (uint32_t)kNB;) {  // ... or the end of bucket q
+        ++q;
+        if (f.hcnt[q] == 0u) continue;
+        ensure_sorted(q);
+        if ((uint32_t)(f.scratch[f.hoff[q]] >> 32) != pk) break;
+        while (g1 < bend(q) && (uint32_t)(f.scratch[g1] >> 32) == pk) ++g1;
+        wide = true;
+    }
+    if (wide) {
+        bitonic_sort_u64(f.scratch + g0, g1 - g0);  // equal high words: index order
+        __threadfence_block();
+        csync();
+    }
     f.chosen = f.scratch[f.pos];
     csync();
 }

@@ -174,3 +174,96 @@ def test_nan_row_raises_panic_error_single_row():
     with pytest.raises(lrs.SamplerPanic):
         s.sample(x, lrs.SamplingParams(), [])
     assert s.state == 3  # untouched
+
+
+def test_headline_full_size():
+    """Every row of the metric's configuration (1024 x 151,936), bit for bit."""
+    w = W.headline()
+    assert _check_workload(w, "headline full") == 1024
+
+
+def test_nucleus_stress_full_rows_subset_of_every_kind():
+    """Config 4 at its full width and window; a quarter of the 4096 rows (both kinds)."""
+    w = W.nucleus(row_ids=range(0, 4096, 4))
+    assert _check_workload(w, "nucleus 1024 rows") == 1024
+
+
+def test_candidate_bound_edges():
+    """Rows that stress the pass-1 candidate lists: the running max grows in every tile,
+    the max sits in the last element, every element is a candidate (temperature 1e3),
+    almost none is (temperature 0.02), and elements placed at the 18.1 bound."""
+    n, rows = 151_936, 10
+    rng = np.random.default_rng(21)
+    i = np.arange(n, dtype=np.float64)
+    x = np.empty((rows, n), np.float32)
+    x[0] = i * 1e-4                                        # slow ramp: everything within 18.1
+    x[1] = i * 4e-4                                        # steep ramp: early tiles far below the final max
+    x[2] = rng.standard_normal(n); x[2, n - 1] = 30.0      # spike in the last element
+    x[3] = rng.standard_normal(n) * 3                      # temperature 1e3 below
+    x[4] = rng.standard_normal(n) * 3                      # temperature 0.02 below
+    x[5] = -18.1 + rng.uniform(-0.02, 0.02, n); x[5, 0] = 0.0   # at the bound, max first
+    x[6] = -18.1 + rng.uniform(-0.02, 0.02, n); x[6, n - 1] = 0.0  # at the bound, max last
+    x[7] = -18.8 + rng.uniform(-0.02, 0.02, n); x[7, 1000] = 0.0
+    x[8] = np.where(rng.random(n) < 0.02, rng.standard_normal(n), -40.0)  # sparse live elements
+    x[9] = np.where((i // 1024) % 2 == 0, rng.standard_normal(n), -30.0)  # dense and empty tiles alternate
+    p = O.make_params(rows=rows)
+    p["temperature"] = [1.0, 1.0, 1.0, 1e3, 0.02, 1.0, 1.0, 1.0, 1.0, 1.3]
+    p["top_k"] = [0, 0, 40, 0, 100, 0, 0, 20, 0, 0]
+    p["top_p"] = [0.9, 1.0, 0.95, 0.999, 1.0, 1.0, 0.9, 1.0, 0.95, 0.97]
+    p["repetition_penalty"] = [1.0, 1.1, 1.0, 1.2, 1.0, 1.0, 1.3, 1.0, 1.1, 1.0]
+    p["repeat_last_n"] = 64
+    hist = rng.integers(0, n, (rows, 64)).astype(np.uint32)
+    hl = np.full(rows, 64, np.uint32)
+    st = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+    gpu = run_device(x, n, hist, hl, p, st)
+    ref = run_oracle(x, n, hist, hl, p, st)
+    compare(gpu, ref, "candidate bound")
+
+
+def test_rows_longer_than_two_to_the_21():
+    """n > 2^21 takes the wider candidate bound (18.8) and the global tile records."""
+    n, rows = (1 << 21) + 4099, 3
+    rng = np.random.default_rng(22)
+    x = (rng.standard_normal((rows, n)) * 2).astype(np.float32)
+    x[1] = (rng.standard_normal(n) * 0.3).astype(np.float32)  # flat: nucleus of ~ the whole row
+    p = O.make_params(rows=rows)
+    p["temperature"] = [1.0, 1.0, 0.7]
+    p["top_k"] = [0, 0, 40]
+    p["top_p"] = [0.9, 0.95, 0.9]
+    hist = rng.integers(0, n, (rows, 64)).astype(np.uint32)
+    hl = np.full(rows, 64, np.uint32)
+    st = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+    gpu = run_device(x, n, hist, hl, p, st)
+    ref = run_oracle(x, n, hist, hl, p, st)
+    compare(gpu, ref, "long rows")
+
+
+def test_equal_probabilities_across_bucket_boundaries():
+    """Elements whose d lies a few ulp either side of -1/32 share one probability; the
+    draw must pick among them in index order (p desc, index asc), whatever side of the
+    boundary each lies on."""
+    n, rows = 4096, 96
+    rng = np.random.default_rng(23)
+    x = np.full((rows, n), -40.0, np.float32)
+    base = np.float32(-0.03125)
+    for r in range(rows):
+        x[r, rng.integers(0, n)] = 0.0 if r % 3 else 0.5  # the max (and d = x - max)
+        m = float(x[r].max())
+        ids = rng.choice(n, 48, replace=False)
+        for j, i in enumerate(ids):
+            if x[r, i] != m:
+                v = np.float32(m) + base
+                steps = int(rng.integers(-24, 25))
+                for _ in range(abs(steps)):
+                    v = np.nextafter(v, np.float32(np.inf if steps > 0 else -np.inf), dtype=np.float32)
+                x[r, i] = v
+    p = O.make_params(rows=rows)
+    p["temperature"] = 1.0
+    p["top_k"] = 0
+    p["top_p"] = np.where(np.arange(rows) % 2 == 0, 1.0, 0.5)
+    p["repetition_penalty"] = 1.0
+    st = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+    empty = np.zeros((rows, 0), np.uint32)
+    gpu = run_device(x, n, empty, np.zeros(rows, np.uint32), p, st)
+    ref = run_oracle(x, n, None, None, p, st)
+    compare(gpu, ref, "bucket-boundary ties")
