@@ -58,6 +58,7 @@ constexpr int kNB = 580;             // path N buckets of width 1/32 in (max - x
                                      // everything below the candidate lists' range (d < -579/32)
 constexpr float kBScale = 32.0f;
 constexpr int kSortCap = 4096;       // largest bucket sorted in shared memory
+constexpr uint32_t kGatherItemsOff = 1024;  // path-N gather: per-warp item lists, in 32-bit words after the cursors
 constexpr float kTopPMargin = 0.002f;
 constexpr int kSerial = 512;         // elements summed one by one at the start of a scan
 constexpr int kTilesSmem = 256;      // tile records kept in shared memory (larger rows: global)
@@ -171,6 +172,14 @@ __device__ __forceinline__ uint32_t row_passes(const lrs_params& P, uint32_t n) 
     return (stochastic && n >= 2) ? 2u : 1u;
 }
 
+// Rows whose finish orders a large candidate set (top_k off or above kKMax, the
+// path-N finish) take the longest; they are claimed first so that no CTA starts one
+// near the end of the launch.
+__device__ __forceinline__ bool row_long(const lrs_params& P, uint32_t n) {
+    const uint32_t k = (P.top_k == 0 || P.top_k > n) ? n : P.top_k;
+    return row_passes(P, n) == 2u && !(k < n && k <= (uint32_t)kKMax);
+}
+
 // Bounded wait on an mbarrier phase.  On timeout the CTA's abort flag and the sticky
 // error word are set; every later wait then returns false at once, so all warps run
 // their (bounded) loops to the end and leave.
@@ -205,7 +214,20 @@ __device__ __forceinline__ bool wait_full(RowShared& sh, uint32_t q, int32_t* er
 // consumers have finished the row's pass 1, the dense tiles again for pass 2.
 __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float* ring) {
     const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
-    uint32_t q = 0, rqi = 0, p1target = 0;
+    uint32_t q = 0, rqi = 0, p1target = 0, sweep = 0;
+    // next row: the first sweep over the rows claims the long ones, the second the rest
+    // (each sweep has its own counter, so every row is claimed exactly once)
+    auto claim = [&]() -> uint32_t {
+        for (;;) {
+            const uint32_t r = atomicAdd(a.row_counter + sweep, 1u);
+            if (r >= a.rows) {
+                if (sweep == 1u) return a.rows;
+                sweep = 1u;
+                continue;
+            }
+            if (row_long(a.params[r], a.n) == (sweep == 0u)) return r;
+        }
+    };
     auto issue = [&](const Geo& g, uint32_t c, uint64_t pol) -> bool {
         const uint32_t s = q % kSlots, use = q / kSlots;
         if (use > 0 && !wait_bar(sh, &sh.empty[s], (use - 1) & 1u, a.err_flag)) return false;
@@ -218,7 +240,7 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
     for (;;) {
         const uint32_t qs = rqi % kRowQ, use = rqi / kRowQ;
         if (use > 0 && !wait_bar(sh, &sh.rq_empty[qs], (use - 1) & 1u, a.err_flag)) break;
-        const uint32_t r = sh.abort ? a.rows : atomicAdd(a.row_counter, 1u);
+        const uint32_t r = sh.abort ? a.rows : claim();
         sh.rq_row[qs] = r < a.rows ? r : a.rows;
         mbar_arrive(&sh.rq_full[qs]);
         ++rqi;
@@ -1009,6 +1031,7 @@ struct FinishCtx {
     Geo g;
     const TileRec* tt;              // tile records
     const uint2* lists;             // candidate lists of the sparse tiles: (scaled logit, index)
+    const float* lmax;              // per tile t and lane: lmax[64 t + lane], the max of the run's scaled logits
     unsigned long long* scratch;    // path N: gathered (p, index) keys
     const uint32_t* bitmap;         // window bitmap
     uint32_t* hcnt;                 // path N: bucket counts and offsets
@@ -1080,12 +1103,30 @@ __device__ __noinline__ void finish_path_k(RowShared& sh, FinishCtx& f) {
 
 // Path N: gather bucket by bucket, sort lazily, scan with the exact emulation.
 __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
+    // The read-only context in registers: loads through `f` go to local memory (the
+    // context lives in the kernel's stack frame), which the shared-memory carve-out
+    // leaves little L1 for.
+    const Geo g = f.g;
+    const TileRec* const tt = f.tt;
+    const uint2* const lists = f.lists;
+    const float* const lmax = f.lmax;
+    unsigned long long* const scratch = f.scratch;
+    const uint32_t* const bitmap = f.bitmap;
+    uint32_t* const hcnt = f.hcnt;
+    uint32_t* const hoff = f.hoff;
+    uint32_t* const cursor = f.cursor;
+    unsigned long long* const sbuf = f.sbuf;
+    const ExpTable exptab = f.exptab;
+    const uint32_t k = f.k;
+    const float mx = f.mx, inv_t = f.inv_t, inv = f.inv, S = f.S, penalty = f.penalty, top_p = f.top_p;
+    const float hist_lim = f.hist_lim;
+    const bool pen_on = f.pen_on, topp_on = f.topp_on;
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
     const float kInf = __int_as_float(0x7F800000);
     auto penal_g = [&](float x, uint32_t gi) -> float {  // sampler.rs:96-100
-        if (f.pen_on && ((__ldcg(f.bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, f.penalty);
+        if (pen_on && ((__ldcg(bitmap + (gi >> 5)) >> (gi & 31)) & 1u)) return penalise(x, penalty);
         return x;
     };
     if (warp == 0) {
@@ -1099,9 +1140,9 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         // margin) S.  Past the first bucket whose probabilities are all below 2^-26 the
         // scan ends (once the top-p sum is at least 1/2 nothing after it changes the
         // sum).  One warp, 32 buckets a step.
-        const double target = f.topp_on ? ((double)f.top_p + kTopPMargin) * (double)f.S : 1e300;
-        const double tail_target = f.topp_on ? (1.0 - (double)f.top_p - kTopPMargin) * (double)f.S : -1.0;
-        const double exit_e = 1.4901161193847656e-08 * (double)f.S;
+        const double target = topp_on ? ((double)top_p + kTopPMargin) * (double)S : 1e300;
+        const double tail_target = topp_on ? (1.0 - (double)top_p - kTopPMargin) * (double)S : -1.0;
+        const double exit_e = 1.4901161193847656e-08 * (double)S;
         const double elane = exp(-(double)(lane + 1) / (double)kBScale) * (1.0 - 1e-12);  // (low: a lower bound)
         const double ewidth = exp(1.0 / (double)kBScale) * (1.0 + 1e-9);  // upper / lower bound of a bucket
         const double estep = __shfl_sync(0xFFFFFFFFu, elane, 31);        // exp(-32/kBScale)
@@ -1112,7 +1153,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             double e32 = 1.0;
             for (uint32_t base = 0; base < (uint32_t)kNB - 1; base += 32) {
                 const uint32_t b = base + (uint32_t)lane;
-                const uint32_t c = b < (uint32_t)kNB - 1 ? f.hcnt[b] : 0u;
+                const uint32_t c = b < (uint32_t)kNB - 1 ? hcnt[b] : 0u;
                 utot += (double)c * e32 * elane * ewidth;
                 ctot += c;
                 e32 *= estep;
@@ -1122,7 +1163,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 utot += __shfl_xor_sync(0xFFFFFFFFu, utot, o);
                 ctot += __shfl_xor_sync(0xFFFFFFFFu, ctot, o);
             }
-            utot += (double)(f.g.n - ctot) * 1.5229979744712629e-08;  // exp(-18)
+            utot += (double)(g.n - ctot) * 1.5229979744712629e-08;  // exp(-18)
         }
         double e32 = 1.0;  // exp(-32 k / kBScale) at the start of each 32-bucket step
         uint32_t cc = 0, acc = 0, found = (uint32_t)kNB - 1;
@@ -1130,7 +1171,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         for (uint32_t base = 0; base < (uint32_t)kNB - 1; base += 32) {
             const uint32_t b = base + (uint32_t)lane;
             const bool in = b < (uint32_t)kNB - 1;
-            const uint32_t c = in ? f.hcnt[b] : 0u;
+            const uint32_t c = in ? hcnt[b] : 0u;
             const double eb = e32 * elane;
             // inclusive prefixes of counts and masses over the lanes
             uint32_t ci = c;
@@ -1144,9 +1185,9 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                     mi += tm;
                 }
             }
-            if (in) f.hoff[b] = acc + ci - c;
+            if (in) hoff[b] = acc + ci - c;
             const bool tail_ok = tail_target > 0.0 && utot - (umass + mi * ewidth) <= tail_target;
-            const bool stop = in && (cc + ci >= f.k || mass + mi >= target || tail_ok || eb < exit_e);
+            const bool stop = in && (cc + ci >= k || mass + mi >= target || tail_ok || eb < exit_e);
             const unsigned m = __ballot_sync(0xFFFFFFFFu, stop);
             if (m && found == (uint32_t)kNB - 1) found = base + (uint32_t)(__ffs(m) - 1);
             cc += __shfl_sync(0xFFFFFFFFu, ci, 31);
@@ -1156,8 +1197,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             e32 *= estep;
         }
         if (lane == 0) {
-            f.hoff[kNB - 1] = acc;
-            f.hcnt[kNB - 1] = f.g.n - acc;  // everything below the histogram range
+            hoff[kNB - 1] = acc;
+            hcnt[kNB - 1] = g.n - acc;  // everything below the histogram range
             sh.misc[3] = found;
         }
     }
@@ -1168,89 +1209,145 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     auto gather = [&](uint32_t blo, uint32_t bhi) {
         const bool all = bhi == (uint32_t)kNB - 1;
         const float dlim = -(float)(bhi + 1) / kBScale;
-        for (uint32_t q = blo + tid; q <= bhi; q += kThreads) f.cursor[q] = 0;
+        for (uint32_t q = blo + tid; q <= bhi; q += kThreads) cursor[q] = 0;
         csync();
         // d: the element's d = fl(fl(x * inv_t) - max) (ops.rs:409)
-        auto take = [&](uint32_t i, float dd, bool valid) {
+        auto take = [=](uint32_t i, float dd, bool valid) {
             bool tk = false;
             int b = 0;
             if (valid && (dd >= dlim || all)) {
-                b = dd >= f.hist_lim ? (int)fminf(-dd * kBScale, (float)(kNB - 1)) : kNB - 1;
+                b = dd >= hist_lim ? (int)fminf(-dd * kBScale, (float)(kNB - 1)) : kNB - 1;
                 tk = (uint32_t)b >= blo && (uint32_t)b <= bhi;
             }
             const unsigned act = __ballot_sync(0xFFFFFFFFu, tk);
             if (tk) {
                 // CUDA's expf (within 2 ulp): keys are exactified before a bucket is ordered
                 const float e = dd == 0.0f ? 1.0f : expf(dd);
-                const float pr = __fmul_rn(e, f.inv);
+                const float pr = __fmul_rn(e, inv);
                 const unsigned peers = __match_any_sync(act, b);
                 const int leader = __ffs(peers) - 1;
                 uint32_t base = 0;
-                if (lane == leader) base = atomicAdd(&f.cursor[b], (uint32_t)__popc(peers));
+                if (lane == leader) base = atomicAdd(&cursor[b], (uint32_t)__popc(peers));
                 base = __shfl_sync(peers, base, leader);
-                const uint32_t slot = f.hoff[b] + base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
-                f.scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i | (dd == 0.0f ? 0u : kApxKey);
+                const uint32_t slot = hoff[b] + base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
+                scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i | (dd == 0.0f ? 0u : kApxKey);
             }
         };
         if (warp == 0) {
-            const uint32_t edges = f.g.head + f.g.tail;
+            const uint32_t edges = g.head + g.tail;
             const bool mine = (uint32_t)lane < edges;
             const uint32_t gi =
-                (uint32_t)lane < f.g.head ? (uint32_t)lane : f.g.head + f.g.body + ((uint32_t)lane - f.g.head);
-            take(gi, mine ? d_of(penal_g(f.g.row[gi], gi), f.inv_t, f.mx) : 0.0f, mine);
+                (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+            take(gi, mine ? d_of(penal_g(g.row[gi], gi), inv_t, mx) : 0.0f, mine);
         }
-        for (uint32_t t = (uint32_t)warp; t < f.g.nchunks; t += kWarps) {  // one tile per warp
-            const TileRec& R = f.tt[t];
-            if (!all && __fsub_rn(R.mt, f.mx) < dlim) continue;
-            if (!all && R.lcnt != kDenseMark) {
-                // sparse tile: its list holds every element with d >= hist_lim
-                const uint2* ent = f.lists + R.loff;
-                for (uint32_t i0 = 0; i0 < R.lcnt; i0 += 32) {
-                    const uint32_t i = i0 + (uint32_t)lane;
-                    uint2 e = make_uint2(0u, 0u);
-                    if (i < R.lcnt) e = __ldcg(ent + i);
-                    take(e.y, __fsub_rn(__uint_as_float(e.x), f.mx), i < R.lcnt);
+        // The warp's tiles t = warp + kWarps j, 32 at a time (j in lane bits).  Work items
+        // of 32 elements, one per lane: a run of a dense tile whose pass-1 run max
+        // reaches the range, or 32 list entries of a sparse tile.  The items are listed
+        // in shared memory (after the bucket cursors), then read eight at a time with
+        // their loads in flight together, across tiles.
+        uint32_t* items = reinterpret_cast<uint32_t*>(sbuf) + kGatherItemsOff + (uint32_t)warp * 1024u;
+        const uint32_t ntw = g.nchunks > (uint32_t)warp ? (g.nchunks - (uint32_t)warp + kWarps - 1) / kWarps : 0u;
+        for (uint32_t j0 = 0; j0 < ntw; j0 += 32) {
+            const uint32_t nj = min(32u, ntw - j0);
+            uint32_t live = 0;  // lane bit j: the lane's run of tile j is an item (dense tiles)
+            for (uint32_t j = 0; j < nj; j += 8) {
+                float lm[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) {
+                    const uint32_t t = (uint32_t)warp + kWarps * (j0 + j + (uint32_t)u);
+                    lm[u] = -kInf;
+                    if (j + (uint32_t)u < nj && (uint32_t)lane * 32u < chunk_count(g, t)) {
+                        const TileRec& R = tt[t];
+                        if (all)
+                            lm[u] = kInf;
+                        else if (R.lcnt == kDenseMark && !(__fsub_rn(R.mt, mx) < dlim))
+                            lm[u] = __ldcg(lmax + t * 64u + (uint32_t)lane);
+                    }
                 }
-                continue;
+#pragma unroll
+                for (int u = 0; u < 8; ++u)
+                    if (lm[u] == kInf || __fsub_rn(lm[u], mx) >= dlim) live |= 1u << (j + (uint32_t)u);
             }
-            const uint32_t cnt = chunk_count(f.g, t), tb = f.g.head + t * kTile;
-            constexpr int kU = 8;  // independent loads in flight per lane
-            for (uint32_t i0 = 0; i0 < cnt; i0 += kU * 32) {
-                float xs[kU];
-                uint32_t pw[kU];  // window-bitmap word of each element
+            // item = j << 6 | group << 1 | list
+            uint32_t nit = 0;
+            for (uint32_t j = 0; j < nj; ++j) {
+                const uint32_t t = (uint32_t)warp + kWarps * (j0 + j);
+                const TileRec& R = tt[t];
+                if (!all && R.lcnt != kDenseMark) {
+                    const uint32_t ng = __fsub_rn(R.mt, mx) < dlim ? 0u : (R.lcnt + 31u) / 32u;
+                    if ((uint32_t)lane < ng) items[nit + (uint32_t)lane] = (j << 6) | ((uint32_t)lane << 1) | 1u;
+                    nit += ng;
+                } else {
+                    const bool mine = (live >> j) & 1u;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, mine);
+                    if (mine) items[nit + (uint32_t)__popc(m & ((1u << lane) - 1u))] = (j << 6) | ((uint32_t)lane << 1);
+                    nit += (uint32_t)__popc(m);
+                }
+            }
+            __syncwarp();
+            for (uint32_t k0 = 0; k0 < nit; k0 += 8) {
+                float xs[8];
+                uint32_t gi[8], pw[8];  // gi: element index (~0u: none)
 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
-                    xs[u] = i < cnt ? f.g.row[tb + i] : 0.0f;
-                    pw[u] = (f.pen_on && i < cnt) ? __ldcg(f.bitmap + ((tb + i) >> 5)) : 0u;
+                for (int u = 0; u < 8; ++u) {
+                    xs[u] = 0.0f;
+                    gi[u] = ~0u;
+                    pw[u] = 0u;
+                    if (k0 + (uint32_t)u >= nit) continue;
+                    const uint32_t itm = items[k0 + (uint32_t)u];
+                    const uint32_t t = (uint32_t)warp + kWarps * (j0 + (itm >> 6));
+                    const uint32_t e = ((itm >> 1) & 31u) * 32u + (uint32_t)lane;
+                    if (itm & 1u) {
+                        // sparse tile: its list holds every element with d >= hist_lim
+                        const TileRec& R = tt[t];
+                        if (e < R.lcnt) {
+                            const uint2 en = __ldcg(lists + R.loff + e);
+                            xs[u] = __uint_as_float(en.x);  // (scaled, penalised)
+                            gi[u] = en.y;
+                        }
+                    } else if (e < chunk_count(g, t)) {
+                        gi[u] = g.head + t * kTile + e;
+                        xs[u] = g.row[gi[u]];
+                        if (pen_on) pw[u] = __ldcg(bitmap + (gi[u] >> 5));
+                    }
                 }
 #pragma unroll
-                for (int u = 0; u < kU; ++u) {
-                    const uint32_t i = i0 + (uint32_t)(u * 32 + lane);
-                    const float xv = ((pw[u] >> ((tb + i) & 31)) & 1u) ? penalise(xs[u], f.penalty) : xs[u];
-                    const float dd = i < cnt ? d_of(xv, f.inv_t, f.mx) : -kInf;
+                for (int u = 0; u < 8; ++u) {
+                    if (k0 + (uint32_t)u >= nit) break;  // (warp-uniform)
+                    const bool ok = gi[u] != ~0u;
+                    float dd = -kInf;
+                    if (ok) {
+                        const uint32_t itm = items[k0 + (uint32_t)u];
+                        if (itm & 1u) {
+                            dd = __fsub_rn(xs[u], mx);
+                        } else {
+                            const bool pen = (pw[u] >> (gi[u] & 31u)) & 1u;
+                            dd = d_of(pen ? penalise(xs[u], penalty) : xs[u], inv_t, mx);
+                        }
+                    }
                     if (!all && !__any_sync(0xFFFFFFFFu, dd >= dlim)) continue;
-                    take(tb + i, dd, i < cnt);
+                    take(gi[u], dd, ok);
                 }
             }
+            __syncwarp();
         }
         __threadfence_block();
         csync();
     };
     gather(0, blim);
     uint32_t gathered_to = blim;
-    f.n_cand = f.hoff[blim] + f.hcnt[blim];
+    f.n_cand = hoff[blim] + hcnt[blim];
     for (int q = tid; q < (kNB + 31) / 32; q += kThreads) sh.bsorted[q] = 0u;
     csync();
     auto bucket_of = [&](uint32_t pos) -> uint32_t {  // bucket holding sorted position pos
         uint32_t lo = 0, hi = (uint32_t)kNB - 1;
         while (lo < hi) {
             const uint32_t mid = (lo + hi + 1) >> 1;
-            if (f.hoff[mid] <= pos) lo = mid; else hi = mid - 1;
+            if (hoff[mid] <= pos) lo = mid; else hi = mid - 1;
         }
         return lo;
     };
-    auto bend = [&](uint32_t q) -> uint32_t { return f.hoff[q] + f.hcnt[q]; };
+    auto bend = [&](uint32_t q) -> uint32_t { return hoff[q] + hcnt[q]; };
     auto ensure_gathered = [&](uint32_t q) {
         while (q > gathered_to) {
             const uint32_t hi = min((uint32_t)kNB - 1, gathered_to + 1 + 2 * (gathered_to + 1));
@@ -1260,8 +1357,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     };
     // exact key of element i: p = fl(libm expf(d) * inv) (sampler.rs:129-131, ops.rs:409-416)
     auto exact_key = [&](uint32_t i) -> unsigned long long {
-        const float d = d_of(penal_g(f.g.row[i], i), f.inv_t, f.mx);
-        const float pr = __fmul_rn(exact_expf(d, f.exptab), f.inv);
+        const float d = d_of(penal_g(g.row[i], i), inv_t, mx);
+        const float pr = __fmul_rn(exact_expf(d, exptab), inv);
         return ((unsigned long long)(~__float_as_uint(pr)) << 32) | i;
     };
     // Bucket q in exact (p desc, index asc) order: exact keys, then a bitonic sort.
@@ -1269,8 +1366,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         ensure_gathered(q);
         if ((sh.bsorted[q >> 5] >> (q & 31)) & 1u) return;
         const long long ts = clock64();
-        const uint32_t cnt = f.hcnt[q];
-        unsigned long long* base = f.scratch + f.hoff[q];
+        const uint32_t cnt = hcnt[q];
+        unsigned long long* base = scratch + hoff[q];
         for (uint32_t i = tid; i < cnt; i += kThreads) {
             const unsigned long long kk = base[i];
             if ((uint32_t)kk & kApxKey) base[i] = exact_key((uint32_t)kk & ~kApxKey);
@@ -1279,10 +1376,10 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         csync();
         if (cnt > 1) {
             if (cnt <= (uint32_t)kSortCap) {
-                for (uint32_t i = tid; i < cnt; i += kThreads) f.sbuf[i] = base[i];
+                for (uint32_t i = tid; i < cnt; i += kThreads) sbuf[i] = base[i];
                 csync();
-                bitonic_sort_u64(f.sbuf, cnt);
-                for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
+                bitonic_sort_u64(sbuf, cnt);
+                for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = sbuf[i];
             } else {
                 bitonic_sort_u64(base, cnt);  // rare: one bucket larger than shared memory
             }
@@ -1299,21 +1396,21 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     auto sort_range = [&](uint32_t qa, uint32_t qb) {
         ensure_gathered(qb);
         const long long ts = clock64();
-        const uint32_t lo = f.hoff[qa], cnt = bend(qb) - lo;
-        unsigned long long* base = f.scratch + lo;
+        const uint32_t lo = hoff[qa], cnt = bend(qb) - lo;
+        unsigned long long* base = scratch + lo;
         for (uint32_t i = tid; i < cnt; i += kThreads) {
             const unsigned long long kk = base[i];
-            f.sbuf[i] = ((uint32_t)kk & kApxKey) ? exact_key((uint32_t)kk & ~kApxKey) : kk;
+            sbuf[i] = ((uint32_t)kk & kApxKey) ? exact_key((uint32_t)kk & ~kApxKey) : kk;
         }
         csync();
-        bitonic_sort_u64(f.sbuf, cnt);
-        for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = f.sbuf[i];
+        bitonic_sort_u64(sbuf, cnt);
+        for (uint32_t i = tid; i < cnt; i += kThreads) base[i] = sbuf[i];
         __threadfence_block();
         for (uint32_t q = qa + tid; q <= qb; q += kThreads) atomicOr(&sh.bsorted[q >> 5], 1u << (q & 31));
         csync();
         f.acc_sort += clock64() - ts;
     };
-    auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(f.scratch[q] >> 32)); };
+    auto pval = [&](uint32_t q) -> float { return __uint_as_float(~(uint32_t)(scratch[q] >> 32)); };
     // Exact sequential run over sorted positions [0, p1) of the candidate sequence
     // (sampler.rs:137-139 / 148-151 / 156-158).  Buckets are in order; inside a bucket
     // the order matters only around an ordered step (a binade crossing, a tie, a big
@@ -1336,7 +1433,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 // their probabilities are all below half the sum's grid unit no
                 // later addition changes the sum (and none is a tie).
                 const float emax = expf(-(float)b / kBScale) * 1.0001f;
-                const float pmax = __fmul_rn(emax, f.inv) * 1.0001f;
+                const float pmax = __fmul_rn(emax, inv) * 1.0001f;
                 const int uu = unit_exp(s);
                 if (uu > -149 && pmax < ldexpf(1.0f, uu - 1)) return -1;
             }
@@ -1347,7 +1444,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                     // every bucket the serial positions reach, in one sort when they fit
                     // (gathered buckets only: the run may stop before it needs more)
                     uint32_t qs = min(bucket_of(min(p1, p + serial_left) - 1u), gathered_to);
-                    while (qs > b && bend(qs) - f.hoff[b] > (uint32_t)kSortCap) --qs;
+                    while (qs > b && bend(qs) - hoff[b] > (uint32_t)kSortCap) --qs;
                     if (qs > b)
                         sort_range(b, qs);
                     else
@@ -1395,7 +1492,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             }
             const uint32_t tc = e - p;
             float v[kVpt];
-            load_sorted_tile(f.scratch + p, tc, v);
+            load_sorted_tile(scratch + p, tc, v);
             // increments on the running value's grid, exact where an approximate key's
             // error bound could change them
             const int uu = unit_exp(s);
@@ -1407,13 +1504,13 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 inc[i] = 0;
                 const int li = li_of(i);
                 if ((uint32_t)li < tc) {
-                    const unsigned long long kk = f.scratch[p + li];
+                    const unsigned long long kk = scratch[p + li];
                     uint32_t vb = __float_as_uint(v[i]);
                     if ((uint32_t)kk & kApxKey) {
                         const Cls lo = classify(vb > 8u ? vb - 8u : 0u, uu), hi = classify(vb + 8u, uu);
                         if (!(lo.inc == hi.inc && !lo.tie && !hi.tie && !lo.big && !hi.big) && !(lo.big && hi.big)) {
                             const unsigned long long ek = exact_key((uint32_t)kk & ~kApxKey);
-                            f.scratch[p + li] = ek;
+                            scratch[p + li] = ek;
                             v[i] = __uint_as_float(~(uint32_t)(ek >> 32));
                             vb = __float_as_uint(v[i]);
                         }
@@ -1452,7 +1549,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             uint32_t first = block_reduce_u32(cand, MinU(), sh.red2);
             if (first >= tc) first = 0;  // (cannot happen: then order the chunk's first bucket)
             const uint32_t qe = bucket_of(p + first);
-            const uint32_t bstart = max(p, f.hoff[qe]);
+            const uint32_t bstart = max(p, hoff[qe]);
             // the buckets before qe in this chunk: summed in any order on this grid
             if (bstart > p) {
 #pragma unroll 1
@@ -1470,7 +1567,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 const uint32_t tq2 = min((uint32_t)kChunk, qend - q0);
                 float w[kVpt];
                 uint32_t ex = 0xFFFFFFFFu;
-                load_sorted_tile(f.scratch + q0, tq2, w);
+                load_sorted_tile(scratch + q0, tq2, w);
                 const int stp = tile2(w, ex, 0, (int)tq2, dir, s, thr, NoExact(), sh);
                 if (stp >= 0) return (int)q0 + stp;
                 q0 += tq2;
@@ -1481,8 +1578,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     };
     // top-p scan capped at k survivors (sampler.rs:122-146)
     float cum = 0.0f;
-    int stp = run(f.k, +1, cum, f.topp_on ? f.top_p : kInf);
-    f.cutoff = stp >= 0 ? (uint32_t)stp + 1 : f.k;
+    int stp = run(k, +1, cum, topp_on ? top_p : kInf);
+    f.cutoff = stp >= 0 ? (uint32_t)stp + 1 : k;
     f.sum = cum;
     // draw (sampler.rs:152-162)
     if (f.sum > 0.0f) {
@@ -1499,42 +1596,42 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     // each side in index order: such a group is put in index order across the boundary.
     uint32_t qp = bucket_of(f.pos);
     ensure_sorted(qp);
-    const uint32_t pk = (uint32_t)(f.scratch[f.pos] >> 32);
-    uint32_t g0 = f.hoff[qp], g1 = bend(qp);
-    while (g0 < f.pos && (uint32_t)(f.scratch[g0] >> 32) != pk) ++g0;   // (sorted: a short scan of
-    while (g1 > f.pos + 1u && (uint32_t)(f.scratch[g1 - 1u] >> 32) != pk) --g1;  // equal keys is rare)
+    const uint32_t pk = (uint32_t)(scratch[f.pos] >> 32);
+    uint32_t g0 = hoff[qp], g1 = bend(qp);
+    while (g0 < f.pos && (uint32_t)(scratch[g0] >> 32) != pk) ++g0;   // (sorted: a short scan of
+    while (g1 > f.pos + 1u && (uint32_t)(scratch[g1 - 1u] >> 32) != pk) --g1;  // equal keys is rare)
     bool wide = false;
     // bucket q holds d in (-(q+1)/kBScale, -q/kBScale], so its probabilities lie in
     // [P(-(q+1)/kBScale), P(-q/kBScale)] with P(d) = fl(expf(d) inv) monotone: a
     // neighbour can hold the same probability only if pk reaches that bound
     auto pbound = [&](uint32_t q) -> float {
-        return __fmul_rn(exact_expf(-(float)q / kBScale, f.exptab), f.inv);
+        return __fmul_rn(exact_expf(-(float)q / kBScale, exptab), inv);
     };
     const float pv = __uint_as_float(~pk);
     const bool look_down = qp > 0u && pv >= pbound(qp);
     const bool look_up = qp + 1u < (uint32_t)kNB && pv <= pbound(qp + 1u);
-    for (uint32_t q = qp; look_down && g0 == f.hoff[q] && q > 0u;) {  // the group reaches the start of bucket q
+    for (uint32_t q = qp; look_down && g0 == hoff[q] && q > 0u;) {  // the group reaches the start of bucket q
         --q;
-        if (f.hcnt[q] == 0u) continue;
+        if (hcnt[q] == 0u) continue;
         ensure_sorted(q);
-        if ((uint32_t)(f.scratch[bend(q) - 1u] >> 32) != pk) break;
-        while (g0 > f.hoff[q] && (uint32_t)(f.scratch[g0 - 1u] >> 32) == pk) --g0;
+        if ((uint32_t)(scratch[bend(q) - 1u] >> 32) != pk) break;
+        while (g0 > hoff[q] && (uint32_t)(scratch[g0 - 1u] >> 32) == pk) --g0;
         wide = true;
     }
     for (uint32_t q = qp; look_up && g1 == bend(q) && q + 1u < (uint32_t)kNB;) {  // ... or the end of bucket q
         ++q;
-        if (f.hcnt[q] == 0u) continue;
+        if (hcnt[q] == 0u) continue;
         ensure_sorted(q);
-        if ((uint32_t)(f.scratch[f.hoff[q]] >> 32) != pk) break;
-        while (g1 < bend(q) && (uint32_t)(f.scratch[g1] >> 32) == pk) ++g1;
+        if ((uint32_t)(scratch[hoff[q]] >> 32) != pk) break;
+        while (g1 < bend(q) && (uint32_t)(scratch[g1] >> 32) == pk) ++g1;
         wide = true;
     }
     if (wide) {
-        bitonic_sort_u64(f.scratch + g0, g1 - g0);  // equal high words: index order
+        bitonic_sort_u64(scratch + g0, g1 - g0);  // equal high words: index order
         __threadfence_block();
         csync();
     }
-    f.chosen = f.scratch[f.pos];
+    f.chosen = scratch[f.pos];
     csync();
 }
 
@@ -1559,7 +1656,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
     unsigned long long* scratch = a.scratch + (uint64_t)blockIdx.x * a.scratch_stride;
     uint32_t* bitmap = reinterpret_cast<uint32_t*>(scratch + a.bitmap_off);
     TileRec* ttab_g = reinterpret_cast<TileRec*>(scratch + a.tiles_off);
-    float* lrec = reinterpret_cast<float*>(scratch + a.lanes_off);  // per tile: 32 lane sums (pass 1)
+    // per tile t (pass 1): lrec[64 t + lane] the lane's candidate exp sum, lrec[64 t + 32 + lane]
+    // the max of its run's scaled logits
+    float* lrec = reinterpret_cast<float*>(scratch + a.lanes_off);
     uint2* lists = reinterpret_cast<uint2*>(scratch + a.lists_off);  // per warp: sparse tiles' candidates
     const ExpTable exptab{a.exp_index, a.exp_entries};
     const float kInf = __int_as_float(0x7F800000);
@@ -1874,7 +1973,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const float cl = (ml == -kInf || mt != mt || sl == 0.0f)
                                      ? 0.0f
                                      : __fmul_rn(sl, ex2_approx(__fmul_rn(__fsub_rn(ml, mt), kLog2e)));
-                lrec[t * 32u + (uint32_t)lane] = cl;
+                lrec[t * 64u + (uint32_t)lane] = cl;
+                lrec[t * 64u + 32u + (uint32_t)lane] = ml;
                 const float tot = warp_sum_f(cl);
                 if (lane == 0) {
                     TileRec& R = tt[t];
@@ -2089,7 +2189,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 // loads of tile t's per-lane inputs, issued one tile ahead of their use
                 auto prefetch = [&](uint32_t t) {
                     bits_nx = tile_bits(t);
-                    lr_nx = __ldcg(lrec + t * 32u + (uint32_t)lane);
+                    lr_nx = __ldcg(lrec + t * 64u + (uint32_t)lane);
                     const uint32_t lc = tt[t].lcnt, e0 = (uint32_t)lane * kRunS;
                     const bool want = !bad && lc != kDenseMark && (tt[t].flags & (kSumLive | kHistLive));
                     const uint2* en = lists + tt[t].loff;
@@ -2376,6 +2476,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             fc.g = g;
             fc.tt = tt;
             fc.lists = lists;
+            fc.lmax = lrec + 32;
             fc.scratch = scratch;
             fc.bitmap = bitmap;
             fc.hcnt = hcnt;
@@ -2463,8 +2564,8 @@ void lrs_kernel_scratch_layout(uint32_t n, uint64_t* stride, uint64_t* bitmap_of
     const uint64_t wtiles = (tiles + lrs::kWarps - 1) / lrs::kWarps;  // tiles of one consumer warp
     *bitmap_off = n;                                     // [0, n): path-N candidate keys
     *tiles_off = *bitmap_off + (words + 1) / 2;          // tile records, 32 bytes each
-    *lanes_off = *tiles_off + 4 * tiles;                 // lane sums, 32 floats per tile
-    *lists_off = *lanes_off + 16 * tiles;                // candidate lists, 8 bytes an entry
+    *lanes_off = *tiles_off + 4 * tiles;                 // lane sums and lane maxima, 64 floats per tile
+    *lists_off = *lanes_off + 32 * tiles;                // candidate lists, 8 bytes an entry
     *stride = (*lists_off + (uint64_t)lrs::kWarps * wtiles * lrs::kDense + 31) & ~(uint64_t)31;
 }
 cudaError_t lrs_kernel_set_smem(size_t bytes) {

@@ -29,7 +29,7 @@ struct lrs_kernel_args_t {
     uint64_t tiles_off;                   // tile records of rows longer than the shared table
     uint64_t lanes_off;                   // per-tile lane sums
     uint64_t lists_off;                   // candidate lists of sparse tiles
-    uint32_t* row_counter;    // zeroed before each launch
+    uint32_t* row_counter;    // two row counters (long rows first, then the rest), zeroed before each launch
     int32_t* err_flag;        // sticky error word
 };
 

@@ -5,7 +5,7 @@
 // implicit device synchronisation) in the decode loop, or a plug-in host that forbids
 // device allocations after initialisation.  lrs_sample_device_noalloc serves them: it runs
 // the same sampling kernel as lrs_sample_device, but the kernel's working memory (the
-// per-CTA candidate scratch of the large-candidate path, the row counter, the error word
+// per-CTA candidate scratch of the large-candidate path, the row counters, the error word
 // and the libm-expf exception table) lives in file-scope __device__ arrays of fixed size,
 // held on each GPU where this library's device code is loaded until the process exits.
 //
@@ -39,7 +39,7 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned long long g_scratch[kScratchBytes / 8];
 static __device__ __align__(256) unsigned long long g_exp_index[lrs::kExpIndexWords];
 static __device__ __align__(256) uint2 g_exp_entries[kMaxTableEntries + 1];
-static __device__ __align__(256) uint32_t g_counter[2];  // [0] row counter, [1] error word
+static __device__ __align__(256) uint32_t g_counter[3];  // [0], [1] row counters, [2] error word
 
 struct DeviceSetup {
     bool done = false;
@@ -185,10 +185,10 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.lanes_off = lanes_off;
         args.lists_off = lists_off;
         args.row_counter = s.counter;
-        args.err_flag = reinterpret_cast<int32_t*>(s.counter + 1);
+        args.err_flag = reinterpret_cast<int32_t*>(s.counter + 2);
         cudaStream_t st = (cudaStream_t)stream;
-        // the row counter and the error word must start at zero on every call
-        if (cudaMemsetAsync(s.counter, 0, 2 * sizeof(uint32_t), st) != cudaSuccess)
+        // the row counters and the error word must start at zero on every call
+        if (cudaMemsetAsync(s.counter, 0, 3 * sizeof(uint32_t), st) != cudaSuccess)
             rc = LRS_E_CUDA;
         else if (lrs_kernel_launch(&args, grid, smem, st) != cudaSuccess)
             rc = LRS_E_CUDA;
