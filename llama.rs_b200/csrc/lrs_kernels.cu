@@ -92,13 +92,13 @@ using SampleArgs = lrs_kernel_args_t;
 // One tile of a row (32 bytes; shared memory, or per-CTA scratch for long rows).
 struct __align__(16) TileRec {
     float mt;        // pass 1: max of the tile's scaled logits
+    uint32_t tag;    // pass 1: the row id once mt is final (kNoTag before); (mt, tag) is one 64-bit word
     float pt;        // pass 1: sum of exp relative to mt; prep: estimate of the running sum at the tile
     uint32_t flags;  // prep: lowest grid exponent + 256 | kSumLive | kHistLive
     uint32_t next;   // prep: next sum-live tile (the baton's route)
     uint32_t loff;   // pass 1: first list entry (sparse tiles)
     uint32_t lcnt;   // pass 1: list entries, or kDenseMark
     uint32_t rank;   // prep: load number of a dense tile within pass 2
-    uint32_t tag;    // pass 1: the row id once the record is complete (kNoTag before)
 };
 
 // ---------------------------------------------------------------- shared state ----
@@ -861,7 +861,7 @@ __device__ __forceinline__ void apply_penalty(float (&v)[32], uint32_t bits, int
 // libm's value (exact_expf(d)) is computed by every such lane at once, before the
 // ordered additions, so one table latency is paid per call, not one per element.
 __device__ __noinline__ float warp_serial_add(float s, float e, float d, bool exact, int lo, int cnt,
-                                              const ExpTable& tab) {
+                                              const ExpTable tab) {
     const int lane = threadIdx.x & 31;
     if (!exact && lane >= lo && lane < lo + cnt) e = exact_expf(d, tab);
     for (int j = lo; j < lo + cnt; ++j) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e, j));
@@ -940,7 +940,7 @@ struct GridAcc {
     bool sp0, sp1;
 };
 __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, float h0, float h1, GridAcc& g,
-                                              const ExpTable& tab) {
+                                              const ExpTable tab) {
     bool ex = d == 0.0f;
     float e = ex ? 1.0f : expf(d);
     float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
@@ -978,6 +978,60 @@ __device__ __noinline__ WState topk_tile(const float* run, uint32_t hmask, uint3
                                         uint32_t gbase, float mrun, uint32_t k, float* wx, uint32_t* wi,
                                         uint32_t* wh, WState ws) {
     const int lane = threadIdx.x & 31;
+    // hits in a lane-rotated order: lane L starts at run offset L, so that the lanes'
+    // reads (run = lane * 32 + offset) fall in different shared-memory banks
+    hmask = __funnelshift_r(hmask, hmask, lane);
+    if (ws.wcnt == 0u && ws.theta == -__int_as_float(0x7F800000)) {
+        // First tile of the warp: every element is a hit.  The k-th largest of the
+        // lanes' four largest values (k <= 128 distinct elements of the tile at or
+        // above it) bounds the tile's k-th largest from below; less the tie margin it
+        // is the starting threshold, and the hits below it are dropped before any
+        // append.  The k-th largest: a radix select over order-preserving keys.
+        float top[4] = {-__int_as_float(0x7F800000), -__int_as_float(0x7F800000), -__int_as_float(0x7F800000),
+                        -__int_as_float(0x7F800000)};
+        for (uint32_t h = hmask; h; h &= h - 1u) {
+            const int pos = (__ffs(h) - 1 + lane) & 31;
+            float x = run[pos];
+            if ((bits >> pos) & 1u) x = penalise(x, penalty);
+            float v = __fmul_rn(x, inv_t);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float hi = fmaxf(top[j], v);
+                v = fminf(top[j], v);
+                top[j] = hi;
+            }
+        }
+        uint32_t key[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t u = __float_as_uint(top[j]);
+            key[j] = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+        }
+        uint32_t res = 0;
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t cand = res | (1u << bit);
+            uint32_t c = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) c += (uint32_t)__popc(__ballot_sync(0xFFFFFFFFu, key[j] >= cand));
+            if (c >= k) res = cand;
+        }
+        const float kth = __uint_as_float((res & 0x80000000u) ? (res & 0x7FFFFFFFu) : ~res);
+        if (kth > -__int_as_float(0x7F800000)) {
+            const float delta = tie_margin(kth, mrun);
+            const float th = kth - delta;
+            if (th > ws.theta) ws.theta = th;
+            ws.wdelta = fminf(ws.wdelta, delta);
+            uint32_t keep = 0;
+            for (uint32_t h = hmask; h; h &= h - 1u) {
+                const int bit = __ffs(h) - 1;
+                const int pos = (bit + lane) & 31;
+                float x = run[pos];
+                if ((bits >> pos) & 1u) x = penalise(x, penalty);
+                if (__fmul_rn(x, inv_t) >= ws.theta) keep |= 1u << bit;
+            }
+            hmask = keep;
+        }
+    }
     while (__any_sync(0xFFFFFFFFu, hmask != 0u)) {
         float xv[4];
         uint32_t gv[4], hm = 0;
@@ -986,7 +1040,7 @@ __device__ __noinline__ WState topk_tile(const float* run, uint32_t hmask, uint3
             xv[c] = 0.0f;
             gv[c] = 0u;
             if (hmask) {
-                const int pos = __ffs(hmask) - 1;
+                const int pos = (__ffs(hmask) - 1 + lane) & 31;
                 hmask &= hmask - 1u;
                 float x = run[pos];
                 if ((bits >> pos) & 1u) x = penalise(x, penalty);
@@ -1056,14 +1110,21 @@ struct FinishCtx {
 __device__ __noinline__ void finish_path_k(RowShared& sh, FinishCtx& f) {
     const int tid = threadIdx.x;
     const float kInf = __int_as_float(0x7F800000);
-    for (uint32_t i = tid; i < f.nk; i += kThreads) {
-        const float e = exact_expf(__fsub_rn(f.cand_x[i], f.mx), f.exptab);
-        const float p = __fmul_rn(e, f.inv);
-        f.keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | f.cand_i[i];
+    // (the context's fields in registers: loads through `f` go to local memory)
+    const uint32_t nk = f.nk;
+    const float* const cand_x = f.cand_x;
+    const uint32_t* const cand_i = f.cand_i;
+    unsigned long long* const keys = f.keys;
+    const float mx = f.mx, inv = f.inv;
+    const ExpTable exptab = f.exptab;
+    for (uint32_t i = tid; i < nk; i += kThreads) {
+        const float e = exact_expf(__fsub_rn(cand_x[i], mx), exptab);
+        const float p = __fmul_rn(e, inv);
+        keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | cand_i[i];
     }
     csync();
     const long long ts = clock64();
-    bitonic_sort_u64(f.keys, f.nk);  // (p desc, index asc)
+    bitonic_sort_u64(keys, nk);  // (p desc, index asc)
     f.acc_sort += clock64() - ts;
     f.n_cand = f.nk;
     for (uint32_t i = tid; i < f.k; i += kThreads) sh.ser[i] = __uint_as_float(~(uint32_t)(f.keys[i] >> 32));
@@ -1857,11 +1918,22 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 // candidate threshold from a lower bound of the max before this tile
                 float cthr = -kInf;
                 if (lists_on) {
+                    // fold in the published maxima of earlier tiles, four (max, tag) words at a time
                     while (front < t) {
-                        if (*reinterpret_cast<volatile uint32_t*>(&tt[front].tag) != r) break;
-                        __threadfence_block();
-                        gpm = fmax_nan(gpm, tt[front].mt);
-                        ++front;
+                        const uint32_t nb = min(4u, t - front);
+                        unsigned long long w[4];
+#pragma unroll
+                        for (uint32_t u = 0; u < 4u; ++u)
+                            w[u] = u < nb ? *reinterpret_cast<volatile unsigned long long*>(&tt[front + u].mt) : 0ull;
+                        uint32_t adv = 0;
+#pragma unroll
+                        for (uint32_t u = 0; u < 4u; ++u)
+                            if (adv == u && u < nb && (uint32_t)(w[u] >> 32) == r) {
+                                gpm = fmax_nan(gpm, __uint_as_float((uint32_t)w[u]));
+                                adv = u + 1u;
+                            }
+                        front += adv;
+                        if (adv < nb) break;
                     }
                     const float mp = fmax_nan(m_w, gpm);
                     cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
@@ -1955,16 +2027,18 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     }
                     sl = (sp[0] + sp[1]) + (sp[2] + sp[3]);
                 } else {
-                    uint32_t p = woff + cinc - nc;
-                    uint32_t m = cmask;
+                    // lane-rotated order (distinct banks); each entry at its index-order place
+                    const uint32_t p0 = woff + cinc - nc;
+                    uint32_t m = __funnelshift_r(cmask, cmask, lane);
                     while (m) {
-                        const int pos = __ffs(m) - 1;
+                        const int pos = (__ffs(m) - 1 + lane) & 31;
                         m &= m - 1u;
                         float xv = slot[pos];
                         if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
                         const float xs = __fmul_rn(xv, inv_t);
                         sl += ex2_approx(__fmul_rn(__fsub_rn(xs, ml), kLog2e));
-                        wlist[p++] = make_uint2(__float_as_uint(xs), tb + l0 + (uint32_t)pos);
+                        wlist[p0 + (uint32_t)__popc(cmask & ((1u << pos) - 1u))] =
+                            make_uint2(__float_as_uint(xs), tb + l0 + (uint32_t)pos);
                     }
                 }
                 __syncwarp();
@@ -1978,7 +2052,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const float tot = warp_sum_f(cl);
                 if (lane == 0) {
                     TileRec& R = tt[t];
-                    R.mt = mt;
                     R.pt = tot;
                     R.loff = (uint32_t)warp * capw + woff;
                     R.lcnt = dense ? kDenseMark : ncand;
@@ -1986,8 +2059,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         atomicOr(&sh.dense[t >> 5], 1u << (t & 31));
                     else
                         atomicAnd(&sh.dense[t >> 5], ~(1u << (t & 31)));
+                    *reinterpret_cast<volatile unsigned long long*>(&R.mt) =
+                        ((unsigned long long)r << 32) | __float_as_uint(mt);  // publishes mt
                     __threadfence_block();
-                    *reinterpret_cast<volatile uint32_t*>(&R.tag) = r;
                     atomicAdd(const_cast<uint32_t*>(&sh.p1done), 1u);
                 }
                 if (!dense) woff += ncand;
@@ -2280,8 +2354,10 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             }
                         }
                         live = lmask != 0u;
-                        while (lmask) {  // the live elements only
-                            const int pos = __ffs(lmask) - 1;
+                        // the live elements only, in a lane-rotated order (distinct banks)
+                        lmask = __funnelshift_r(lmask, lmask, lane);
+                        while (lmask) {
+                            const int pos = (__ffs(lmask) - 1 + lane) & 31;
                             lmask &= lmask - 1u;
                             float xv = slot[l0 + (uint32_t)pos];
                             if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
