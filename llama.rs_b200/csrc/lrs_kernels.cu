@@ -107,6 +107,7 @@ struct RowShared {
     uint64_t empty[kSlots];
     uint64_t rq_full[kRowQ];
     uint64_t rq_empty[kRowQ];
+    uint64_t bwait[kWarps];    // baton: one phase per hand-over to warp w (its next chain step)
     uint32_t rq_row[kRowQ];
     volatile uint32_t abort;   // a wait ran out: every later wait returns at once
     volatile uint32_t bseq;    // baton: the tile whose chain step may run
@@ -863,7 +864,19 @@ __device__ __forceinline__ void apply_penalty(float (&v)[32], uint32_t bits, int
 __device__ __noinline__ float warp_serial_add(float s, float e, float d, bool exact, int lo, int cnt,
                                               const ExpTable tab) {
     const int lane = threadIdx.x & 31;
-    if (!exact && lane >= lo && lane < lo + cnt) e = exact_expf(d, tab);
+    // libm's value only where CUDA's (within 2 ulp) could round differently: s only
+    // grows, so its grid at the start (unit 2^uu) is the finest of the run, and every
+    // rounding boundary of s + e, on that grid or a coarser one, lies at a multiple of
+    // half the unit; a value more than 2^-21 e from all of them adds what libm's adds.
+    if (!exact && lane >= lo && lane < lo + cnt) {
+        const int uu = unit_exp(s);
+        bool amb = true;
+        if (uu > -149) {
+            const float x = ldexpf(e, 1 - uu);  // e / (half unit), exact below 2^22
+            amb = !(x < 4194304.0f) || fabsf(__fsub_rn(x, rintf(x))) <= __fmul_rn(x, 4.76837158203125e-07f);
+        }
+        if (amb) e = exact_expf(d, tab);
+    }
     for (int j = lo; j < lo + cnt; ++j) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e, j));
     return s;
 }
@@ -932,8 +945,8 @@ __device__ __noinline__ WState warp_compact(float* wx, uint32_t* wi, WState s, u
     return s;
 }
 
-// Increments of one element on the two grids a run is classified for (units
-// 2^u0 and 2^(u0+1)): e = libm's expf(d) where CUDA's expf (within 2 ulp) could round
+// Increments of elements on the two grids a run is classified for (units 2^u0 and
+// 2^(u0+1)): e = libm's expf(d) where CUDA's expf (within 2 ulp) could round
 // differently; a tie or an element of half a binade or more flags the grid.
 struct GridAcc {
     float s0, s1;  // sums of the rounded increments (multiples of the units)
@@ -1736,6 +1749,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             mbar_init(&sh.rq_full[i], 1);
             mbar_init(&sh.rq_empty[i], 1);
         }
+        for (int i = 0; i < kWarps; ++i) mbar_init(&sh.bwait[i], 1);
         sh.abort = 0u;
         sh.bseq = 0xFFFFFFFFu;
         sh.p1done = 0u;
@@ -1749,6 +1763,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
 
     uint32_t qbase = 0;  // loads of earlier rows (same count in every consumer thread)
     uint32_t rqi = 0;
+    uint32_t bcnt = 0;   // batons this warp has received (its bwait phase)
     for (;;) {
         if (tid == 0) {
             const uint32_t qs = rqi % kRowQ;
@@ -2245,6 +2260,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     sh.bval = s0;
                     __threadfence_block();
                     sh.bseq = carry;  // first sum-live tile
+                    if (carry < g.nchunks) mbar_arrive(&sh.bwait[carry % kWarps]);  // (release)
                 }
             }
             csync();
@@ -2410,17 +2426,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const long long tb0 = clock64();
                         float Sx = 0.0f;
                         if (lane == 0) {
-                            const long long t0w = clock64();
-                            while (sh.bseq != t) {
-                                if (sh.abort) break;
-                                if (clock64() - t0w > kWaitCycles) {
-                                    sh.abort = 1u;
-                                    atomicExch(a.err_flag, LRS_E_TIMEOUT);
-                                    break;
-                                }
-                                __nanosleep(20);
-                            }
-                            __threadfence_block();
+                            // the message arrives on this warp's barrier (acquire on completion)
+                            wait_bar(sh, &sh.bwait[warp], bcnt & 1u, a.err_flag);
+                            ++bcnt;
                             Sx = sh.bval;
                         }
                         Sx = __shfl_sync(0xFFFFFFFFu, Sx, 0);
@@ -2485,15 +2493,20 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                                     }
                                 }
                             } else {
-                                const uint32_t j = (uint32_t)L * kRunS + (uint32_t)lane;
                                 len = kRunS;
-                                if (lane < kRunS && j < lcnt) {
-                                    const float d = __fsub_rn(__uint_as_float(__ldcg(&ent[j].x)), mx);
-                                    if (d >= thr_d) {
-                                        de = d;
-                                        exe = de == 0.0f;
-                                        e = exe ? 1.0f : expf(de);
-                                    }
+                                // run L's entries (lane L's prefetched scaled logits, -inf
+                                // where absent) to lanes 0 .. kRunS-1
+                                float xl = -kInf;
+#pragma unroll
+                                for (int i = 0; i < kRunS; ++i) {
+                                    const float v = __shfl_sync(0xFFFFFFFFu, xsv[i], L);
+                                    if (lane == i) xl = v;
+                                }
+                                const float d = __fsub_rn(xl, mx);
+                                if (xl != -kInf && d >= thr_d) {
+                                    de = d;
+                                    exe = de == 0.0f;
+                                    e = exe ? 1.0f : expf(de);
                                 }
                             }
                             Sx = warp_serial_add(Sx, e, de, exe, 0, len, exptab);
@@ -2502,9 +2515,10 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             if (p >= 32u) break;
                         }
                         if (lane == 0) {
+                            const uint32_t nx = tt[t].next;
                             sh.bval = Sx;
-                            __threadfence_block();
-                            sh.bseq = tt[t].next;
+                            sh.bseq = nx;
+                            if (nx < g.nchunks) mbar_arrive(&sh.bwait[nx % kWarps]);  // (release)
                         }
                         acc_baton += tb1 - tb0;
                         acc_chain += clock64() - tb1 + (tb0 - tc);
