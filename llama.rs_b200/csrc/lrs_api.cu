@@ -271,7 +271,7 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     CKF(cudaMalloc(&ctx->d_hist_len, R * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
     CKF(cudaMemset(ctx->d_scratch, 0, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
-    CKF(cudaMalloc(&ctx->d_counter, 2 * sizeof(uint32_t)));
+    CKF(cudaMalloc(&ctx->d_counter, kLrsRowCounters * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_err, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_err, 0, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_state, 0, R * sizeof(unsigned long long)));
@@ -358,7 +358,7 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.err_flag = ctx->d_err;
     uint32_t grid = ctx->scratch_ctas;
     if (grid > rows) grid = rows;
-    CK(cudaMemsetAsync(ctx->d_counter, 0, 2 * sizeof(uint32_t), s));
+    CK(cudaMemsetAsync(ctx->d_counter, 0, kLrsRowCounters * sizeof(uint32_t), s));
     CK(lrs_kernel_launch(&args, grid, smem, s));
     return LRS_OK;
 }

@@ -86,6 +86,8 @@ static_assert(kRegionABytes >= (size_t)kNB * 8, "bucket counts and offsets");
 static_assert(kRegionBBytes >= (size_t)kKCap * 8 + (size_t)kKSortMax * 8, "candidates and sort keys");
 static_assert(kRegionBBytes >= (size_t)kWarps * 256 * 4, "per-warp radix counts");
 static_assert(kRegionBBytes >= (size_t)kNB * 4, "bucket cursors");
+static_assert(kRegionBBytes >= ((size_t)kGatherItemsOff + (size_t)kWarps * 1024) * 4, "gather item lists");
+static_assert((size_t)kNB <= (size_t)kGatherItemsOff, "bucket cursors before the gather item lists");
 
 using SampleArgs = lrs_kernel_args_t;
 
@@ -173,12 +175,19 @@ __device__ __forceinline__ uint32_t row_passes(const lrs_params& P, uint32_t n) 
     return (stochastic && n >= 2) ? 2u : 1u;
 }
 
-// Rows whose finish orders a large candidate set (top_k off or above kKMax, the
-// path-N finish) take the longest; they are claimed first so that no CTA starts one
-// near the end of the launch.
-__device__ __forceinline__ bool row_long(const lrs_params& P, uint32_t n) {
+// Rows are claimed roughly longest first, so that no CTA starts a long row near the
+// end of the launch: the exact softmax sum costs most at high temperature (many
+// elements can change it), and rows whose finish orders a large candidate set (top_k
+// off or above kKMax, the path-N finish) cost more than the others.  Class 0 is
+// claimed first, kRowClasses - 1 last.
+constexpr uint32_t kRowClasses = 4;
+static_assert(kRowClasses == (uint32_t)kLrsRowCounters, "one row counter per claim class");
+__device__ __forceinline__ uint32_t row_class(const lrs_params& P, uint32_t n) {
+    if (row_passes(P, n) != 2u) return kRowClasses - 1;
     const uint32_t k = (P.top_k == 0 || P.top_k > n) ? n : P.top_k;
-    return row_passes(P, n) == 2u && !(k < n && k <= (uint32_t)kKMax);
+    const bool long_finish = !(k < n && k <= (uint32_t)kKMax);
+    const bool hot = !(P.temperature < 1.0f);
+    return hot ? (long_finish ? 0u : 1u) : (long_finish ? 2u : 3u);
 }
 
 // Bounded wait on an mbarrier phase.  On timeout the CTA's abort flag and the sticky
@@ -216,17 +225,17 @@ __device__ __forceinline__ bool wait_full(RowShared& sh, uint32_t q, int32_t* er
 __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float* ring) {
     const uint64_t pol_keep = policy_evict_last(), pol_drop = policy_evict_first();
     uint32_t q = 0, rqi = 0, p1target = 0, sweep = 0;
-    // next row: the first sweep over the rows claims the long ones, the second the rest
-    // (each sweep has its own counter, so every row is claimed exactly once)
+    // next row: sweep c over the rows claims the rows of class c (each sweep has its
+    // own counter, so every row is claimed exactly once)
     auto claim = [&]() -> uint32_t {
         for (;;) {
             const uint32_t r = atomicAdd(a.row_counter + sweep, 1u);
             if (r >= a.rows) {
-                if (sweep == 1u) return a.rows;
-                sweep = 1u;
+                if (sweep + 1u == kRowClasses) return a.rows;
+                ++sweep;
                 continue;
             }
-            if (row_long(a.params[r], a.n) == (sweep == 0u)) return r;
+            if (row_class(a.params[r], a.n) == sweep) return r;
         }
     };
     auto issue = [&](const Geo& g, uint32_t c, uint64_t pol) -> bool {

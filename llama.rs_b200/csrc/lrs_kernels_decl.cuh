@@ -7,6 +7,8 @@
 
 #include "../../include/llamars_sampler.h"
 
+constexpr int kLrsRowCounters = 4;  // row claim classes of the sampling kernel
+
 struct lrs_kernel_args_t {
     const float* logits;      // row r at logits + r * ld
     uint64_t ld;
@@ -29,7 +31,7 @@ struct lrs_kernel_args_t {
     uint64_t tiles_off;                   // tile records of rows longer than the shared table
     uint64_t lanes_off;                   // per-tile lane sums
     uint64_t lists_off;                   // candidate lists of sparse tiles
-    uint32_t* row_counter;    // two row counters (long rows first, then the rest), zeroed before each launch
+    uint32_t* row_counter;    // kLrsRowCounters row counters (one per claim class), zeroed before each launch
     int32_t* err_flag;        // sticky error word
 };
 

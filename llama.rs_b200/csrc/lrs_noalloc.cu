@@ -39,7 +39,7 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned long long g_scratch[kScratchBytes / 8];
 static __device__ __align__(256) unsigned long long g_exp_index[lrs::kExpIndexWords];
 static __device__ __align__(256) uint2 g_exp_entries[kMaxTableEntries + 1];
-static __device__ __align__(256) uint32_t g_counter[3];  // [0], [1] row counters, [2] error word
+static __device__ __align__(256) uint32_t g_counter[kLrsRowCounters + 1];  // row counters, then the error word
 
 struct DeviceSetup {
     bool done = false;
@@ -185,10 +185,10 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.lanes_off = lanes_off;
         args.lists_off = lists_off;
         args.row_counter = s.counter;
-        args.err_flag = reinterpret_cast<int32_t*>(s.counter + 2);
+        args.err_flag = reinterpret_cast<int32_t*>(s.counter + kLrsRowCounters);
         cudaStream_t st = (cudaStream_t)stream;
         // the row counters and the error word must start at zero on every call
-        if (cudaMemsetAsync(s.counter, 0, 3 * sizeof(uint32_t), st) != cudaSuccess)
+        if (cudaMemsetAsync(s.counter, 0, (kLrsRowCounters + 1) * sizeof(uint32_t), st) != cudaSuccess)
             rc = LRS_E_CUDA;
         else if (lrs_kernel_launch(&args, grid, smem, st) != cudaSuccess)
             rc = LRS_E_CUDA;
