@@ -122,6 +122,8 @@ struct RowShared {
     uint32_t cand_over;
     float theta;
     float delta_min;
+    uint32_t ktheta;     // path K: largest threshold any warp has applied (order-preserving key)
+    uint32_t kdelta;     // path K: smallest margin of a published threshold (float bits, >= 0)
     uint32_t hist256[256];
     float vk;
     uint32_t events;
@@ -993,6 +995,31 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
     }
 }
 
+// The same on grid u0 alone (runs whose running sum cannot leave u0's binade by the
+// estimate; the caller flags grid u0 + 1, so a run that lands there is summed element
+// by element).
+__device__ __forceinline__ void classify_elem1(float d, float bm0, float h0, GridAcc& g, const ExpTable tab) {
+    bool ex = d == 0.0f;
+    float e = ex ? 1.0f : expf(d);
+    float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
+    if (!ex) {
+        const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
+        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
+                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
+        if (amb) {
+            e = exact_expf(d, tab);
+            ex = true;
+            i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
+        }
+    }
+    if (e >= bm0) {
+        g.sp0 = true;
+    } else {
+        g.s0 += i0;
+        if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) g.sp0 = true;
+    }
+}
+
 // Path K, one tile: appends this lane's hits (run offsets in hmask, values re-read from
 // the staged run) to the warp buffer in index order, 4 per lane at a time, compacting
 // the buffer when a batch would not fit.  mrun: the max of everything seen so far.
@@ -1854,6 +1881,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             sh.cand_over = 0;
             sh.theta = -kInf;
             sh.delta_min = kInf;
+            sh.ktheta = fkey(-kInf);
+            sh.kdelta = __float_as_uint(kInf);
             sh.vk = -kInf;
             sh.misc[7] = 0;
             sh.events = 0;
@@ -1968,6 +1997,12 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const float* slot = ring + (size_t)s * kTile + l0;
                 float ml = -kInf;                // lane: max of its scaled logits
                 uint32_t cmask = 0, hmask = 0;   // lane: candidate / top-k hit run offsets
+                if (kact) {
+                    // every warp's threshold bounds the row's k-th largest from below: take
+                    // the largest one published (its margin is in kdelta)
+                    const float gth = fkey_inv(*reinterpret_cast<volatile uint32_t*>(&sh.ktheta));
+                    if (gth > ws.theta) ws.theta = gth;
+                }
                 const float theta = kact ? ws.theta : kInf;
 #pragma unroll 2
                 for (int j = 0; j < 8; ++j) {
@@ -2013,7 +2048,13 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 const float mt = warp_max_nan(ml);
                 // path K: the tile's hits join the warp's buffer
                 if (kact && __any_sync(0xFFFFFFFFu, hmask != 0u)) {
+                    const float th_in = ws.theta;
                     ws = topk_tile(slot, hmask, bits, penalty, inv_t, tb + l0, fmax_nan(m_w, mt), k, wx, wi, wh, ws);
+                    if (lane == 0 && ws.theta > th_in && !ws.over) {
+                        atomicMin(&sh.kdelta, __float_as_uint(ws.wdelta));  // (before the threshold)
+                        __threadfence_block();
+                        atomicMax(&sh.ktheta, fkey(ws.theta));
+                    }
                     if (ws.over) {
                         kact = false;
                         if (lane == 0) sh.wover = 1u;
@@ -2162,6 +2203,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     if (tid == 0) {
                         float dm = kInf;
                         for (int w = 0; w < kWarps; ++w) dm = fminf(dm, sh.wdelta[w]);
+                        dm = fminf(dm, __uint_as_float(sh.kdelta));  // thresholds taken from other warps
                         sh.cand_n = tot;
                         sh.delta_min = dm;
                     }
@@ -2336,9 +2378,13 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     bool live = false;
                     int u0 = ulo;
                     float bm0 = 0.0f, bm1 = 0.0f, h0 = 0.0f, h1 = 0.0f;
+                    bool one = false;  // the run is classified on grid u0 alone
                     auto set_grids = [&](float pl, uint32_t first_index) {
                         const float dl = __fmaf_rn((float)first_index, 1.1920929e-07f, 1.2207031e-04f);
                         u0 = max(unit_exp(__fmul_rn(pl, __fsub_rn(1.0f, dl))), ulo);
+                        // an upper estimate (twice the margin: not a bound, a run that lands on
+                        // another grid is summed element by element) in the same binade
+                        one = unit_exp(__fmul_rn(pl, __fadd_rn(1.0f, __fadd_rn(dl, dl)))) == u0;
                         bm0 = grid_value(u0, kTwo23);
                         bm1 = __fadd_rn(bm0, bm0);
                         h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
@@ -2379,15 +2425,21 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             }
                         }
                         live = lmask != 0u;
-                        // the live elements only, in a lane-rotated order (distinct banks)
+                        // the live elements only, in a lane-rotated order (distinct banks);
+                        // on grid u0 alone when every run of the warp allows it
+                        const bool one_w = __all_sync(0xFFFFFFFFu, one);
                         lmask = __funnelshift_r(lmask, lmask, lane);
                         while (lmask) {
                             const int pos = (__ffs(lmask) - 1 + lane) & 31;
                             lmask &= lmask - 1u;
                             float xv = slot[l0 + (uint32_t)pos];
                             if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
-                            classify_elem(d_of(xv, inv_t, mx), bm0, bm1, h0, h1, acc, exptab);
+                            if (one_w)
+                                classify_elem1(d_of(xv, inv_t, mx), bm0, h0, acc, exptab);
+                            else
+                                classify_elem(d_of(xv, inv_t, mx), bm0, bm1, h0, h1, acc, exptab);
                         }
+                        if (one_w) acc.sp1 = true;
                     } else {
                         // run = kRunS consecutive list entries of the sparse tile
                         const uint32_t e0 = (uint32_t)lane * kRunS;
@@ -2410,12 +2462,17 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             float excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
                             if (lane == 0) excl = 0.0f;
                             set_grids(__fadd_rn(ptile, excl), e0 < lcnt ? i0v : tb);
+                            const bool one_w = __all_sync(0xFFFFFFFFu, one);
 #pragma unroll
                             for (int i = 0; i < kRunS; ++i)
                                 if (dv[i] != -kInf) {
                                     live = true;
-                                    classify_elem(dv[i], bm0, bm1, h0, h1, acc, exptab);
+                                    if (one_w)
+                                        classify_elem1(dv[i], bm0, h0, acc, exptab);
+                                    else
+                                        classify_elem(dv[i], bm0, bm1, h0, h1, acc, exptab);
                                 }
+                            if (one_w) acc.sp1 = true;
                         }
                     }
                     if (sum_live) {
