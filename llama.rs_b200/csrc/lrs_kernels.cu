@@ -88,6 +88,7 @@ static_assert(kRegionBBytes >= (size_t)kWarps * 256 * 4, "per-warp radix counts"
 static_assert(kRegionBBytes >= (size_t)kNB * 4, "bucket cursors");
 static_assert(kRegionBBytes >= ((size_t)kGatherItemsOff + (size_t)kWarps * 1024) * 4, "gather item lists");
 static_assert((size_t)kNB <= (size_t)kGatherItemsOff, "bucket cursors before the gather item lists");
+static_assert((size_t)kKCap * 8 + (size_t)kWarps * 32 * kRunS * 4 <= (size_t)kRegionBBytes, "pass-2 live list values");
 
 using SampleArgs = lrs_kernel_args_t;
 
@@ -967,13 +968,15 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
                                               const ExpTable tab) {
     bool ex = d == 0.0f;
     float e = ex ? 1.0f : expf(d);
+    // An element of a quarter of bm (2^21 units) or more flags its grid without its
+    // libm value: it is summed element by element anyway if its run lands there.
+    const bool big0 = e >= __fmul_rn(bm0, 0.25f), big1 = e >= __fmul_rn(bm1, 0.25f);
     float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
     float i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
     if (!ex) {
         const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
-        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol || fabsf(__fsub_rn(e, bm1)) <= tol ||
-                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
-                         (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
+        const bool amb = e < 7.8886091e-31f || (!big0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
+                         (!big1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
         if (amb) {
             e = exact_expf(d, tab);
             ex = true;
@@ -981,13 +984,13 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
             i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
         }
     }
-    if (e >= bm0) {
+    if (big0 || e >= bm0) {
         g.sp0 = true;
     } else {
         g.s0 += i0;
         if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) g.sp0 = true;
     }
-    if (e >= bm1) {
+    if (big1 || e >= bm1) {
         g.sp1 = true;
     } else {
         g.s1 += i1;
@@ -1001,18 +1004,18 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
 __device__ __forceinline__ void classify_elem1(float d, float bm0, float h0, GridAcc& g, const ExpTable tab) {
     bool ex = d == 0.0f;
     float e = ex ? 1.0f : expf(d);
+    const bool big0 = e >= __fmul_rn(bm0, 0.25f);
     float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
     if (!ex) {
         const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
-        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
-                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
+        const bool amb = e < 7.8886091e-31f || (!big0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
         if (amb) {
             e = exact_expf(d, tab);
             ex = true;
             i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
         }
     }
-    if (e >= bm0) {
+    if (big0 || e >= bm0) {
         g.sp0 = true;
     } else {
         g.s0 += i0;
@@ -2463,15 +2466,28 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             if (lane == 0) excl = 0.0f;
                             set_grids(__fadd_rn(ptile, excl), e0 < lcnt ? i0v : tb);
                             const bool one_w = __all_sync(0xFFFFFFFFu, one);
+                            // the live entries only (a few per lane), through shared memory: per
+                            // warp [entry][lane] in the space of the path-K keys (unused until the finish)
+                            float* const wlive = reinterpret_cast<float*>(smem_raw + kRingBytes + kRegionABytes +
+                                                                          (size_t)kKCap * 8) +
+                                                 (size_t)warp * 32 * kRunS;
+                            uint32_t lmk = 0;
 #pragma unroll
                             for (int i = 0; i < kRunS; ++i)
                                 if (dv[i] != -kInf) {
-                                    live = true;
-                                    if (one_w)
-                                        classify_elem1(dv[i], bm0, h0, acc, exptab);
-                                    else
-                                        classify_elem(dv[i], bm0, bm1, h0, h1, acc, exptab);
+                                    lmk |= 1u << i;
+                                    wlive[i * 32 + lane] = dv[i];
                                 }
+                            live = lmk != 0u;
+                            while (lmk) {
+                                const int i = __ffs(lmk) - 1;
+                                lmk &= lmk - 1u;
+                                const float d = wlive[i * 32 + lane];
+                                if (one_w)
+                                    classify_elem1(d, bm0, h0, acc, exptab);
+                                else
+                                    classify_elem(d, bm0, bm1, h0, h1, acc, exptab);
+                            }
                             if (one_w) acc.sp1 = true;
                         }
                     }
@@ -2490,28 +2506,39 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const bool any1 = __any_sync(0xFFFFFFFFu, live && acc.sp1);
                         // ---- chain step: wait for the exact sum before this tile
                         const long long tb0 = clock64();
+                        // Lane 0 alone takes a step that is one add (the common case) and hands
+                        // the baton on at once; the warp joins only for a walk over the runs.
                         float Sx = 0.0f;
+                        bool done = false;
                         if (lane == 0) {
+                            const uint32_t nx = tt[t].next;
                             // the message arrives on this warp's barrier (acquire on completion)
                             wait_bar(sh, &sh.bwait[warp], bcnt & 1u, a.err_flag);
                             ++bcnt;
                             Sx = sh.bval;
-                        }
-                        Sx = __shfl_sync(0xFFFFFFFFu, Sx, 0);
-                        const long long tb1 = clock64();
-                        if (unit_exp(Sx) < ulo && lane == 0) sh.misc[7] = 1u;  // estimate bound broken
-                        bool done = lm == 0u;
-                        if (!done && uni) {
-                            const int u = unit_exp(Sx);
-                            const uint32_t A = grid_count(Sx, u);
-                            if (u == u0w && !any0 && A + t0 < kTwo24) {
-                                Sx = grid_value(u, A + t0);
-                                done = true;
-                            } else if (u == u0w + 1 && !any1 && A + t1 < kTwo24) {
-                                Sx = grid_value(u, A + t1);
-                                done = true;
+                            done = lm == 0u;
+                            if (!done && uni) {
+                                const int u = unit_exp(Sx);
+                                const uint32_t A = grid_count(Sx, u);
+                                if (u == u0w && !any0 && A + t0 < kTwo24) {
+                                    Sx = grid_value(u, A + t0);
+                                    done = true;
+                                } else if (u == u0w + 1 && !any1 && A + t1 < kTwo24) {
+                                    Sx = grid_value(u, A + t1);
+                                    done = true;
+                                }
+                            }
+                            if (done) {
+                                sh.bval = Sx;
+                                sh.bseq = nx;
+                                if (nx < g.nchunks) mbar_arrive(&sh.bwait[nx % kWarps]);  // (release)
                             }
                         }
+                        done = __shfl_sync(0xFFFFFFFFu, done, 0);
+                        Sx = __shfl_sync(0xFFFFFFFFu, Sx, 0);
+                        const long long tb1 = clock64();
+                        if (lane == 0 && !done && unit_exp(Sx) < ulo) sh.misc[7] = 1u;  // estimate bound broken
+                        const bool walked = !done;
                         uint32_t p = 0;
                         for (int guard = 0; guard <= 32 && !done; ++guard) {
                             const int u = unit_exp(Sx);
@@ -2580,7 +2607,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             p = (uint32_t)L + 1u;
                             if (p >= 32u) break;
                         }
-                        if (lane == 0) {
+                        if (lane == 0 && walked) {
                             const uint32_t nx = tt[t].next;
                             sh.bval = Sx;
                             sh.bseq = nx;
