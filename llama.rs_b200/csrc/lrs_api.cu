@@ -26,10 +26,17 @@ namespace {
 thread_local std::string g_create_error;
 }  // namespace
 
+// lrs_sample with pinned host rows: copies overlapped with sampling in this many pieces
+// (batches of at least kPipeMinRows rows)
+constexpr uint32_t kPipeChunks = 4;
+constexpr uint32_t kPipeMinRows = 512;
+
 struct lrs_ctx {
     int device = 0;
     uint32_t max_rows = 0, max_vocab = 0, max_hist = 0;
     cudaStream_t stream = nullptr;
+    cudaStream_t copy_stream = nullptr;          // host rows: copies overlapped with sampling
+    cudaEvent_t copied[kPipeChunks] = {};
     int num_sms = 0;
     int ctas_per_sm = 0;
     // device buffers
@@ -201,6 +208,9 @@ int lrs_destroy(lrs_ctx* ctx) {
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
+    if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
+    for (cudaEvent_t e : ctx->copied)
+        if (e) cudaEventDestroy(e);
     delete ctx;
     return LRS_OK;
 }
@@ -381,6 +391,7 @@ int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t
     cudaStream_t s = ctx->stream;
     const float* d_logits = logits;
     uint64_t dld = ld;
+    bool pipelined = false;
     if (!logits_on_device && n > 0) {
         // One H2D copy of the rows (all rows share one when ld == 0).  Caller memory
         // that is already pinned is copied from directly; pageable memory goes through
@@ -392,7 +403,9 @@ int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t
         cudaPointerAttributes pa;
         const bool pinned = cudaPointerGetAttributes(&pa, logits) == cudaSuccess && pa.type == cudaMemoryTypeHost;
         cudaGetLastError();
-        if (pinned) {
+        if (pinned && ld != 0 && rows >= kPipeMinRows) {
+            pipelined = true;  // copied chunk by chunk below, each sampled as soon as it lands
+        } else if (pinned) {
             CK(cudaMemcpy2DAsync(ctx->d_logits, (size_t)n * 4, logits, (size_t)(ld ? ld : n) * 4, (size_t)n * 4,
                                  rcopy, cudaMemcpyHostToDevice, s));
         } else {
@@ -420,10 +433,38 @@ int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t
         d_hlen = ctx->d_hist_len;
         dhld = hmax;
     }
-    int rc = lrs_sample_device(ctx, d_logits, rows, n, dld, d_hist, dhld, d_hlen, ctx->d_params,
+    int rc = LRS_OK;
+    if (pipelined) {
+        // Pinned host rows in kPipeChunks pieces: the copy of piece c + 1 (copy stream,
+        // copy engine) runs while piece c is sampled (sampling stream); the launches stay
+        // in order on one stream, so they never share the per-CTA scratch at once.
+        if (!ctx->copy_stream) {
+            CK(cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking));
+            for (cudaEvent_t& e : ctx->copied) CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        }
+        // the copies may not overwrite rows an earlier call is still sampling
+        CK(cudaEventRecord(ctx->copied[0], s));
+        CK(cudaStreamWaitEvent(ctx->copy_stream, ctx->copied[0], 0));
+        const uint32_t per = (rows + kPipeChunks - 1) / kPipeChunks;
+        for (uint32_t c = 0, r0 = 0; r0 < rows; ++c, r0 += per) {
+            const uint32_t nr = rows - r0 < per ? rows - r0 : per;
+            float* dst = ctx->d_logits + (size_t)r0 * n;
+            CK(cudaMemcpy2DAsync(dst, (size_t)n * 4, logits + (size_t)r0 * ld, (size_t)ld * 4, (size_t)n * 4, nr,
+                                 cudaMemcpyHostToDevice, ctx->copy_stream));
+            CK(cudaEventRecord(ctx->copied[c], ctx->copy_stream));
+            CK(cudaStreamWaitEvent(s, ctx->copied[c], 0));
+            rc = lrs_sample_device(ctx, dst, nr, n, n, d_hist ? d_hist + (size_t)r0 * dhld : nullptr, dhld,
+                                   d_hlen ? d_hlen + r0 : nullptr, ctx->d_params + r0,
+                                   reinterpret_cast<uint64_t*>(ctx->d_state) + r0, ctx->d_tokens + r0,
+                                   ctx->d_probs + r0, ctx->d_status + r0, nullptr, s);
+            if (rc != LRS_OK) return rc;
+        }
+    } else {
+        rc = lrs_sample_device(ctx, d_logits, rows, n, dld, d_hist, dhld, d_hlen, ctx->d_params,
                                reinterpret_cast<uint64_t*>(ctx->d_state), ctx->d_tokens, ctx->d_probs,
                                ctx->d_status, nullptr, s);
-    if (rc != LRS_OK) return rc;
+        if (rc != LRS_OK) return rc;
+    }
     CK(cudaMemcpyAsync(ctx->h_tokens, ctx->d_tokens, rows * 4, cudaMemcpyDeviceToHost, s));
     CK(cudaMemcpyAsync(ctx->h_status, ctx->d_status, rows * 4, cudaMemcpyDeviceToHost, s));
     if (out_probs) CK(cudaMemcpyAsync(ctx->h_probs, ctx->d_probs, rows * 4, cudaMemcpyDeviceToHost, s));

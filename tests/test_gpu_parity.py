@@ -267,3 +267,20 @@ def test_equal_probabilities_across_bucket_boundaries():
     gpu = run_device(x, n, empty, np.zeros(rows, np.uint32), p, st)
     ref = run_oracle(x, n, None, None, p, st)
     compare(gpu, ref, "bucket-boundary ties")
+
+
+def test_pinned_host_rows_copied_in_pieces():
+    """lrs_sample with pinned host rows (>= 512): copies overlapped with sampling, piece by piece."""
+    import torch
+    w = W.headline(row_ids=range(600))
+    pinned = torch.from_numpy(w.logits).pin_memory().numpy()
+    bs = lrs.BatchSampler(len(w.params), w.vocab, w.window)
+    bs.set_params(w.params)
+    bs.set_state(w.state)
+    tok, probs = bs.sample(pinned, hist=w.hist, hist_len=w.hist_len, probs=True)
+    st = bs.get_state(len(w.params))
+    rtok, rinfo, rst = run_oracle(w.logits, w.vocab, w.hist, w.hist_len, w.params, w.state)
+    np.testing.assert_array_equal(tok, rtok)
+    np.testing.assert_array_equal(st, rst)
+    np.testing.assert_array_equal(probs.view(np.uint32), rinfo["prob"].view(np.uint32))
+    bs.close()
