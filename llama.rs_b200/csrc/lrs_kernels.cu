@@ -179,18 +179,20 @@ __device__ __forceinline__ uint32_t row_passes(const lrs_params& P, uint32_t n) 
 }
 
 // Rows are claimed roughly longest first, so that no CTA starts a long row near the
-// end of the launch: the exact softmax sum costs most at high temperature (many
-// elements can change it), and rows whose finish orders a large candidate set (top_k
-// off or above kKMax, the path-N finish) cost more than the others.  Class 0 is
-// claimed first, kRowClasses - 1 last.
-constexpr uint32_t kRowClasses = 4;
+// end of the launch: the exact softmax sum costs more the higher the temperature
+// (more elements can change it), and rows whose finish orders a large candidate set
+// (top_k off or above kKMax, the path-N finish) cost more than the others.  Four
+// temperature bands (from 1.25 down, 0.25 apart) times the two finishes; class 0 is
+// claimed first, kRowClasses - 1 last (with greedy rows).
+constexpr uint32_t kRowClasses = 8;
 static_assert(kRowClasses == (uint32_t)kLrsRowCounters, "one row counter per claim class");
 __device__ __forceinline__ uint32_t row_class(const lrs_params& P, uint32_t n) {
     if (row_passes(P, n) != 2u) return kRowClasses - 1;
     const uint32_t k = (P.top_k == 0 || P.top_k > n) ? n : P.top_k;
     const bool long_finish = !(k < n && k <= (uint32_t)kKMax);
-    const bool hot = !(P.temperature < 1.0f);
-    return hot ? (long_finish ? 0u : 1u) : (long_finish ? 2u : 3u);
+    const float t = P.temperature;  // (NaN: the hottest band; such a row fails fast anyway)
+    const uint32_t band = t < 0.75f ? 3u : t < 1.0f ? 2u : t < 1.25f ? 1u : 0u;
+    return band * 2u + (long_finish ? 0u : 1u);
 }
 
 // Bounded wait on an mbarrier phase.  On timeout the CTA's abort flag and the sticky

@@ -7,7 +7,7 @@
 
 #include "../../include/llamars_sampler.h"
 
-constexpr int kLrsRowCounters = 4;  // row claim classes of the sampling kernel
+constexpr int kLrsRowCounters = 8;  // row claim classes of the sampling kernel
 
 struct lrs_kernel_args_t {
     const float* logits;      // row r at logits + r * ld
