@@ -1976,22 +1976,22 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 // candidate threshold from a lower bound of the max before this tile
                 float cthr = -kInf;
                 if (lists_on) {
-                    // fold in the published maxima of earlier tiles, four (max, tag) words at a time
-                    while (front < t) {
-                        const uint32_t nb = min(4u, t - front);
-                        unsigned long long w[4];
+                    // fold in the published maxima of earlier tiles: one batch of up to eight
+                    // (max, tag) words a tile (seven tiles pass between a warp's tiles)
+                    {
+                        const uint32_t nb = min(8u, t - front);
+                        unsigned long long w[8];
 #pragma unroll
-                        for (uint32_t u = 0; u < 4u; ++u)
+                        for (uint32_t u = 0; u < 8u; ++u)
                             w[u] = u < nb ? *reinterpret_cast<volatile unsigned long long*>(&tt[front + u].mt) : 0ull;
                         uint32_t adv = 0;
 #pragma unroll
-                        for (uint32_t u = 0; u < 4u; ++u)
+                        for (uint32_t u = 0; u < 8u; ++u)
                             if (adv == u && u < nb && (uint32_t)(w[u] >> 32) == r) {
                                 gpm = fmax_nan(gpm, __uint_as_float((uint32_t)w[u]));
                                 adv = u + 1u;
                             }
                         front += adv;
-                        if (adv < nb) break;
                     }
                     const float mp = fmax_nan(m_w, gpm);
                     cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
@@ -2009,52 +2009,59 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     if (gth > ws.theta) ws.theta = gth;
                 }
                 const float theta = kact ? ws.theta : kInf;
+                if (greedy) {
 #pragma unroll 2
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
-                    const bool gv = c4 < nval;
-                    float4 q = make_float4(-kInf, -kInf, -kInf, -kInf);
-                    if (gv) q = *reinterpret_cast<const float4*>(slot + c4);
-                    float x[4] = {q.x, q.y, q.z, q.w};
-                    const uint32_t pb = (bits >> c4) & 15u;
-                    if (pb) {
-#pragma unroll
-                        for (int c = 0; c < 4; ++c)
-                            if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
-                    }
-                    if (greedy) {
-                        // lowest index among the maximal non-NaN values (strict '>' from index 0)
-                        const uint32_t gi0 = tb + l0 + c4;
-                        if (gv) {
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                        if (c4 >= nval) continue;
+                        const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                        float x[4] = {q.x, q.y, q.z, q.w};
+                        const uint32_t pb = (bits >> c4) & 15u;
+                        if (pb) {
 #pragma unroll
                             for (int c = 0; c < 4; ++c)
-                                if (x[c] > bv || (x[c] == bv && gi0 + c < bi)) {
-                                    bv = x[c];
-                                    bi = gi0 + c;
-                                }
+                                if ((pb >> c) & 1u) x[c] = penalise(x[c], penalty);
                         }
-                        continue;
-                    }
-                    if (gv) {
+                        // lowest index among the maximal non-NaN values (strict '>' from index 0)
+                        const uint32_t gi0 = tb + l0 + c4;
 #pragma unroll
-                        for (int c = 0; c < 4; ++c) {
-                            const float xs = __fmul_rn(x[c], inv_t);
-                            ml = fmax_nan(ml, xs);
-                            if (xs >= cthr) cmask |= 1u << (c4 + c);
-                            if (xs >= theta) hmask |= 1u << (c4 + c);
-                        }
+                        for (int c = 0; c < 4; ++c)
+                            if (x[c] > bv || (x[c] == bv && gi0 + c < bi)) {
+                                bv = x[c];
+                                bi = gi0 + c;
+                            }
                     }
-                }
-                if (greedy) {
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&sh.empty[s]);
                     continue;
+                }
+                // The penalty (a few ids per row) is applied to the staged run in place, so
+                // the loop below and pass 1's later reads of the run see penalised values
+                // (pass 2 stages the tile again and applies it itself).
+                for (uint32_t pm = bits; pm; pm &= pm - 1u) {
+                    float* const px = const_cast<float*>(slot) + (__ffs(pm) - 1);
+                    *px = penalise(*px, penalty);
+                }
+                const uint32_t bits1 = 0u;  // (pass 1 from here on: already applied)
+#pragma unroll 4
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                    if (c4 >= nval) continue;
+                    const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                    const float x[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                    for (int c = 0; c < 4; ++c) {
+                        const float xs = __fmul_rn(x[c], inv_t);
+                        ml = fmax_nan(ml, xs);
+                        if (xs >= cthr) cmask |= 1u << (c4 + c);
+                        if (xs >= theta) hmask |= 1u << (c4 + c);
+                    }
                 }
                 const float mt = warp_max_nan(ml);
                 // path K: the tile's hits join the warp's buffer
                 if (kact && __any_sync(0xFFFFFFFFu, hmask != 0u)) {
                     const float th_in = ws.theta;
-                    ws = topk_tile(slot, hmask, bits, penalty, inv_t, tb + l0, fmax_nan(m_w, mt), k, wx, wi, wh, ws);
+                    ws = topk_tile(slot, hmask, bits1, penalty, inv_t, tb + l0, fmax_nan(m_w, mt), k, wx, wi, wh, ws);
                     if (lane == 0 && ws.theta > th_in && !ws.over) {
                         atomicMin(&sh.kdelta, __float_as_uint(ws.wdelta));  // (before the threshold)
                         __threadfence_block();
@@ -2082,7 +2089,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         if (c4 >= nval) continue;
                         const float4 q = *reinterpret_cast<const float4*>(slot + c4);
                         float x[4] = {q.x, q.y, q.z, q.w};
-                        const uint32_t pb = (bits >> c4) & 15u;
+                        const uint32_t pb = (bits1 >> c4) & 15u;
                         if (pb) {
 #pragma unroll
                             for (int c = 0; c < 4; ++c)
@@ -2104,7 +2111,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const int pos = (__ffs(m) - 1 + lane) & 31;
                         m &= m - 1u;
                         float xv = slot[pos];
-                        if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
+                        if ((bits1 >> pos) & 1u) xv = penalise(xv, penalty);
                         const float xs = __fmul_rn(xv, inv_t);
                         sl += ex2_approx(__fmul_rn(__fsub_rn(xs, ml), kLog2e));
                         wlist[p0 + (uint32_t)__popc(cmask & ((1u << pos) - 1u))] =
