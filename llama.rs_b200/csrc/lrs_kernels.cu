@@ -2058,8 +2058,21 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     }
                 }
                 const float mt = warp_max_nan(ml);
-                // path K: the tile's hits join the warp's buffer
-                if (kact && __any_sync(0xFFFFFFFFu, hmask != 0u)) {
+                // path K: the tile's hits join the warp's buffer; a few hits with room in
+                // the buffer (the common case once a threshold is set) go straight in
+                const uint32_t nhit = kact ? __reduce_add_sync(0xFFFFFFFFu, (uint32_t)__popc(hmask)) : 0u;
+                if (nhit != 0u && ws.theta > -kInf && ws.wcnt + nhit <= (uint32_t)kWCap) {
+                    const uint32_t nh = (uint32_t)__popc(hmask);
+                    uint32_t o = ws.wcnt + warp_incl_scan_plain(nh) - nh;
+                    for (uint32_t m = hmask; m; m &= m - 1u) {
+                        const int pos = __ffs(m) - 1;
+                        wx[o] = __fmul_rn(slot[pos], inv_t);  // (the staged run is penalised)
+                        wi[o] = tb + l0 + (uint32_t)pos;
+                        ++o;
+                    }
+                    ws.wcnt += nhit;
+                    __syncwarp();
+                } else if (nhit != 0u) {
                     const float th_in = ws.theta;
                     ws = topk_tile(slot, hmask, bits1, penalty, inv_t, tb + l0, fmax_nan(m_w, mt), k, wx, wi, wh, ws);
                     if (lane == 0 && ws.theta > th_in && !ws.over) {
