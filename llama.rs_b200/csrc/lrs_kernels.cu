@@ -765,6 +765,16 @@ struct NoExact {  // sorted probability tiles are exact already
 // The scaled, shifted logit d = fl(fl(x * inv_t) - max) of sampler.rs:117 / ops.rs:409.
 __device__ __forceinline__ float d_of(float x, float inv_t, float mx) { return __fsub_rn(__fmul_rn(x, inv_t), mx); }
 
+// 2^e for -149 <= e <= 127, from its bits (normal or subnormal).
+__device__ __forceinline__ float pow2f(int e) {
+    return e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : __uint_as_float(1u << (e + 149));
+}
+// x * 2^e exactly, for x a multiple of 2^-e below 2^25 2^-e (a grid count): the integer
+// count, by two power-of-two products where 2^e alone is not a float.
+__device__ __forceinline__ uint32_t grid_units(float x, int e) {
+    return e > 127 ? (uint32_t)__fmul_rn(__fmul_rn(x, pow2f(127)), pow2f(e - 127)) : (uint32_t)__fmul_rn(x, pow2f(e));
+}
+
 // Largest (penalised) raw logit x with d_of(x) < thr, by bisection over the float order
 // (d_of is non-decreasing in x since inv_t >= 0).  -inf if there is none.
 __device__ __noinline__ float raw_threshold(float thr, float inv_t, float mx) {
@@ -2354,9 +2364,11 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 uint32_t i0_nx = 0;      // and the index of its first entry
                 // loads of tile t's per-lane inputs, issued one tile ahead of their use
                 auto prefetch = [&](uint32_t t) {
-                    bits_nx = tile_bits(t);
-                    lr_nx = __ldcg(lrec + t * 64u + (uint32_t)lane);
+                    // dense tiles: penalty bits and lane sums; sparse tiles: the list entries
                     const uint32_t lc = tt[t].lcnt, e0 = (uint32_t)lane * kRunS;
+                    const bool dn = lc == kDenseMark;
+                    bits_nx = dn ? tile_bits(t) : 0u;
+                    lr_nx = dn ? __ldcg(lrec + t * 64u + (uint32_t)lane) : 0.0f;
                     const bool want = !bad && lc != kDenseMark && (tt[t].flags & (kSumLive | kHistLive));
                     const uint2* en = lists + tt[t].loff;
 #pragma unroll
@@ -2412,8 +2424,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         one = unit_exp(__fmul_rn(pl, __fadd_rn(1.0f, __fadd_rn(dl, dl)))) == u0;
                         bm0 = grid_value(u0, kTwo23);
                         bm1 = __fadd_rn(bm0, bm0);
-                        h0 = u0 > -149 ? ldexpf(1.0f, u0 - 1) : 0.0f;
-                        h1 = ldexpf(1.0f, u0);
+                        h0 = u0 > -149 ? pow2f(u0 - 1) : 0.0f;
+                        h1 = pow2f(u0);
                     };
                     if (dense) {
                         // run = 32 consecutive elements of the staged tile
@@ -2516,8 +2528,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     if (sum_live) {
                         // multiples of U summed in f32 are exact below 2^24 U; at or above it the
                         // run leaves the grid anyway (saturated count)
-                        const uint32_t c0 = acc.s0 >= __fadd_rn(bm0, bm0) ? kSat : (uint32_t)ldexpf(acc.s0, -u0);
-                        const uint32_t c1 = acc.s1 >= __fadd_rn(bm1, bm1) ? kSat : (uint32_t)ldexpf(acc.s1, -(u0 + 1));
+                        const uint32_t c0 = acc.s0 >= __fadd_rn(bm0, bm0) ? kSat : grid_units(acc.s0, -u0);
+                        const uint32_t c1 = acc.s1 >= __fadd_rn(bm1, bm1) ? kSat : grid_units(acc.s1, -(u0 + 1));
                         // tile totals for the common case: every run classified on the same grids
                         const unsigned lm = __ballot_sync(0xFFFFFFFFu, live);
                         const int u0w = __shfl_sync(0xFFFFFFFFu, u0, lm ? __ffs(lm) - 1 : 0);
