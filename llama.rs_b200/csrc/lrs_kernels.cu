@@ -1035,6 +1035,48 @@ __device__ __forceinline__ void classify_elem1(float d, float bm0, float h0, Gri
     }
 }
 
+// Two elements at once on grid u0 alone (b absent: !vb), straight-line up to the rare
+// libm lookups so that the two dependency chains overlap.
+__device__ __forceinline__ void classify_pair1(float da, float db, bool vb, float bm0, float h0, GridAcc& g,
+                                               const ExpTable tab) {
+    bool exa = da == 0.0f, exb = db == 0.0f;
+    float ea = exa ? 1.0f : expf(da);
+    float eb = exb ? 1.0f : expf(db);
+    const float q = __fmul_rn(bm0, 0.25f);
+    const bool biga = ea >= q, bigb = eb >= q;
+    float ia = __fsub_rn(__fadd_rn(bm0, ea), bm0);
+    float ib = __fsub_rn(__fadd_rn(bm0, eb), bm0);
+    const float ta = __fmul_rn(ea, 4.76837158203125e-07f), tb = __fmul_rn(eb, 4.76837158203125e-07f);
+    const bool amba = !exa && (ea < 7.8886091e-31f || (!biga && fabsf(__fsub_rn(ea, ia)) >= __fsub_rn(h0, ta)));
+    const bool ambb = vb && !exb && (eb < 7.8886091e-31f || (!bigb && fabsf(__fsub_rn(eb, ib)) >= __fsub_rn(h0, tb)));
+    if (amba || ambb) {
+        if (amba) {
+            ea = exact_expf(da, tab);
+            exa = true;
+            ia = __fsub_rn(__fadd_rn(bm0, ea), bm0);
+        }
+        if (ambb) {
+            eb = exact_expf(db, tab);
+            exb = true;
+            ib = __fsub_rn(__fadd_rn(bm0, eb), bm0);
+        }
+    }
+    if (biga || ea >= bm0) {
+        g.sp0 = true;
+    } else {
+        g.s0 += ia;
+        if (exa && h0 > 0.0f && fabsf(__fsub_rn(ea, ia)) == h0) g.sp0 = true;
+    }
+    if (vb) {
+        if (bigb || eb >= bm0) {
+            g.sp0 = true;
+        } else {
+            g.s0 += ib;
+            if (exb && h0 > 0.0f && fabsf(__fsub_rn(eb, ib)) == h0) g.sp0 = true;
+        }
+    }
+}
+
 // Path K, one tile: appends this lane's hits (run offsets in hmask, values re-read from
 // the staged run) to the warp buffer in index order, 4 per lane at a time, compacting
 // the buffer when a batch would not fit.  mrun: the max of everything seen so far.
@@ -2466,17 +2508,30 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         // on grid u0 alone when every run of the warp allows it
                         const bool one_w = __all_sync(0xFFFFFFFFu, one);
                         lmask = __funnelshift_r(lmask, lmask, lane);
-                        while (lmask) {
-                            const int pos = (__ffs(lmask) - 1 + lane) & 31;
-                            lmask &= lmask - 1u;
-                            float xv = slot[l0 + (uint32_t)pos];
-                            if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
-                            if (one_w)
-                                classify_elem1(d_of(xv, inv_t, mx), bm0, h0, acc, exptab);
-                            else
+                        if (one_w) {
+                            // two elements an iteration
+                            while (lmask) {
+                                const int pa = (__ffs(lmask) - 1 + lane) & 31;
+                                lmask &= lmask - 1u;
+                                const bool vb = lmask != 0u;
+                                const int pb = vb ? (__ffs(lmask) - 1 + lane) & 31 : pa;
+                                lmask &= lmask - 1u;
+                                float xa = slot[l0 + (uint32_t)pa], xb = slot[l0 + (uint32_t)pb];
+                                if ((bits >> pa) & 1u) xa = penalise(xa, penalty);
+                                if (vb && ((bits >> pb) & 1u)) xb = penalise(xb, penalty);
+                                classify_pair1(d_of(xa, inv_t, mx), vb ? d_of(xb, inv_t, mx) : -kInf, vb, bm0, h0, acc,
+                                               exptab);
+                            }
+                            acc.sp1 = true;
+                        } else {
+                            while (lmask) {
+                                const int pos = (__ffs(lmask) - 1 + lane) & 31;
+                                lmask &= lmask - 1u;
+                                float xv = slot[l0 + (uint32_t)pos];
+                                if ((bits >> pos) & 1u) xv = penalise(xv, penalty);
                                 classify_elem(d_of(xv, inv_t, mx), bm0, bm1, h0, h1, acc, exptab);
+                            }
                         }
-                        if (one_w) acc.sp1 = true;
                     } else {
                         // run = kRunS consecutive list entries of the sparse tile
                         const uint32_t e0 = (uint32_t)lane * kRunS;
