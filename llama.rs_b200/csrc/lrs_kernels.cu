@@ -2589,8 +2589,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const unsigned lm = __ballot_sync(0xFFFFFFFFu, live);
                         const int u0w = __shfl_sync(0xFFFFFFFFu, u0, lm ? __ffs(lm) - 1 : 0);
                         const bool uni = __all_sync(0xFFFFFFFFu, !live || u0 == u0w);
-                        const uint32_t t0 = warp_reduce(live ? c0 : 0u, SatAdd());
-                        const uint32_t t1 = warp_reduce(live ? c1 : 0u, SatAdd());
+                        // (32 counts of at most 2^25 cannot wrap: one hardware sum, then saturate)
+                        const uint32_t t0 = min(__reduce_add_sync(0xFFFFFFFFu, live ? c0 : 0u), kSat);
+                        const uint32_t t1 = min(__reduce_add_sync(0xFFFFFFFFu, live ? c1 : 0u), kSat);
                         const bool any0 = __any_sync(0xFFFFFFFFu, live && acc.sp0);
                         const bool any1 = __any_sync(0xFFFFFFFFu, live && acc.sp1);
                         // ---- chain step: wait for the exact sum before this tile
