@@ -84,10 +84,9 @@ typedef struct lrs_row_info {
     float    prob;       /* probability of the returned token */
     uint32_t n_cand;     /* candidates examined after the streaming pass (implementation detail) */
     uint32_t events;     /* ordered (exact) steps taken by the sum emulation (implementation detail) */
-    uint32_t cycles[8];  /* SM clock cycles (saturating) by phase: 0 max/filter pass, 1 softmax-sum
-                            pass, 2 top-k/top-p/draw, 3 waits for staged tiles in the sum pass,
-                            4 ordered steps in the sum pass, 5 skip-threshold searches,
-                            6 waits in the max pass, 7 sorting (implementation detail) */
+    uint32_t cycles[8];  /* SM clock cycles (saturating) by phase: 0 max/filter pass, 1 estimates and
+                            thresholds, 2 softmax-sum pass, 3 top-k/top-p/draw, 4-6 zero,
+                            7 sorting within 3 (implementation detail) */
     uint32_t reserved;
 } lrs_row_info;
 

@@ -1914,7 +1914,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             if (tid == 0) inf.cycles[q] = sat32(now - t_mark);
             t_mark = now;
         };
-        long long acc_full = 0, acc_baton = 0, acc_chain = 0, acc_sort = 0;
+        long long acc_sort = 0;
         int32_t status = LRS_OK;
         uint32_t token = 0;
         float prob = 1.0f;
@@ -2048,9 +2048,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     const float mp = fmax_nan(m_w, gpm);
                     cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
                 }
-                const long long tw = clock64();
                 wait_full(sh, qq, a.err_flag);
-                acc_full += clock64() - tw;
                 const float* slot = ring + (size_t)s * kTile + l0;
                 float ml = -kInf;                // lane: max of its scaled logits
                 uint32_t cmask = 0, hmask = 0;   // lane: candidate / top-k hit run offsets
@@ -2447,11 +2445,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const uint32_t qq = q2 + tt[t].rank;
                         s = qq % kSlots;
                         slot = ring + (size_t)s * kTile;
-                        const long long tw = clock64();
                         wait_full(sh, qq, a.err_flag);
-                        acc_full += clock64() - tw;
                     }
-                    const long long tc = clock64();
                     // ---- this lane's run: its grid estimate and its increments on two grids
                     GridAcc acc{0.0f, 0.0f, false, false};
                     bool live = false;
@@ -2595,7 +2590,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         const bool any0 = __any_sync(0xFFFFFFFFu, live && acc.sp0);
                         const bool any1 = __any_sync(0xFFFFFFFFu, live && acc.sp1);
                         // ---- chain step: wait for the exact sum before this tile
-                        const long long tb0 = clock64();
                         // Lane 0 alone takes a step that is one add (the common case) and hands
                         // the baton on at once; the warp joins only for a walk over the runs.
                         float Sx = 0.0f;
@@ -2626,7 +2620,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                         }
                         done = __shfl_sync(0xFFFFFFFFu, done, 0);
                         Sx = __shfl_sync(0xFFFFFFFFu, Sx, 0);
-                        const long long tb1 = clock64();
                         if (lane == 0 && !done && unit_exp(Sx) < ulo) sh.misc[7] = 1u;  // estimate bound broken
                         const bool walked = !done;
                         uint32_t p = 0;
@@ -2703,8 +2696,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             sh.bseq = nx;
                             if (nx < g.nchunks) mbar_arrive(&sh.bwait[nx % kWarps]);  // (release)
                         }
-                        acc_baton += tb1 - tb0;
-                        acc_chain += clock64() - tb1 + (tb0 - tc);
                     }
                     if (dense) {
                         __syncwarp();
@@ -2805,9 +2796,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             inf.token = token;
             inf.prob = prob;
             inf.events = sh.events;
-            inf.cycles[4] = sat32(acc_full);
-            inf.cycles[5] = sat32(acc_baton);
-            inf.cycles[6] = sat32(acc_chain);
             inf.cycles[7] = sat32(acc_sort);
             if (status == LRS_OK && advance_state) a.state[r] = st;
             a.tokens[r] = token;
