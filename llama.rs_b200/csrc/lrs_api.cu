@@ -50,6 +50,7 @@ struct lrs_ctx {
     uint32_t* d_hist_len = nullptr;
     unsigned long long* d_exp_index = nullptr;
     uint2* d_exp_entries = nullptr;
+    float exp_near = 0.5f;
     unsigned long long* d_scratch = nullptr;
     uint64_t scratch_stride = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0, lists_off = 0;
     uint32_t scratch_ctas = 0;
@@ -146,6 +147,7 @@ static int load_exp_table(lrs_ctx* ctx) {
     CK(cudaMemcpy(ctx->d_exp_index, index.data(), index.size() * sizeof(unsigned long long),
                   cudaMemcpyHostToDevice));
     CK(cudaMemcpy(ctx->d_exp_entries, ent.data(), ent.size() * sizeof(uint2), cudaMemcpyHostToDevice));
+    ctx->exp_near = lrs_exp_near(ent.data(), ent.size());
     return LRS_OK;
 }
 
@@ -358,6 +360,7 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.info = d_info;
     args.exp_index = ctx->d_exp_index;
     args.exp_entries = ctx->d_exp_entries;
+    args.exp_near = ctx->exp_near;
     args.scratch = ctx->d_scratch;
     args.scratch_stride = ctx->scratch_stride;
     args.bitmap_off = ctx->bitmap_off;

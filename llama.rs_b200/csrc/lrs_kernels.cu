@@ -1827,7 +1827,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
     // the max of its run's scaled logits
     float* lrec = reinterpret_cast<float*>(scratch + a.lanes_off);
     uint2* lists = reinterpret_cast<uint2*>(scratch + a.lists_off);  // per warp: sparse tiles' candidates
-    const ExpTable exptab{a.exp_index, a.exp_entries};
+    const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
     const float kInf = __int_as_float(0x7F800000);
     const int tid = threadIdx.x;
     const int lane = tid & 31;

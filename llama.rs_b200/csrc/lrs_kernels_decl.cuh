@@ -3,7 +3,9 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <cstdint>
+#include <cstring>
 
 #include "../../include/llamars_sampler.h"
 
@@ -25,6 +27,7 @@ struct lrs_kernel_args_t {
     lrs_row_info* info;       // nullable
     const unsigned long long* exp_index;  // libm expf exception table (see lrs_device.cuh)
     const uint2* exp_entries;
+    float exp_near;           // every table entry lies within this many float ulps of a rounding midpoint
     unsigned long long* scratch;          // per CTA: scratch_stride 8-byte words
     uint64_t scratch_stride;              // laid out by lrs_kernel_scratch_layout
     uint64_t bitmap_off;                  // window bitmap (zero between rows)
@@ -34,6 +37,27 @@ struct lrs_kernel_args_t {
     uint32_t* row_counter;    // kLrsRowCounters row counters (one per claim class), zeroed before each launch
     int32_t* err_flag;        // sticky error word
 };
+
+// Largest distance (in float ulps, plus a margin for the difference between two
+// double-precision exps) of a libm-expf table entry from the rounding midpoint next to
+// its exact value: an input farther than this from every midpoint has no entry, so
+// libm's value there is the correctly rounded one.  Computed by the loaders from the
+// entries with this machine's double exp.
+inline float lrs_exp_near(const uint2* ent, size_t n) {
+    double m = 0x1p-16;  // (the generator's near-midpoint entries lie within 2^-16)
+    for (size_t i = 0; i < n; ++i) {
+        float x;
+        memcpy(&x, &ent[i].x, 4);
+        const double d = exp((double)x);
+        const float c = (float)d;
+        if (!(c >= 0x1p-126f)) continue;  // (subnormal results always take the table)
+        float nb = d >= (double)c ? nextafterf(c, INFINITY) : nextafterf(c, 0.0f);
+        const double u = fabs((double)nb - (double)c);
+        const double dist = 0.5 - fabs(d - (double)c) / u;
+        if (dist > m) m = dist;
+    }
+    return (float)(m + 0x1p-20);
+}
 
 size_t lrs_kernel_smem_bytes();   // dynamic shared memory of a CTA (independent of n)
 int lrs_kernel_block_threads();

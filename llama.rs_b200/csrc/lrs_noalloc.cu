@@ -57,6 +57,7 @@ std::mutex g_setup_lock;
 uint2 h_entries[kMaxTableEntries];
 unsigned long long h_index[lrs::kExpIndexWords];
 uint32_t h_count = 0;
+float h_near = 0.5f;  // lrs_exp_near of the table
 bool h_loaded = false;
 
 int load_table_once() {
@@ -101,6 +102,7 @@ int load_table_once() {
     }
     if (j != hdr[0]) return LRS_E_INVALID;
     h_count = hdr[0];
+    h_near = lrs_exp_near(h_entries, h_count);
     h_loaded = true;
     return LRS_OK;
 }
@@ -178,6 +180,7 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.info = nullptr;
         args.exp_index = s.index;
         args.exp_entries = s.entries;
+        args.exp_near = h_near;
         args.scratch = s.scratch;
         args.scratch_stride = per_cta;
         args.bitmap_off = bitmap_off;
