@@ -980,15 +980,13 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
                                               const ExpTable tab) {
     bool ex = d == 0.0f;
     float e = ex ? 1.0f : expf(d);
-    // An element of a quarter of bm (2^21 units) or more flags its grid without its
-    // libm value: it is summed element by element anyway if its run lands there.
-    const bool big0 = e >= __fmul_rn(bm0, 0.25f), big1 = e >= __fmul_rn(bm1, 0.25f);
     float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm
     float i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
     if (!ex) {
         const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
-        const bool amb = e < 7.8886091e-31f || (!big0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
-                         (!big1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
+        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol || fabsf(__fsub_rn(e, bm1)) <= tol ||
+                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol)) ||
+                         (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
         if (amb) {
             e = exact_expf(d, tab);
             ex = true;
@@ -996,13 +994,13 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
             i1 = __fsub_rn(__fadd_rn(bm1, e), bm1);
         }
     }
-    if (big0 || e >= bm0) {
+    if (e >= bm0) {
         g.sp0 = true;
     } else {
         g.s0 += i0;
         if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) g.sp0 = true;
     }
-    if (big1 || e >= bm1) {
+    if (e >= bm1) {
         g.sp1 = true;
     } else {
         g.s1 += i1;
@@ -1016,18 +1014,18 @@ __device__ __forceinline__ void classify_elem(float d, float bm0, float bm1, flo
 __device__ __forceinline__ void classify_elem1(float d, float bm0, float h0, GridAcc& g, const ExpTable tab) {
     bool ex = d == 0.0f;
     float e = ex ? 1.0f : expf(d);
-    const bool big0 = e >= __fmul_rn(bm0, 0.25f);
     float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
     if (!ex) {
         const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
-        const bool amb = e < 7.8886091e-31f || (!big0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
+        const bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
+                         (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
         if (amb) {
             e = exact_expf(d, tab);
             ex = true;
             i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
         }
     }
-    if (big0 || e >= bm0) {
+    if (e >= bm0) {
         g.sp0 = true;
     } else {
         g.s0 += i0;
@@ -1042,13 +1040,13 @@ __device__ __forceinline__ void classify_pair1(float da, float db, bool vb, floa
     bool exa = da == 0.0f, exb = db == 0.0f;
     float ea = exa ? 1.0f : expf(da);
     float eb = exb ? 1.0f : expf(db);
-    const float q = __fmul_rn(bm0, 0.25f);
-    const bool biga = ea >= q, bigb = eb >= q;
     float ia = __fsub_rn(__fadd_rn(bm0, ea), bm0);
     float ib = __fsub_rn(__fadd_rn(bm0, eb), bm0);
     const float ta = __fmul_rn(ea, 4.76837158203125e-07f), tb = __fmul_rn(eb, 4.76837158203125e-07f);
-    const bool amba = !exa && (ea < 7.8886091e-31f || (!biga && fabsf(__fsub_rn(ea, ia)) >= __fsub_rn(h0, ta)));
-    const bool ambb = vb && !exb && (eb < 7.8886091e-31f || (!bigb && fabsf(__fsub_rn(eb, ib)) >= __fsub_rn(h0, tb)));
+    const bool amba = !exa && (ea < 7.8886091e-31f || fabsf(__fsub_rn(ea, bm0)) <= ta ||
+                               (ea < bm0 && fabsf(__fsub_rn(ea, ia)) >= __fsub_rn(h0, ta)));
+    const bool ambb = vb && !exb && (eb < 7.8886091e-31f || fabsf(__fsub_rn(eb, bm0)) <= tb ||
+                                     (eb < bm0 && fabsf(__fsub_rn(eb, ib)) >= __fsub_rn(h0, tb)));
     if (amba || ambb) {
         if (amba) {
             ea = exact_expf(da, tab);
@@ -1061,14 +1059,14 @@ __device__ __forceinline__ void classify_pair1(float da, float db, bool vb, floa
             ib = __fsub_rn(__fadd_rn(bm0, eb), bm0);
         }
     }
-    if (biga || ea >= bm0) {
+    if (ea >= bm0) {
         g.sp0 = true;
     } else {
         g.s0 += ia;
         if (exa && h0 > 0.0f && fabsf(__fsub_rn(ea, ia)) == h0) g.sp0 = true;
     }
     if (vb) {
-        if (bigb || eb >= bm0) {
+        if (eb >= bm0) {
             g.sp0 = true;
         } else {
             g.s0 += ib;
