@@ -18,6 +18,10 @@ cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of 
            N ranks; a step is the exchange (NCCL all-gather of the shards + row assembly) and
            the sampling of every row on every rank; reports latency, the exchange's share and
            a check of the tokens against an unsharded sample
+--workload configs  one GPU, the other configurations of the benchmark at their sizes: config 1
+           (one row: latency of a draw through the drop-in single-row API, and 10,000 draws as
+           rows sharing the logits), config 2 (greedy), config 3 (mixed, 109,051 wide), config 4
+           (nucleus stress, 4096 rows, window 1024); rows/s and the roofline fraction of each
 """
 from __future__ import annotations
 
@@ -257,6 +261,87 @@ def run_vocab_sharded(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_configs(args):
+    """The benchmark's configurations 1-4 on one GPU (auxiliary to the headline line)."""
+    import torch
+    import lrs
+    from lrs import workloads as W
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peak, _ = peaks()
+    out = {"metric": "configs 1-4 of the benchmark (auxiliary)", "n_gpus": 1, "data": "synthetic", "configs": {}}
+
+    def device_rate(w, shared_row=False, reps=None):
+        rows = len(w.params)
+        bs = lrs.BatchSampler(rows, w.vocab, max(w.window, 1))
+        # (shared_row: every row reads logits row 0, ld = 0)
+        x = torch.from_numpy(w.logits).to(dev)
+        hist = torch.from_numpy(w.hist.view(np.int32)).to(dev) if w.window else None
+        hlen = torch.from_numpy(w.hist_len.view(np.int32)).to(dev) if w.window else None
+        params = torch.from_numpy(w.params.view(np.uint8)).to(dev)
+        state = torch.from_numpy(w.state.view(np.int64)).to(dev)
+        tokens = torch.zeros(rows, dtype=torch.int32, device=dev)
+        status = torch.zeros(rows, dtype=torch.int32, device=dev)
+        ld = 0 if shared_row else None
+
+        def step():
+            bs.sample_device(x, params, state, tokens, n=w.vocab, hist=hist, hist_len=hlen, status=status, ld=ld,
+                             rows=rows)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        if int((status != 0).sum()):
+            raise SystemExit("a row reported a non-zero status")
+        k = reps or max(3, args.steps // 2)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / k
+        bs.close()
+        row_bytes = 4 * w.vocab * (0 if shared_row else 1) + 4 * w.window
+        frac = (rows * row_bytes / (ms / 1e3) / 1e9) / peak if row_bytes else None
+        return {"rows": rows, "vocab": w.vocab, "window": w.window, "ms_per_step": ms,
+                "rows_per_s": rows / (ms / 1e3), "roofline_frac": frac}
+
+    c = out["configs"]
+    c["config2_greedy"] = device_rate(W.greedy())
+    c["config3_mixed"] = device_rate(W.mixed())
+    c["config4_nucleus"] = device_rate(W.nucleus(), reps=3)
+    # config 1: 10,000 draws on one row's logits and history (per-draw PRNG states)
+    w1 = W.single(1)
+    draws = 10000
+
+    class Draws:  # one logits row, `draws` rows of parameters, history and PRNG states
+        vocab, window = w1.vocab, w1.window
+        logits = w1.logits[:1]
+        params = np.repeat(w1.params, draws)
+        hist = np.repeat(w1.hist, draws, axis=0)
+        hist_len = np.repeat(w1.hist_len, draws)
+        state = W.xorshift_states(int(w1.state[0]), draws)
+
+    c["config1_batched_draws"] = device_rate(Draws, shared_row=True, reps=5)
+    # config 1: one draw at a time through the drop-in Sampler (host logits, synchronous)
+    s = lrs.Sampler(42)
+    sp = lrs.SamplingParams(temperature=float(w1.params["temperature"][0]), top_k=int(w1.params["top_k"][0]),
+                            top_p=float(w1.params["top_p"][0]),
+                            repetition_penalty=float(w1.params["repetition_penalty"][0]),
+                            repeat_last_n=int(w1.params["repeat_last_n"][0]), seed=42)
+    recent = w1.hist[0, :int(w1.hist_len[0])]
+    for _ in range(5):
+        s.sample(w1.logits[0], sp, recent)
+    n1 = 200
+    t = time.perf_counter()
+    for _ in range(n1):
+        s.sample(w1.logits[0], sp, recent)
+    us = (time.perf_counter() - t) / n1 * 1e6
+    c["config1_single_draw"] = {"us_per_draw": us, "api": "lrs_sampler_sample (host logits, synchronous)"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -268,7 +353,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=256)
     ap.add_argument("--ref-rows", type=int, default=128)
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
-    ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded"])
+    ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded", "configs"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
@@ -276,6 +361,10 @@ def main():
         return
     if args.workload == "vocab_sharded":
         run_vocab_sharded(args, world, rank, local)
+        return
+    if args.workload == "configs":
+        if rank == 0:
+            run_configs(args)
         return
 
     import torch
