@@ -94,3 +94,40 @@ def test_expf_table_matches_this_libm(built_lib):
             continue
         cr = np.float32(np.exp(np.float64(x)))
         assert np.float32(libm.expf(float(x))) == cr
+
+
+def _midpoint_distance(x32):
+    """Distance (float ulps) of exp(x) from the rounding midpoint next to it, as the
+    loaders compute it (host double exp)."""
+    d = np.exp(x32.astype(np.float64))
+    c = d.astype(np.float32)
+    up = d >= c.astype(np.float64)
+    nb = np.where(up, np.nextafter(c, np.float32(np.inf)), np.nextafter(c, np.float32(0)))
+    u = np.abs(nb.astype(np.float64) - c.astype(np.float64))
+    return 0.5 - np.abs(d - c.astype(np.float64)) / u, c
+
+
+def test_expf_entries_lie_near_midpoints():
+    """The kernel answers an input without the table when its exp lies farther from a
+    rounding midpoint than every table entry does; check that premise on this libm: the
+    entries' largest distance is small, and sampled inputs farther than it have libm's
+    value equal to the correctly rounded one."""
+    from lrs import build
+    raw = open(build.TABLE, "rb").read()
+    ent = np.frombuffer(raw[20:], np.uint32).reshape(-1, 2)
+    x = ent[:, 0].view(np.float32)
+    dist, c = _midpoint_distance(x)
+    normal = c >= np.float32(2.0 ** -126)
+    near = max(float(dist[normal].max()), 2.0 ** -16) + 2.0 ** -20
+    assert near < 2.0 ** -8  # (0.0016 ulp for glibc 2.39)
+    libm = ctypes.CDLL("libm.so.6")
+    libm.expf.restype = ctypes.c_float
+    libm.expf.argtypes = [ctypes.c_float]
+    rng = np.random.default_rng(1)
+    probe = (-rng.random(40000) * 104).astype(np.float32)
+    pd, pc = _midpoint_distance(probe)
+    normal_p = pc >= np.float32(2.0 ** -126)
+    far = (pd > near) & normal_p
+    assert far.sum() > 0.99 * normal_p.sum()  # (subnormal results always take the table)
+    got = np.array([libm.expf(float(v)) for v in probe[far]], np.float32)
+    np.testing.assert_array_equal(got.view(np.uint32), pc[far].view(np.uint32))
