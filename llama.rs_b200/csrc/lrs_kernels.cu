@@ -582,11 +582,19 @@ __device__ __noinline__ int tile2(float (&v)[kVpt], uint32_t& exact, int start, 
 // Returns the stop position or -1 (sampler.rs:137-139, 148-151, 156-158).
 __device__ __forceinline__ int serial_run(const float* vals, int cnt, int dir, float& s, float thr) {
     float cur = s;
-    for (int i = 0; i < cnt; ++i) {
-        cur = dir > 0 ? __fadd_rn(cur, vals[i]) : __fsub_rn(cur, vals[i]);
-        if (dir > 0 ? cur >= thr : cur <= 0.0f) {
-            s = cur;
-            return i;
+    // eight values loaded at a time (the loads do not wait for the sum)
+    for (int i0 = 0; i0 < cnt; i0 += 8) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = i0 + j < cnt ? vals[i0 + j] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            if (i0 + j >= cnt) break;
+            cur = dir > 0 ? __fadd_rn(cur, v[j]) : __fsub_rn(cur, v[j]);
+            if (dir > 0 ? cur >= thr : cur <= 0.0f) {
+                s = cur;
+                return i0 + j;
+            }
         }
     }
     s = cur;
@@ -901,7 +909,14 @@ __device__ __noinline__ float warp_serial_add(float s, float e, float d, bool ex
         }
         if (amb) e = exact_expf(d, tab);
     }
-    for (int j = lo; j < lo + cnt; ++j) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e, j));
+    // (unrolled over all 32 lanes: the shuffles do not wait for the sum, only the adds
+    // form the serial chain)
+    const int hi = lo + cnt;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const float v = __shfl_sync(0xFFFFFFFFu, e, j);
+        if (j >= lo && j < hi) s = __fadd_rn(s, v);
+    }
     return s;
 }
 
