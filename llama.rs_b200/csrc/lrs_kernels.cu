@@ -2030,6 +2030,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 }
             }
             uint32_t bits_nx = (uint32_t)warp < g.nchunks ? tile_bits((uint32_t)warp) : 0u;
+            const float2 it2 = make_float2(inv_t, inv_t);
             for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
                 const uint32_t qq = q1 + t, s = qq % kSlots;
                 const uint32_t cnt = chunk_count(g, t);
@@ -2041,22 +2042,20 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 // candidate threshold from a lower bound of the max before this tile
                 float cthr = -kInf;
                 if (lists_on) {
-                    // fold in the published maxima of earlier tiles: one batch of up to eight
-                    // (max, tag) words a tile (seven tiles pass between a warp's tiles)
+                    // fold in the published maxima of earlier tiles: lane u reads the (max, tag)
+                    // word of tile front + u, and the leading run of published ones is folded
                     {
-                        const uint32_t nb = min(8u, t - front);
-                        unsigned long long w[8];
-#pragma unroll
-                        for (uint32_t u = 0; u < 8u; ++u)
-                            w[u] = u < nb ? *reinterpret_cast<volatile unsigned long long*>(&tt[front + u].mt) : 0ull;
-                        uint32_t adv = 0;
-#pragma unroll
-                        for (uint32_t u = 0; u < 8u; ++u)
-                            if (adv == u && u < nb && (uint32_t)(w[u] >> 32) == r) {
-                                gpm = fmax_nan(gpm, __uint_as_float((uint32_t)w[u]));
-                                adv = u + 1u;
-                            }
-                        front += adv;
+                        const uint32_t nb = min(32u, t - front);
+                        unsigned long long w = 0ull;
+                        if ((uint32_t)lane < nb) w = *reinterpret_cast<volatile unsigned long long*>(&tt[front + lane].mt);
+                        const unsigned pub = __ballot_sync(0xFFFFFFFFu, (uint32_t)lane < nb && (uint32_t)(w >> 32) == r);
+                        const uint32_t adv = (uint32_t)__clz(__brev(~pub));
+                        if (adv != 0u) {
+                            const float v = (uint32_t)lane < adv ? __uint_as_float((uint32_t)w) : -kInf;
+                            const float vm = fkey_inv(__reduce_max_sync(0xFFFFFFFFu, fkey(v)));
+                            gpm = __any_sync(0xFFFFFFFFu, v != v) ? __uint_as_float(0x7FC00000u) : fmax_nan(gpm, vm);
+                            front += adv;
+                        }
                     }
                     const float mp = fmax_nan(m_w, gpm);
                     cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
@@ -2106,18 +2105,53 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     *px = penalise(*px, penalty);
                 }
                 const uint32_t bits1 = 0u;  // (pass 1 from here on: already applied)
-#pragma unroll 4
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
-                    if (c4 >= nval) continue;
-                    const float4 q = *reinterpret_cast<const float4*>(slot + c4);
-                    const float x[4] = {q.x, q.y, q.z, q.w};
+                if (nval == 32u) {
+                    // a full run: its max first (packed products, three-input maxima), the
+                    // candidate and top-k masks only in lanes whose max reaches a threshold.
+                    // The packed products are only compared here: the compiler may fuse a
+                    // packed product into a following add even when both are written with
+                    // explicit rounding, so every difference of a product (x inv_t - max)
+                    // is computed from a scalar __fmul_rn product
+                    float ma = -kInf, mb = -kInf;
 #pragma unroll
-                    for (int c = 0; c < 4; ++c) {
-                        const float xs = __fmul_rn(x[c], inv_t);
-                        ml = fmax_nan(ml, xs);
-                        if (xs >= cthr) cmask |= 1u << (c4 + c);
-                        if (xs >= theta) hmask |= 1u << (c4 + c);
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                        const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                        const float2 lo = __fmul2_rn(make_float2(q.x, q.y), it2);
+                        const float2 hi = __fmul2_rn(make_float2(q.z, q.w), it2);
+                        ma = fmax3_nan(ma, lo.x, lo.y);
+                        mb = fmax3_nan(mb, hi.x, hi.y);
+                    }
+                    ml = fmax_nan(ma, mb);
+                    if (ml >= cthr || ml >= theta) {
+#pragma unroll 4
+                        for (int j = 0; j < 8; ++j) {
+                            const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                            const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                            const float2 lo = __fmul2_rn(make_float2(q.x, q.y), it2);
+                            const float2 hi = __fmul2_rn(make_float2(q.z, q.w), it2);
+                            const float xs[4] = {lo.x, lo.y, hi.x, hi.y};
+#pragma unroll
+                            for (int c = 0; c < 4; ++c) {
+                                if (xs[c] >= cthr) cmask |= 1u << (c4 + c);
+                                if (xs[c] >= theta) hmask |= 1u << (c4 + c);
+                            }
+                        }
+                    }
+                } else {
+#pragma unroll 4
+                    for (int j = 0; j < 8; ++j) {
+                        const uint32_t c4 = (uint32_t)((j + lane) & 7) * 4u;
+                        if (c4 >= nval) continue;
+                        const float4 q = *reinterpret_cast<const float4*>(slot + c4);
+                        const float x[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                        for (int c = 0; c < 4; ++c) {
+                            const float xs = __fmul_rn(x[c], inv_t);
+                            ml = fmax_nan(ml, xs);
+                            if (xs >= cthr) cmask |= 1u << (c4 + c);
+                            if (xs >= theta) hmask |= 1u << (c4 + c);
+                        }
                     }
                 }
                 const float mt = warp_max_nan(ml);
@@ -2451,7 +2485,6 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     const float xthr = sum_live ? sh.xthr[ulo + kUBase] : kInf;
                     const float ptile = tt[t].pt;
                     const uint32_t lcnt = dense ? 0u : tt[t].lcnt;
-                    const uint2* ent = lists + (dense ? 0u : tt[t].loff);
                     uint32_t s = 0;
                     const float* slot = ring;
                     if (dense) {
