@@ -142,6 +142,8 @@ struct RowShared {
     lrs_row_info info;     // the row's diagnostics, assembled by thread 0
     uint32_t dense[kMaxTiles / 32];  // pass 1: tiles streamed again in pass 2 (read by the producer)
     volatile uint32_t p1done;        // pass-1 tiles of two-pass rows finished by this CTA (monotone)
+    volatile uint32_t claim_ok;      // rows taken by the consumers after which the producer may
+                                     // claim the next one (monotone)
     uint32_t ndense;                 // dense tiles of the current row
     uint32_t bsorted[(kNB + 31) / 32];  // path N: buckets in exact sorted order
 };
@@ -282,6 +284,22 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
             for (uint32_t c = 0; c < g.nchunks && ok; ++c)
                 if ((sh.dense[c >> 5] >> (c & 31)) & 1u) ok = issue(g, c, pol_drop);
             if (!ok) break;
+        }
+        if (passes == 2) {
+            // A two-pass row can run long after its last load (pass 2, a long finish): the
+            // next row is claimed only once the consumers say the row is nearly done, so
+            // that a CTA still busy with a long row leaves the remaining rows to others.
+            const long long t0 = clock64();
+            while ((int)(sh.claim_ok - rqi) < 0) {
+                if (sh.abort) break;
+                if (clock64() - t0 > kWaitCycles) {
+                    sh.abort = 1u;
+                    atomicExch(a.err_flag, LRS_E_TIMEOUT);
+                    break;
+                }
+                __nanosleep(256);
+            }
+            if (sh.abort) break;
         }
     }
     // Leave no copy in flight behind: wait (bounded, ignoring the abort flag) for the
@@ -1859,6 +1877,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
         sh.abort = 0u;
         sh.bseq = 0xFFFFFFFFu;
         sh.p1done = 0u;
+        sh.claim_ok = 0u;
         fence_barrier_init();
     }
     __syncthreads();
@@ -2452,15 +2471,17 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 // loads of tile t's per-lane inputs, issued one tile ahead of their use
                 auto prefetch = [&](uint32_t t) {
                     // dense tiles: penalty bits and lane sums; sparse tiles: the list entries
-                    const uint32_t lc = tt[t].lcnt, e0 = (uint32_t)lane * kRunS;
+                    // (runs of ceil(entries / 32) <= kRunS entries, spread over the lanes)
+                    const uint32_t lc = tt[t].lcnt;
                     const bool dn = lc == kDenseMark;
+                    const uint32_t rs = dn ? 0u : (lc + 31u) >> 5, e0 = (uint32_t)lane * rs;
                     bits_nx = dn ? tile_bits(t) : 0u;
                     lr_nx = dn ? __ldcg(lrec + t * 64u + (uint32_t)lane) : 0.0f;
                     const bool want = !bad && lc != kDenseMark && (tt[t].flags & (kSumLive | kHistLive));
                     const uint2* en = lists + tt[t].loff;
 #pragma unroll
                     for (int i = 0; i < kRunS; ++i)
-                        xs_nx[i] = (want && e0 + (uint32_t)i < lc) ? __uint_as_float(__ldcg(&en[e0 + i].x)) : -kInf;
+                        xs_nx[i] = (want && (uint32_t)i < rs && e0 + (uint32_t)i < lc) ? __uint_as_float(__ldcg(&en[e0 + i].x)) : -kInf;
                     i0_nx = (want && e0 < lc) ? __ldcg(&en[e0].y) : 0u;
                 };
                 if ((uint32_t)warp < g.nchunks) prefetch((uint32_t)warp);
@@ -2485,6 +2506,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                     const float xthr = sum_live ? sh.xthr[ulo + kUBase] : kInf;
                     const float ptile = tt[t].pt;
                     const uint32_t lcnt = dense ? 0u : tt[t].lcnt;
+                    const uint32_t rs = (lcnt + 31u) >> 5;  // list entries per lane run (sparse)
                     uint32_t s = 0;
                     const float* slot = ring;
                     if (dense) {
@@ -2574,14 +2596,15 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             }
                         }
                     } else {
-                        // run = kRunS consecutive list entries of the sparse tile
-                        const uint32_t e0 = (uint32_t)lane * kRunS;
+                        // run = rs consecutive list entries of the sparse tile (rs = ceil(lcnt / 32)
+                        // <= kRunS: the live entries spread over as many lanes as there are)
+                        const uint32_t e0 = (uint32_t)lane * rs;
                         float dv[kRunS];
                         float lsum = 0.0f;
 #pragma unroll
                         for (int i = 0; i < kRunS; ++i) {
                             dv[i] = -kInf;
-                            if (e0 + (uint32_t)i < lcnt) {
+                            if ((uint32_t)i < rs && e0 + (uint32_t)i < lcnt) {
                                 const float d = __fsub_rn(xsv[i], mx);
                                 if (hl && d >= hist_lim) atomicAdd(&hcnt[(int)fminf(-d * kBScale, (float)(kNB - 1))], 1u);
                                 if (sum_live && d >= thr_d) {
@@ -2715,9 +2738,9 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                                     }
                                 }
                             } else {
-                                len = kRunS;
+                                len = (int)rs;
                                 // run L's entries (lane L's prefetched scaled logits, -inf
-                                // where absent) to lanes 0 .. kRunS-1
+                                // where absent) to lanes 0 .. rs-1
                                 float xl = -kInf;
 #pragma unroll
                                 for (int i = 0; i < kRunS; ++i) {
@@ -2774,6 +2797,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             }
             if (tid == 0) inf.sum_exp = S;
             lap(2);
+            if (tid == 0 && pathK) sh.claim_ok = rqi;  // a short finish remains: the producer may claim
             if (bad) {
                 status = LRS_E_NAN;
                 token = LRS_TOKEN_NONE;
@@ -2838,6 +2862,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
         if (sh.misc[7]) status = LRS_E_INTERNAL;
         if (sh.abort) status = LRS_E_TIMEOUT;
         if (tid == 0) {
+            sh.claim_ok = rqi;
             inf.status = status;
             inf.token = token;
             inf.prob = prob;
