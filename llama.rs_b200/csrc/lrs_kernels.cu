@@ -59,10 +59,13 @@ constexpr int kNB = 580;             // path N buckets of width 1/32 in (max - x
 constexpr float kBScale = 32.0f;
 constexpr int kSortCap = 4096;       // largest bucket sorted in shared memory
 constexpr uint32_t kGatherItemsOff = 1024;  // path-N gather: per-warp item lists, in 32-bit words after the cursors
-constexpr float kTopPMargin = 0.002f;
+constexpr float kTopPMargin = 0.002f;     // first-gather limit: head mass reached by (top_p + this) S
+constexpr float kTailMargin = 4.8828125e-04f;  // ... or tail mass at most (1 - top_p - this) S (2^-11:
+                                           // the f32 rounding of a cumulative sum of a few thousand terms)
 constexpr int kSerial = 512;         // elements summed one by one at the start of a scan
 constexpr int kTilesSmem = 256;      // tile records kept in shared memory (larger rows: global)
 constexpr int kMaxTiles = 4096;      // tiles of the longest row (n <= 2^22)
+constexpr int kGatherRuns = 48;      // path-N gather: dense runs a warp stages at a time
 constexpr int kDense = 256;          // a tile with more candidates is streamed again in pass 2
 constexpr int kRunS = kDense / 32;   // list entries per lane run of a sparse tile
 constexpr uint32_t kDenseMark = 0xFFFFFFFFu;  // TileRec::lcnt of a dense tile
@@ -88,6 +91,7 @@ static_assert(kRegionBBytes >= (size_t)kWarps * 256 * 4, "per-warp radix counts"
 static_assert(kRegionBBytes >= (size_t)kNB * 4, "bucket cursors");
 static_assert(kRegionBBytes >= ((size_t)kGatherItemsOff + (size_t)kWarps * 1024) * 4, "gather item lists");
 static_assert((size_t)kNB <= (size_t)kGatherItemsOff, "bucket cursors before the gather item lists");
+static_assert((size_t)kWarps * kGatherRuns * 32 * 4 <= kRingBytes, "gather staging areas in the ring");
 static_assert((size_t)kKCap * 8 + (size_t)kWarps * 32 * kRunS * 4 <= (size_t)kRegionBBytes, "pass-2 live list values");
 
 using SampleArgs = lrs_kernel_args_t;
@@ -111,6 +115,8 @@ struct RowShared {
     uint64_t rq_full[kRowQ];
     uint64_t rq_empty[kRowQ];
     uint64_t bwait[kWarps];    // baton: one phase per hand-over to warp w (its next chain step)
+    uint64_t gbar[kWarps];     // path-N gather: bulk copies into warp w's staging area
+    uint32_t gph[kWarps];      // ... and the phase warp w waits for next
     uint32_t rq_row[kRowQ];
     volatile uint32_t abort;   // a wait ran out: every later wait returns at once
     volatile uint32_t bseq;    // baton: the tile whose chain step may run
@@ -1229,6 +1235,8 @@ struct FinishCtx {
     uint32_t* hoff;
     uint32_t* cursor;
     unsigned long long* sbuf;       // path N: bucket sort buffer (aliases cursor)
+    float* ring;                    // path N: the (idle) ring, staging area of the gather
+    int32_t* err;                   // sticky error word (bounded waits)
     float* cand_x;                  // path K: candidates and sort keys
     uint32_t* cand_i;
     unsigned long long* keys;
@@ -1314,6 +1322,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     uint32_t* const hoff = f.hoff;
     uint32_t* const cursor = f.cursor;
     unsigned long long* const sbuf = f.sbuf;
+    float* const ring = f.ring;
+    int32_t* const err = f.err;
     const ExpTable exptab = f.exptab;
     const uint32_t k = f.k;
     const float mx = f.mx, inv_t = f.inv_t, inv = f.inv, S = f.S, penalty = f.penalty, top_p = f.top_p;
@@ -1339,7 +1349,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         // scan ends (once the top-p sum is at least 1/2 nothing after it changes the
         // sum).  One warp, 32 buckets a step.
         const double target = topp_on ? ((double)top_p + kTopPMargin) * (double)S : 1e300;
-        const double tail_target = topp_on ? (1.0 - (double)top_p - kTopPMargin) * (double)S : -1.0;
+        const double tail_target = topp_on ? (1.0 - (double)top_p - kTailMargin) * (double)S : -1.0;
         const double exit_e = 1.4901161193847656e-08 * (double)S;
         const double elane = exp(-(double)(lane + 1) / (double)kBScale) * (1.0 - 1e-12);  // (low: a lower bound)
         const double ewidth = exp(1.0 / (double)kBScale) * (1.0 + 1e-9);  // upper / lower bound of a bucket
@@ -1406,6 +1416,8 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
     // max lies below the range are skipped
     auto gather = [&](uint32_t blo, uint32_t bhi) {
         const bool all = bhi == (uint32_t)kNB - 1;
+        uint32_t gph = sh.gph[warp];  // (the warp's staging barrier phase)
+        bool gdead = false;           // a staging wait ran out after an abort: wait no more
         const float dlim = -(float)(bhi + 1) / kBScale;
         for (uint32_t q = blo + tid; q <= bhi; q += kThreads) cursor[q] = 0;
         csync();
@@ -1417,17 +1429,12 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                 b = dd >= hist_lim ? (int)fminf(-dd * kBScale, (float)(kNB - 1)) : kNB - 1;
                 tk = (uint32_t)b >= blo && (uint32_t)b <= bhi;
             }
-            const unsigned act = __ballot_sync(0xFFFFFFFFu, tk);
             if (tk) {
-                // CUDA's expf (within 2 ulp): keys are exactified before a bucket is ordered
+                // CUDA's expf (within 2 ulp): keys are exactified before a bucket is ordered.
+                // A bucket's storage order is free (it is sorted where the order matters).
                 const float e = dd == 0.0f ? 1.0f : expf(dd);
                 const float pr = __fmul_rn(e, inv);
-                const unsigned peers = __match_any_sync(act, b);
-                const int leader = __ffs(peers) - 1;
-                uint32_t base = 0;
-                if (lane == leader) base = atomicAdd(&cursor[b], (uint32_t)__popc(peers));
-                base = __shfl_sync(peers, base, leader);
-                const uint32_t slot = hoff[b] + base + (uint32_t)__popc(peers & ((1u << lane) - 1u));
+                const uint32_t slot = hoff[b] + atomicAdd(&cursor[b], 1u);
                 scratch[slot] = ((unsigned long long)(~__float_as_uint(pr)) << 32) | i | (dd == 0.0f ? 0u : kApxKey);
             }
         };
@@ -1441,9 +1448,15 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
         // The warp's tiles t = warp + kWarps j, 32 at a time (j in lane bits).  Work items
         // of 32 elements, one per lane: a run of a dense tile whose pass-1 run max
         // reaches the range, or 32 list entries of a sparse tile.  The items are listed
-        // in shared memory (after the bucket cursors), then read eight at a time with
-        // their loads in flight together, across tiles.
+        // in shared memory (after the bucket cursors): dense runs from the front, list
+        // groups from the back (at most 1024 together).  List groups are read eight at
+        // a time with their loads in flight together; dense runs are brought into the
+        // warp's part of the ring by bulk copies, kGatherRuns at a time (the ring is
+        // idle: the producer streams nothing until this row is done).
         uint32_t* items = reinterpret_cast<uint32_t*>(sbuf) + kGatherItemsOff + (uint32_t)warp * 1024u;
+        float* const stage = ring + (size_t)warp * kGatherRuns * 32u;
+        uint64_t* const gbar = &sh.gbar[warp];
+        const uint64_t pol = policy_evict_first();
         const uint32_t ntw = g.nchunks > (uint32_t)warp ? (g.nchunks - (uint32_t)warp + kWarps - 1) / kWarps : 0u;
         for (uint32_t j0 = 0; j0 < ntw; j0 += 32) {
             const uint32_t nj = min(32u, ntw - j0);
@@ -1467,68 +1480,109 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
                     if (lm[u] == kInf || __fsub_rn(lm[u], mx) >= dlim) live |= 1u << (j + (uint32_t)u);
             }
             // item = j << 6 | group << 1 | list
-            uint32_t nit = 0;
+            uint32_t nd = 0, nl = 0;
             for (uint32_t j = 0; j < nj; ++j) {
                 const uint32_t t = (uint32_t)warp + kWarps * (j0 + j);
                 const TileRec& R = tt[t];
                 if (!all && R.lcnt != kDenseMark) {
                     const uint32_t ng = __fsub_rn(R.mt, mx) < dlim ? 0u : (R.lcnt + 31u) / 32u;
-                    if ((uint32_t)lane < ng) items[nit + (uint32_t)lane] = (j << 6) | ((uint32_t)lane << 1) | 1u;
-                    nit += ng;
+                    if ((uint32_t)lane < ng) items[1023u - nl - (uint32_t)lane] = (j << 6) | ((uint32_t)lane << 1) | 1u;
+                    nl += ng;
                 } else {
                     const bool mine = (live >> j) & 1u;
                     const unsigned m = __ballot_sync(0xFFFFFFFFu, mine);
-                    if (mine) items[nit + (uint32_t)__popc(m & ((1u << lane) - 1u))] = (j << 6) | ((uint32_t)lane << 1);
-                    nit += (uint32_t)__popc(m);
+                    if (mine) items[nd + (uint32_t)__popc(m & ((1u << lane) - 1u))] = (j << 6) | ((uint32_t)lane << 1);
+                    nd += (uint32_t)__popc(m);
                 }
             }
             __syncwarp();
-            for (uint32_t k0 = 0; k0 < nit; k0 += 8) {
+            // list groups: the pass-1 lists hold every element of a sparse tile with
+            // d >= hist_lim (scaled, penalised)
+            for (uint32_t k0 = 0; k0 < nl; k0 += 8) {
                 float xs[8];
-                uint32_t gi[8], pw[8];  // gi: element index (~0u: none)
+                uint32_t gi[8];  // element index (~0u: none)
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
                     xs[u] = 0.0f;
                     gi[u] = ~0u;
-                    pw[u] = 0u;
-                    if (k0 + (uint32_t)u >= nit) continue;
-                    const uint32_t itm = items[k0 + (uint32_t)u];
+                    if (k0 + (uint32_t)u >= nl) continue;
+                    const uint32_t itm = items[1023u - k0 - (uint32_t)u];
                     const uint32_t t = (uint32_t)warp + kWarps * (j0 + (itm >> 6));
                     const uint32_t e = ((itm >> 1) & 31u) * 32u + (uint32_t)lane;
-                    if (itm & 1u) {
-                        // sparse tile: its list holds every element with d >= hist_lim
-                        const TileRec& R = tt[t];
-                        if (e < R.lcnt) {
-                            const uint2 en = __ldcg(lists + R.loff + e);
-                            xs[u] = __uint_as_float(en.x);  // (scaled, penalised)
-                            gi[u] = en.y;
-                        }
-                    } else if (e < chunk_count(g, t)) {
-                        gi[u] = g.head + t * kTile + e;
-                        xs[u] = g.row[gi[u]];
-                        if (pen_on) pw[u] = __ldcg(bitmap + (gi[u] >> 5));
+                    const TileRec& R = tt[t];
+                    if (e < R.lcnt) {
+                        const uint2 en = __ldcg(lists + R.loff + e);
+                        xs[u] = __uint_as_float(en.x);
+                        gi[u] = en.y;
                     }
                 }
 #pragma unroll
                 for (int u = 0; u < 8; ++u) {
-                    if (k0 + (uint32_t)u >= nit) break;  // (warp-uniform)
+                    if (k0 + (uint32_t)u >= nl) break;  // (warp-uniform)
                     const bool ok = gi[u] != ~0u;
-                    float dd = -kInf;
-                    if (ok) {
-                        const uint32_t itm = items[k0 + (uint32_t)u];
-                        if (itm & 1u) {
-                            dd = __fsub_rn(xs[u], mx);
-                        } else {
-                            const bool pen = (pw[u] >> (gi[u] & 31u)) & 1u;
-                            dd = d_of(pen ? penalise(xs[u], penalty) : xs[u], inv_t, mx);
-                        }
-                    }
+                    const float dd = ok ? __fsub_rn(xs[u], mx) : -kInf;
                     if (!all && !__any_sync(0xFFFFFFFFu, dd >= dlim)) continue;
                     take(gi[u], dd, ok);
                 }
             }
-            __syncwarp();
+            // dense runs through the staging area
+            for (uint32_t k0 = 0; k0 < nd; k0 += kGatherRuns) {
+                const uint32_t nb = min((uint32_t)kGatherRuns, nd - k0);
+                // run k0 + u: its first element and length (a multiple of 4: 16-byte copies)
+                auto run_of = [&](uint32_t u, uint32_t& e0, uint32_t& len) {
+                    const uint32_t itm = items[k0 + u];
+                    const uint32_t t = (uint32_t)warp + kWarps * (j0 + (itm >> 6));
+                    const uint32_t o = ((itm >> 1) & 31u) * 32u;
+                    e0 = g.head + t * kTile + o;
+                    len = min(32u, chunk_count(g, t) - o);
+                };
+                uint32_t bytes = 0;
+                for (uint32_t u = (uint32_t)lane; u < nb; u += 32) {
+                    uint32_t e0, len;
+                    run_of(u, e0, len);
+                    bytes += len * 4u;
+                }
+                bytes = __reduce_add_sync(0xFFFFFFFFu, bytes);
+                if (lane == 0) {
+                    fence_proxy_async_smem();  // (the warp's earlier reads of the area come first)
+                    mbar_expect_tx(gbar, bytes);
+                }
+                __syncwarp();
+                uint32_t pb0 = 0, pb1 = 0;  // penalty bits of runs lane and lane + 32
+                for (uint32_t u = (uint32_t)lane; u < nb; u += 32) {
+                    uint32_t e0, len;
+                    run_of(u, e0, len);
+                    bulk_load(stage + u * 32u, g.row + e0, len * 4u, gbar, pol);
+                    if (pen_on) (u < 32u ? pb0 : pb1) = lane_bits(bitmap, e0);
+                }
+                if (!wait_bar(sh, gbar, gph & 1u, err) && !gdead) {
+                    // aborted: still let this warp's copies land before going on (once)
+                    const long long t0 = clock64();
+                    while (!mbar_try_wait(gbar, gph & 1u))
+                        if (clock64() - t0 > kWaitCycles) {
+                            gdead = true;
+                            break;
+                        }
+                }
+                ++gph;
+                for (uint32_t u = 0; u < nb; ++u) {
+                    uint32_t e0, len;
+                    run_of(u, e0, len);
+                    const bool ok = (uint32_t)lane < len && !sh.abort;
+                    const uint32_t pb = __shfl_sync(0xFFFFFFFFu, u < 32u ? pb0 : pb1, (int)(u & 31u));  // (all lanes)
+                    float dd = -kInf;
+                    if (ok) {
+                        float x = stage[u * 32u + (uint32_t)lane];
+                        if ((pb >> lane) & 1u) x = penalise(x, penalty);
+                        dd = d_of(x, inv_t, mx);
+                    }
+                    if (!all && !__any_sync(0xFFFFFFFFu, dd >= dlim)) continue;
+                    take(e0 + (uint32_t)lane, dd, ok);
+                }
+                __syncwarp();
+            }
         }
+        if (lane == 0) sh.gph[warp] = gph;
         __threadfence_block();
         csync();
     };
@@ -1873,7 +1927,11 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             mbar_init(&sh.rq_full[i], 1);
             mbar_init(&sh.rq_empty[i], 1);
         }
-        for (int i = 0; i < kWarps; ++i) mbar_init(&sh.bwait[i], 1);
+        for (int i = 0; i < kWarps; ++i) {
+            mbar_init(&sh.bwait[i], 1);
+            mbar_init(&sh.gbar[i], 1);
+            sh.gph[i] = 0u;
+        }
         sh.abort = 0u;
         sh.bseq = 0xFFFFFFFFu;
         sh.p1done = 0u;
@@ -2817,6 +2875,8 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
             fc.hoff = hoff;
             fc.cursor = cursor;
             fc.sbuf = sbuf;
+            fc.ring = ring;
+            fc.err = a.err_flag;
             fc.cand_x = cand_x;
             fc.cand_i = cand_i;
             fc.keys = keys;
