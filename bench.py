@@ -253,7 +253,7 @@ def run_vocab_sharded(args, world, rank, local):
                                    f"({V // world} each), one all-gather per step, top_k 50, top_p 0.95, temp 0.7",
                        "parallelism": f"vocabulary over {world} GPU(s)"},
             "exchange_ms_per_step": exch_ms / args.steps, "exchange_share": exch_ms / total_ms,
-            "tokens_match_unsharded": ok, "gpu_launches": 2 * args.steps,
+            "tokens_match_unsharded": ok, "gpu_launches": 3 * args.steps,
         }
         print(json.dumps(line), flush=True)
     vsamp.close()
@@ -480,7 +480,7 @@ def main():
                          "peak_kind": kind, "kernel": "lrs_sample_rows",
                          "kernel_ms_mean": mean_launch, "bytes_per_launch": rows * bytes_per_row},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps,
+            "gpu_launches": 2 * args.steps,  # the ordering pass and the sampling kernel
             "clocks": clk,
             "cpu_baseline": cpu,
         }

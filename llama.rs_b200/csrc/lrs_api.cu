@@ -55,6 +55,7 @@ struct lrs_ctx {
     uint64_t scratch_stride = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0, lists_off = 0;
     uint32_t scratch_ctas = 0;
     uint32_t* d_counter = nullptr;
+    uint32_t* d_order = nullptr;  // claim order of a launch (max_rows entries)
     int32_t* d_err = nullptr;
     // pinned host staging
     float* h_logits = nullptr;
@@ -203,7 +204,7 @@ int lrs_destroy(lrs_ctx* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     void* dev[] = {ctx->d_params, ctx->d_state, ctx->d_tokens, ctx->d_probs, ctx->d_status, ctx->d_logits,
                    ctx->d_hist, ctx->d_hist_len, ctx->d_exp_index, ctx->d_exp_entries, ctx->d_scratch,
-                   ctx->d_counter, ctx->d_err};
+                   ctx->d_counter, ctx->d_order, ctx->d_err};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {ctx->h_logits, ctx->h_hist, ctx->h_hist_len, ctx->h_tokens, ctx->h_probs, ctx->h_status};
@@ -284,6 +285,7 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     CKF(cudaMalloc(&ctx->d_scratch, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
     CKF(cudaMemset(ctx->d_scratch, 0, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
     CKF(cudaMalloc(&ctx->d_counter, kLrsRowCounters * sizeof(uint32_t)));
+    CKF(cudaMalloc(&ctx->d_order, R * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_err, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_err, 0, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_state, 0, R * sizeof(unsigned long long)));
@@ -368,6 +370,7 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.lanes_off = ctx->lanes_off;
     args.lists_off = ctx->lists_off;
     args.row_counter = ctx->d_counter;
+    args.order = ctx->d_order;
     args.err_flag = ctx->d_err;
     uint32_t grid = ctx->scratch_ctas;
     if (grid > rows) grid = rows;

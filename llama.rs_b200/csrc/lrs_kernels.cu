@@ -241,6 +241,10 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
     // next row: sweep c over the rows claims the rows of class c (each sweep has its
     // own counter, so every row is claimed exactly once)
     auto claim = [&]() -> uint32_t {
+        if (a.order) {  // rows in the order of the ordering pass
+            const uint32_t i = atomicAdd(a.row_counter, 1u);
+            return i < a.rows ? __ldcg(a.order + i) : a.rows;
+        }
         for (;;) {
             const uint32_t r = atomicAdd(a.row_counter + sweep, 1u);
             if (r >= a.rows) {
@@ -2944,6 +2948,43 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
     }
 }
 
+// --------------------------------------------------------------- row order ----
+// The claim order of a launch: rows by estimated cost, longest first (list scheduling of
+// rows of unequal length over the persistent CTAs ends sooner when the rows left for the
+// end are the short ones).  The cost grows with the temperature (more elements can change
+// the exact softmax sum) and with a path-N finish; one-pass rows (greedy) are cheapest.
+// Key: 32 temperature bands from 1.5 down to 0.5 (hotter and NaN in band 0, colder in
+// band 31) times the two finishes, then the one-pass rows.  One block, a counting sort
+// in shared memory; the order inside a key is free (rows are independent).
+constexpr int kOrderThreads = 1024;
+constexpr uint32_t kOrderKeys = 65;
+__device__ __forceinline__ uint32_t order_key(const lrs_params& P, uint32_t n) {
+    if (row_passes(P, n) != 2u) return kOrderKeys - 1;
+    const uint32_t k = (P.top_k == 0 || P.top_k > n) ? n : P.top_k;
+    const bool long_finish = !(k < n && k <= (uint32_t)kKMax);
+    const float f = (1.5f - P.temperature) * 32.0f;
+    const uint32_t band = !(f > 0.0f) ? 0u : f >= 31.0f ? 31u : (uint32_t)f;
+    return band * 2u + (long_finish ? 0u : 1u);
+}
+__global__ void __launch_bounds__(kOrderThreads) lrs_order_rows(const lrs_params* __restrict__ params, uint32_t rows,
+                                                                 uint32_t n, uint32_t* __restrict__ order) {
+    __shared__ uint32_t cnt[kOrderKeys];
+    for (uint32_t i = threadIdx.x; i < kOrderKeys; i += blockDim.x) cnt[i] = 0u;
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) atomicAdd(&cnt[order_key(params[r], n)], 1u);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t acc = 0;
+        for (uint32_t i = 0; i < kOrderKeys; ++i) {
+            const uint32_t c = cnt[i];
+            cnt[i] = acc;
+            acc += c;
+        }
+    }
+    __syncthreads();
+    for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) order[atomicAdd(&cnt[order_key(params[r], n)], 1u)] = r;
+}
+
 }  // namespace lrs
 
 // ------------------------------------------------------------------ host side ----
@@ -2969,6 +3010,11 @@ cudaError_t lrs_kernel_occupancy(int* ctas_per_sm, size_t smem) {
 cudaError_t lrs_kernel_launch(const lrs_kernel_args_t* args, uint32_t grid, size_t smem, cudaStream_t s) {
     cudaError_t e = lrs_kernel_set_smem(smem);
     if (e != cudaSuccess) return e;
+    if (args->order) {
+        lrs::lrs_order_rows<<<1, lrs::kOrderThreads, 0, s>>>(args->params, args->rows, args->n, args->order);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return e;
+    }
     lrs::lrs_sample_rows<<<grid, lrs::kBlock, smem, s>>>(*args);
     return cudaGetLastError();
 }

@@ -35,6 +35,8 @@ struct lrs_kernel_args_t {
     uint64_t lanes_off;                   // per-tile lane sums
     uint64_t lists_off;                   // candidate lists of sparse tiles
     uint32_t* row_counter;    // kLrsRowCounters row counters (one per claim class), zeroed before each launch
+    uint32_t* order;          // nullable: rows in claim order, written by the launch's ordering pass
+                              // (rows entries; then row_counter[0] alone indexes it)
     int32_t* err_flag;        // sticky error word
 };
 
