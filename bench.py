@@ -262,7 +262,7 @@ def run_vocab_sharded(args, world, rank, local):
                                    f"({V // world} each), one all-gather per step, top_k 50, top_p 0.95, temp 0.7",
                        "parallelism": f"vocabulary over {world} GPU(s)"},
             "exchange_ms_per_step": exch_ms / args.steps, "exchange_share": exch_ms / total_ms,
-            "tokens_match_unsharded": ok, "gpu_launches": 3 * args.steps,
+            "tokens_match_unsharded": ok, "gpu_launches": 2 * args.steps,
         }
         print(json.dumps(line), flush=True)
     vsamp.close()

@@ -370,10 +370,12 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.lanes_off = ctx->lanes_off;
     args.lists_off = ctx->lists_off;
     args.row_counter = ctx->d_counter;
-    args.order = ctx->d_order;
     args.err_flag = ctx->d_err;
     uint32_t grid = ctx->scratch_ctas;
     if (grid > rows) grid = rows;
+    // the claim order matters only when some CTA takes more than one row: smaller batches
+    // skip the ordering pass (and its launch) and claim by the class sweeps
+    args.order = rows > grid ? ctx->d_order : nullptr;
     CK(cudaMemsetAsync(ctx->d_counter, 0, kLrsRowCounters * sizeof(uint32_t), s));
     CK(lrs_kernel_launch(&args, grid, smem, s));
     return LRS_OK;
