@@ -299,10 +299,12 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
             // A two-pass row can run long after its last load (pass 2, a long finish): the
             // next row is claimed only once the consumers say the row is nearly done, so
             // that a CTA still busy with a long row leaves the remaining rows to others.
+            // (Bounded at 16 times the usual wait: a whole row's work lies in between, and
+            // the consumers' own waits are bounded separately.)
             const long long t0 = clock64();
             while ((int)(sh.claim_ok - rqi) < 0) {
                 if (sh.abort) break;
-                if (clock64() - t0 > kWaitCycles) {
+                if (clock64() - t0 > 16 * kWaitCycles) {
                     sh.abort = 1u;
                     atomicExch(a.err_flag, LRS_E_TIMEOUT);
                     break;
