@@ -45,6 +45,7 @@ WORKLOAD = ("headline: 1024 rows x 151,936 f32 logits per GPU, Gumbel + Zipf-lik
             "permutation, temperature U[0.5,1.5], top_k {0,20,40,100}, top_p U[0.8,1.0], "
             "repetition penalty U[1.0,1.3] over a 64-token window")
 FALLBACK_HBM_GBS = 6650.0
+NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal (the north star quotes 8 TB/s)
 
 
 def peaks():
@@ -473,9 +474,13 @@ def main():
         threads = os.cpu_count() or 1
         nrows = min(args.cpu_rows, rows)
         v, dt, passes = cpu_sample(w, nrows, threads, args.cpu_seconds)
+        # the reference's sampler is single-threaded: the same sample on one host thread too
+        n1 = min(nrows, 64)
+        v1, dt1, _ = cpu_sample(w, n1, 1, 0.0)
         cpu = {"value": v, "unit": "rows/s", "cores": threads, "kind": "port",
                "sample": f"first {nrows} rows of this rank's headline workload, {passes} passes, one sampler "
-                         f"per row over {threads} host threads ({dt:.1f} s)"}
+                         f"per row over {threads} host threads ({dt:.1f} s)",
+               "value_1_thread": v1, "sample_1_thread": f"first {n1} rows on one host thread ({dt1:.1f} s)"}
 
     if rank == 0:
         line = {
@@ -487,6 +492,7 @@ def main():
                        "l2": "inputs larger than L2 (622 MB of logits per GPU per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
+                         "nominal_peak": NOMINAL_HBM_GBS, "frac_of_nominal": achieved / NOMINAL_HBM_GBS,
                          "peak_kind": kind, "kernel": "lrs_sample_rows",
                          "kernel_ms_mean": mean_launch, "bytes_per_launch": rows * bytes_per_row},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
