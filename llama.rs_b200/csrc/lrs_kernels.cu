@@ -2061,7 +2061,10 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
 
         {
             // -------------------------------------------------------- pass 1 ----
-            float m_w = -kInf;          // warp: running max of the scaled logits (its own tiles)
+            float m_w = -kInf;          // warp: running max of the scaled logits (its own tiles; warp 0: and
+                                        // the unaligned head and tail elements)
+            float m_pre = -kInf;        // warp: max of elements known to precede its next tile (its own
+                                        // earlier tiles; warp 0: the head, never the tail)
             float bv = -kInf;           // lane: greedy best value and index
             uint32_t bi = 0xFFFFFFFFu;
             WState ws{0u, -kInf, kInf, 0u};  // warp: path-K filter
@@ -2100,6 +2103,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 } else {
                     const float xs = __fmul_rn(x, inv_t);
                     m_w = fmax_nan(m_w, warp_max_nan(mine ? xs : -kInf));
+                    m_pre = warp_max_nan(mine && (uint32_t)lane < g.head ? xs : -kInf);
                     if (kact) {  // at most 6 entries: the buffer is empty
                         const bool hit = mine && xs >= ws.theta;
                         const unsigned hb = __ballot_sync(0xFFFFFFFFu, hit);
@@ -2140,7 +2144,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                             front += adv;
                         }
                     }
-                    const float mp = fmax_nan(m_w, gpm);
+                    const float mp = fmax_nan(m_pre, gpm);
                     cthr = __fsub_rn(mp, __fmaf_rn(fabsf(mp), 9.5367432e-07f, theta_c));  // slack 2^-20 |mp|
                 }
                 wait_full(sh, qq, a.err_flag);
@@ -2336,6 +2340,7 @@ extern "C" __global__ void __launch_bounds__(kBlock, 2) lrs_sample_rows(SampleAr
                 }
                 if (!dense) woff += ncand;
                 m_w = fmax_nan(m_w, mt);
+                m_pre = fmax_nan(m_pre, mt);
             }
             if (greedy) {
 #pragma unroll

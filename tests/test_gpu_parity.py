@@ -60,6 +60,27 @@ def test_mixed_pruned_vocab_unaligned_rows():
     assert _check_workload(w, "mixed") == 64
 
 
+def test_many_short_rows_every_claim_key():
+    # More rows than the ordering pass's block has threads and than the grid has CTAs,
+    # so rows are claimed in cost order (every temperature band, both finishes, greedy
+    # rows last), on short misaligned rows; the results must not depend on the order.
+    rng = np.random.default_rng(11)
+    rows, n, ld = 2500, 2003, 2005
+    buf = (rng.standard_normal((rows, ld)) * 3).astype(np.float32)
+    p = O.make_params(rows=rows)
+    p["temperature"] = rng.choice(np.array([0.0, 0.05, 0.3, 0.5, 0.7, 0.9, 1.1, 1.3, 1.5, 2.5], np.float32), rows)
+    p["top_k"] = rng.choice(np.array([0, 1, 40, 128, 200, n], np.uint32), rows)
+    p["top_p"] = rng.choice(np.array([0.5, 0.9, 0.99, 1.0], np.float32), rows)
+    p["repetition_penalty"] = rng.choice(np.array([1.0, 1.2], np.float32), rows)
+    p["repeat_last_n"] = 64
+    hist = rng.integers(0, n, (rows, 64)).astype(np.uint32)
+    hl = rng.integers(0, 65, rows).astype(np.uint32)
+    st = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+    gpu = run_device(buf, n, hist, hl, p, st, ld=ld)
+    ref = run_oracle(np.ascontiguousarray(buf[:, :n]), n, hist, hl, p, st)
+    assert compare(gpu, ref, "many short rows") == rows
+
+
 def test_greedy_rows_with_planted_ties():
     w = W.greedy(row_ids=range(0, 256, 4))
     assert _check_workload(w, "greedy") == 64
