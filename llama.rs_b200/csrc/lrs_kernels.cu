@@ -1533,6 +1533,7 @@ __device__ __noinline__ void finish_path_n(RowShared& sh, FinishCtx& f) {
             }
             // dense runs through the staging area
             for (uint32_t k0 = 0; k0 < nd; k0 += kGatherRuns) {
+                if (__any_sync(0xFFFFFFFFu, sh.abort != 0u)) break;  // (aborted: issue no more copies)
                 const uint32_t nb = min((uint32_t)kGatherRuns, nd - k0);
                 // run k0 + u: its first element and length (a multiple of 4: 16-byte copies)
                 auto run_of = [&](uint32_t u, uint32_t& e0, uint32_t& len) {
