@@ -136,6 +136,14 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(inside)}
 
 
+def headline_config(rows, vocab, window, world):
+    """The `config` object of the headline line, the same for both arms (the reference arm
+    samples the same rows of the same workload on the host cores)."""
+    return {"workload": WORKLOAD, "rows_per_gpu": rows, "vocab": vocab, "window": window,
+            "parallelism": f"rows sharded over {world} GPU(s), replicas, no collective",
+            "l2": "inputs larger than L2 (622 MB of logits per GPU per step)"}
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -169,7 +177,7 @@ def run_reference(args, world, rank):
     if rank != 0:
         return
     from lrs import workloads as W
-    rows = min(args.rows, args.ref_rows)
+    rows = args.rows if args.ref_rows is None else min(args.rows, args.ref_rows)
     w = W.headline(row_ids=range(rows))
     threads = os.cpu_count() or 1
     times = []
@@ -182,7 +190,7 @@ def run_reference(args, world, rank):
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": WORKLOAD, "rows_per_step": rows, "vocab": w.vocab, "window": w.window},
+        "config": headline_config(rows, w.vocab, w.window, world),
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
                          "sample": f"{rows} rows of the headline workload per step, one sampler per row, "
                                    f"rows spread over {threads} host threads"},
@@ -362,7 +370,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-rows", type=int, default=1024)
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="cpu_baseline: repeat the sample this long")
-    ap.add_argument("--ref-rows", type=int, default=128)
+    ap.add_argument("--ref-rows", type=int, default=None,
+                    help="--impl reference: rows per step (default: --rows, the GPU arm's rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
     ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded", "configs"])
     args = ap.parse_args()
@@ -487,9 +496,7 @@ def main():
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "rows_per_gpu": rows, "vocab": V, "window": Wn,
-                       "parallelism": f"rows sharded over {world} GPU(s), replicas, no collective",
-                       "l2": "inputs larger than L2 (622 MB of logits per GPU per step)"},
+            "config": headline_config(rows, V, Wn, world),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "nominal_peak": NOMINAL_HBM_GBS, "frac_of_nominal": achieved / NOMINAL_HBM_GBS,

@@ -129,12 +129,21 @@ int  lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_
  * (a cudaStream_t, NULL = legacy default stream), no host synchronisation.
  * d_params[rows], d_state[rows] (read and advanced in place), d_tokens[rows],
  * d_probs[rows] (nullable), d_status[rows] (nullable, int32), d_info[rows] (nullable).
- * Returns LRS_OK once enqueued; row errors are reported through d_status.           */
+ * Returns LRS_OK once enqueued; row errors are reported through d_status.
+ * Errors of the launch as a whole (a bounded wait that ran out, LRS_E_TIMEOUT, or a
+ * failed internal check, LRS_E_INTERNAL) are also kept in the context's sticky error
+ * word, so that they are seen when d_status is NULL: the next call on the context
+ * returns such an error of an earlier launch once it is known on the host (that call
+ * is then not enqueued), and lrs_poll_error waits for the last launch and returns it.  */
 int  lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t n, uint64_t ld,
                        const uint32_t* d_hist, uint64_t hist_ld, const uint32_t* d_hist_len,
                        const lrs_params* d_params, uint64_t* d_state,
                        uint32_t* d_tokens, float* d_probs, int32_t* d_status,
                        lrs_row_info* d_info, void* stream);
+/* Replaces: nothing (the reference's sampler cannot fail this way).  Waits for the
+ * context's last launch and returns (and clears) the error it reported: LRS_OK,
+ * LRS_E_TIMEOUT or LRS_E_INTERNAL; LRS_E_CUDA if the wait itself failed.          */
+int  lrs_poll_error(lrs_ctx* ctx);
 
 /* ---- batched sampling without allocation ----------------------------------------
  * No counterpart in the reference (rust-llama has no GPU path); an addition for callers
@@ -153,13 +162,23 @@ int  lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint3
  * whose kernels can overlap on the GPU race with each other: issue them on one stream.
  * Returns LRS_OK once enqueued, LRS_E_INVALID for bad arguments (or a missing or
  * mismatching libm-expf table), LRS_E_CUDA if a CUDA call failed; row errors go to
- * d_status as with lrs_sample_device.                                                */
-#define LRS_NOALLOC_SCRATCH_BYTES (32u << 20)
+ * d_status as with lrs_sample_device, and an error of the launch as a whole (a bounded
+ * wait that ran out, a failed internal check) stays in the device's sticky error word
+ * until lrs_noalloc_poll_error reads it: pass d_status, or poll, to see such errors.
+ * Parallelism: the kernel runs as many CTAs as the fixed scratch holds at this n, at
+ * most one per row: 84 at n = 151,936 (the context entry point runs 296 on a B200), 49
+ * at the largest n.  Throughput on large batches is lower than lrs_sample_device's by
+ * about that ratio; small batches (up to 84 rows at n = 151,936) are not affected.   */
+#define LRS_NOALLOC_SCRATCH_BYTES (128u << 20)
 #define LRS_NOALLOC_MAX_VOCAB     262144u
 int  lrs_sample_device_noalloc(int device, const float* d_logits, uint32_t rows, uint32_t n, uint64_t ld,
                                const uint32_t* d_hist, uint64_t hist_ld, const uint32_t* d_hist_len,
                                const lrs_params* d_params, uint64_t* d_state,
                                uint32_t* d_tokens, float* d_probs, int32_t* d_status, void* stream);
+/* No counterpart in the reference.  Waits for the work enqueued on `stream` and returns
+ * (and clears) the device's sticky error word of lrs_sample_device_noalloc launches:
+ * LRS_OK, LRS_E_TIMEOUT or LRS_E_INTERNAL; the set-up's error if set-up failed for good. */
+int  lrs_noalloc_poll_error(int device, void* stream);
 
 /* ---- vocabulary-sharded rows (multi-GPU exchange) -------------------------------
  * lrs_assemble_shards  the exchange step of vocabulary sharding: G ranks each hold

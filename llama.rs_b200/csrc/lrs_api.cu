@@ -57,6 +57,11 @@ struct lrs_ctx {
     uint32_t* d_counter = nullptr;
     uint32_t* d_order = nullptr;  // claim order of a launch (max_rows entries)
     int32_t* d_err = nullptr;
+    // the sticky error word as of the last launch: copied to pinned memory after every
+    // launch (err_ev marks the copy), reported by the next call or lrs_poll_error
+    int32_t* h_err = nullptr;
+    cudaEvent_t err_ev = nullptr;
+    bool err_pending = false;     // err_ev recorded and not yet looked at
     // pinned host staging
     float* h_logits = nullptr;
     uint32_t* h_hist = nullptr;
@@ -207,13 +212,15 @@ int lrs_destroy(lrs_ctx* ctx) {
                    ctx->d_counter, ctx->d_order, ctx->d_err};
     for (void* p : dev)
         if (p) cudaFree(p);
-    void* host[] = {ctx->h_logits, ctx->h_hist, ctx->h_hist_len, ctx->h_tokens, ctx->h_probs, ctx->h_status};
+    void* host[] = {ctx->h_logits, ctx->h_hist, ctx->h_hist_len, ctx->h_tokens, ctx->h_probs, ctx->h_status,
+                    ctx->h_err};
     for (void* p : host)
         if (p) cudaFreeHost(p);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
     for (cudaEvent_t e : ctx->copied)
         if (e) cudaEventDestroy(e);
+    if (ctx->err_ev) cudaEventDestroy(ctx->err_ev);
     delete ctx;
     return LRS_OK;
 }
@@ -295,6 +302,9 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     CKF(cudaMallocHost(&ctx->h_tokens, R * sizeof(uint32_t)));
     CKF(cudaMallocHost(&ctx->h_probs, R * sizeof(float)));
     CKF(cudaMallocHost(&ctx->h_status, R * sizeof(int32_t)));
+    CKF(cudaMallocHost(&ctx->h_err, sizeof(int32_t)));
+    *ctx->h_err = 0;
+    CKF(cudaEventCreateWithFlags(&ctx->err_ev, cudaEventDisableTiming));
     int rc = load_exp_table(ctx);
     if (rc != LRS_OK) return fail(rc);
 #undef CKF
@@ -328,6 +338,32 @@ int lrs_set_params(lrs_ctx* ctx, const lrs_params* params, uint32_t rows) {
     return LRS_OK;
 }
 
+// The sticky error word of earlier launches, if the copy made after the last launch has
+// landed (wait: block until it has).  A non-zero word is returned once and cleared.
+static int take_pending_error(lrs_ctx* ctx, bool wait) {
+    if (!ctx->err_pending) return LRS_OK;
+    if (wait) {
+        CK(cudaEventSynchronize(ctx->err_ev));
+    } else {
+        const cudaError_t q = cudaEventQuery(ctx->err_ev);
+        if (q == cudaErrorNotReady) return LRS_OK;
+        if (q != cudaSuccess) return set_err(ctx, LRS_E_CUDA, "error-word copy failed: %s", cudaGetErrorString(q));
+    }
+    ctx->err_pending = false;
+    const int32_t err = *ctx->h_err;
+    if (err == 0) return LRS_OK;
+    *ctx->h_err = 0;
+    CK(cudaMemset(ctx->d_err, 0, sizeof(int32_t)));
+    return set_err(ctx, err, "an earlier launch on this context reported error %d (%s)", err,
+                   err == LRS_E_TIMEOUT ? "a bounded wait ran out" : "an internal check failed");
+}
+
+int lrs_poll_error(lrs_ctx* ctx) {
+    if (!ctx) return set_err(nullptr, LRS_E_INVALID, "lrs_poll_error: ctx is NULL");
+    CK(cudaSetDevice(ctx->device));
+    return take_pending_error(ctx, true);
+}
+
 int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32_t n, uint64_t ld,
                       const uint32_t* d_hist, uint64_t hist_ld, const uint32_t* d_hist_len,
                       const lrs_params* d_params, uint64_t* d_state, uint32_t* d_tokens, float* d_probs,
@@ -343,6 +379,10 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     if (!d_params || !d_state || !d_tokens) return set_err(ctx, LRS_E_INVALID, "lrs_sample_device: NULL buffer");
     if (d_hist_len && !d_hist) return set_err(ctx, LRS_E_INVALID, "lrs_sample_device: hist_len without hist");
     CK(cudaSetDevice(ctx->device));
+    {
+        const int perr = take_pending_error(ctx, false);
+        if (perr != LRS_OK) return perr;  // (this call is not enqueued)
+    }
     cudaStream_t s = (cudaStream_t)stream;
     const size_t smem = dyn_smem_bytes(n);
     lrs_kernel_args_t args;
@@ -378,6 +418,10 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.order = rows > grid ? ctx->d_order : nullptr;
     CK(cudaMemsetAsync(ctx->d_counter, 0, kLrsRowCounters * sizeof(uint32_t), s));
     CK(lrs_kernel_launch(&args, grid, smem, s));
+    // the error word after this launch, for the next call (no host synchronisation)
+    CK(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaEventRecord(ctx->err_ev, s));
+    ctx->err_pending = true;
     return LRS_OK;
 }
 
@@ -479,11 +523,9 @@ int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t
     CK(cudaStreamSynchronize(s));
     memcpy(out_tokens, ctx->h_tokens, rows * 4);
     if (out_probs) memcpy(out_probs, ctx->h_probs, rows * 4);
-    int32_t err = 0;
-    CK(cudaMemcpy(&err, ctx->d_err, 4, cudaMemcpyDeviceToHost));
-    if (err) {
-        CK(cudaMemset(ctx->d_err, 0, 4));
-        return set_err(ctx, err, "lrs_sample: kernel reported error %d", err);
+    {
+        const int perr = take_pending_error(ctx, true);  // (the stream is idle: the copy has landed)
+        if (perr != LRS_OK) return perr;
     }
     for (uint32_t r = 0; r < rows; ++r)
         if (ctx->h_status[r] != LRS_OK)

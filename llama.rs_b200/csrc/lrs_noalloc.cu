@@ -42,13 +42,15 @@ static __device__ __align__(256) uint2 g_exp_entries[kMaxTableEntries + 1];
 static __device__ __align__(256) uint32_t g_counter[kLrsRowCounters + 1];  // row counters, then the error word
 
 struct DeviceSetup {
-    bool done = false;
+    bool done = false;     // set-up finished (successfully, or with a permanent failure)
     int status = LRS_OK;
     unsigned long long* scratch = nullptr;
     unsigned long long* index = nullptr;
     uint2* entries = nullptr;
     uint32_t* counter = nullptr;
-    int ctas = 0;  // CTAs that fit on the device at the largest shared-memory size
+    int ctas = 0;          // CTAs that fit on the device at once (SMs x resident CTAs per SM)
+    uint32_t layout_n = 0; // vocabulary the scratch's window bitmaps are laid out for (0: none yet)
+    uint32_t layout_grid = 0;  // ... and the CTAs whose bitmaps were cleared for it
 };
 DeviceSetup g_setup[kMaxDevices];
 std::mutex g_setup_lock;
@@ -107,28 +109,45 @@ int load_table_once() {
     return LRS_OK;
 }
 
-// One-time set-up of `device` (current): device addresses of the arrays, table upload.
+// One-time set-up of `device` (current): device addresses of the arrays, table upload,
+// occupancy.  A missing or mismatching table is permanent (latched); a failed CUDA call
+// is not, so a later call retries the set-up.
 int setup_device(int device) {
     DeviceSetup& s = g_setup[device];
     if (s.done) return s.status;
-    s.done = true;
-    s.status = LRS_E_CUDA;
     int rc = load_table_once();
     if (rc != LRS_OK) {
         s.status = rc;
+        s.done = true;
         return rc;
     }
-    if (cudaGetSymbolAddress((void**)&s.scratch, g_scratch) != cudaSuccess) return s.status;
-    if (cudaGetSymbolAddress((void**)&s.index, g_exp_index) != cudaSuccess) return s.status;
-    if (cudaGetSymbolAddress((void**)&s.entries, g_exp_entries) != cudaSuccess) return s.status;
-    if (cudaGetSymbolAddress((void**)&s.counter, g_counter) != cudaSuccess) return s.status;
-    if (cudaMemcpy(s.index, h_index, sizeof h_index, cudaMemcpyHostToDevice) != cudaSuccess) return s.status;
-    if (cudaMemcpy(s.entries, h_entries, (size_t)h_count * sizeof(uint2), cudaMemcpyHostToDevice) != cudaSuccess)
-        return s.status;
     cudaDeviceProp prop;
-    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return s.status;
-    s.ctas = prop.multiProcessorCount * 2;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess) return LRS_E_CUDA;
+    if (prop.major < 10) {  // the kernel is built for sm_100a only
+        s.status = LRS_E_INVALID;
+        s.done = true;
+        return s.status;
+    }
+    if (cudaGetSymbolAddress((void**)&s.scratch, g_scratch) != cudaSuccess) return LRS_E_CUDA;
+    if (cudaGetSymbolAddress((void**)&s.index, g_exp_index) != cudaSuccess) return LRS_E_CUDA;
+    if (cudaGetSymbolAddress((void**)&s.entries, g_exp_entries) != cudaSuccess) return LRS_E_CUDA;
+    if (cudaGetSymbolAddress((void**)&s.counter, g_counter) != cudaSuccess) return LRS_E_CUDA;
+    if (cudaMemcpy(s.index, h_index, sizeof h_index, cudaMemcpyHostToDevice) != cudaSuccess) return LRS_E_CUDA;
+    if (cudaMemcpy(s.entries, h_entries, (size_t)h_count * sizeof(uint2), cudaMemcpyHostToDevice) != cudaSuccess)
+        return LRS_E_CUDA;
+    const size_t smem = lrs_kernel_smem_bytes();
+    if (lrs_kernel_set_smem(smem) != cudaSuccess) return LRS_E_CUDA;
+    int occ = 0;
+    if (lrs_kernel_occupancy(&occ, smem) != cudaSuccess) return LRS_E_CUDA;
+    if (occ < 1) {
+        s.status = LRS_E_INVALID;
+        s.done = true;
+        return s.status;
+    }
+    s.ctas = prop.multiProcessorCount * (occ > 2 ? 2 : occ);
+    s.layout_n = 0;
     s.status = LRS_OK;
+    s.done = true;
     return LRS_OK;
 }
 
@@ -155,14 +174,19 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         std::lock_guard<std::mutex> lock(g_setup_lock);
         rc = setup_device(device);
     }
-    const DeviceSetup& s = g_setup[device];
+    DeviceSetup& s = g_setup[device];
     if (rc == LRS_OK) {
         const size_t smem = lrs_kernel_smem_bytes();
         uint64_t per_cta = 0, bitmap_off = 0, tiles_off = 0, lanes_off = 0, lists_off = 0;  // scratch words per CTA and its layout
         lrs_kernel_scratch_layout(n, &per_cta, &bitmap_off, &tiles_off, &lanes_off, &lists_off);
+        // as many CTAs as the fixed scratch holds at this n (for example 84 at n = 151,936,
+        // of the 296 that the context entry point runs), at most one per row
         uint32_t grid = (uint32_t)(kScratchBytes / 8 / per_cta);
         if (grid > (uint32_t)s.ctas) grid = (uint32_t)s.ctas;
         if (grid > rows) grid = rows;
+        // (a change of the grid at the same n leaves bitmaps of CTAs beyond the last
+        // cleared grid untouched: clear again whenever this call reaches further)
+        if (grid > s.layout_grid) s.layout_n = 0;
         lrs_kernel_args_t args;
         memset(&args, 0, sizeof args);
         args.logits = d_logits;
@@ -190,10 +214,46 @@ extern "C" int lrs_sample_device_noalloc(int device, const float* d_logits, uint
         args.row_counter = s.counter;
         args.err_flag = reinterpret_cast<int32_t*>(s.counter + kLrsRowCounters);
         cudaStream_t st = (cudaStream_t)stream;
-        // the row counters and the error word must start at zero on every call
-        if (cudaMemsetAsync(s.counter, 0, (kLrsRowCounters + 1) * sizeof(uint32_t), st) != cudaSuccess)
+        // The kernel needs every CTA's window bitmap to be zero on entry (each row clears
+        // the bits it sets).  The scratch is laid out for this call's n, so a call with
+        // another n than the last one finds other data (an earlier call's candidate keys)
+        // where its bitmaps lie: clear them first.
+        if (s.layout_n != n) {
+            if (cudaMemset2DAsync(s.scratch + bitmap_off, per_cta * 8, 0, (tiles_off - bitmap_off) * 8, grid,
+                                  st) != cudaSuccess)
+                rc = LRS_E_CUDA;
+            else {
+                s.layout_n = n;
+                s.layout_grid = grid;
+            }
+        }
+        // the row counters start at zero on every call; the error word is read back (and
+        // cleared) by lrs_noalloc_poll_error
+        if (rc == LRS_OK && cudaMemsetAsync(s.counter, 0, kLrsRowCounters * sizeof(uint32_t), st) != cudaSuccess)
             rc = LRS_E_CUDA;
-        else if (lrs_kernel_launch(&args, grid, smem, st) != cudaSuccess)
+        if (rc == LRS_OK && lrs_kernel_launch(&args, grid, smem, st) != cudaSuccess) rc = LRS_E_CUDA;
+    }
+    if (cur != device) cudaSetDevice(cur);
+    return rc;
+}
+
+extern "C" int lrs_noalloc_poll_error(int device, void* stream) {
+    if (device < 0 || device >= kMaxDevices) return LRS_E_INVALID;
+    DeviceSetup& s = g_setup[device];
+    if (!s.done || s.status != LRS_OK) return s.done ? s.status : LRS_OK;
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess) return LRS_E_CUDA;
+    if (cur != device && cudaSetDevice(device) != cudaSuccess) return LRS_E_CUDA;
+    int32_t err = 0;
+    int rc = LRS_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    if (cudaMemcpyAsync(&err, s.counter + kLrsRowCounters, sizeof err, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        rc = LRS_E_CUDA;
+    else if (err != 0) {
+        rc = err;
+        if (cudaMemsetAsync(s.counter + kLrsRowCounters, 0, sizeof err, st) != cudaSuccess ||
+            cudaStreamSynchronize(st) != cudaSuccess)
             rc = LRS_E_CUDA;
     }
     if (cur != device) cudaSetDevice(cur);

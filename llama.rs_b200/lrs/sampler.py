@@ -44,6 +44,7 @@ EXPORTS = [
     "lrs_create", "lrs_destroy", "lrs_last_error", "lrs_seed_state", "lrs_set_state", "lrs_get_state",
     "lrs_set_params", "lrs_sample", "lrs_sample_device", "lrs_sampler_new", "lrs_sampler_free",
     "lrs_sampler_state", "lrs_sampler_sample", "lrs_sample_device_noalloc", "lrs_assemble_shards",
+    "lrs_poll_error", "lrs_noalloc_poll_error",
 ]
 
 
@@ -85,6 +86,10 @@ def lib() -> ctypes.CDLL:
         L.lrs_sample_device.restype = I
         L.lrs_sample_device_noalloc.argtypes = [I, P, U32, U32, U64, P, U64, P, P, P, P, P, P, P]
         L.lrs_sample_device_noalloc.restype = I
+        L.lrs_poll_error.argtypes = [P]
+        L.lrs_poll_error.restype = I
+        L.lrs_noalloc_poll_error.argtypes = [I, P]
+        L.lrs_noalloc_poll_error.restype = I
         L.lrs_assemble_shards.argtypes = [P, U32, U32, U32, P, U64, P]
         L.lrs_assemble_shards.restype = I
         L.lrs_sampler_new.argtypes = [U64, I]
@@ -224,6 +229,10 @@ class BatchSampler:
                                        params.data_ptr(), state.data_ptr(), tokens.data_ptr(), ptr(probs),
                                        ptr(status), ptr(info), stream)
         _check(code, self._h)
+
+    def poll_error(self):
+        """Waits for the last launch and raises the error it reported (lrs_poll_error)."""
+        _check(lib().lrs_poll_error(self._h), self._h)
 
     def close(self):
         if getattr(self, "_h", None):

@@ -123,14 +123,18 @@ def sample_one(logits: np.ndarray, params, recent, state: int):
 def sample_batch(logits: np.ndarray, n: int, hist: np.ndarray | None, hist_len: np.ndarray | None,
                  params: np.ndarray, state: np.ndarray, threads: int = 1):
     """Independent samplers per row.  logits (rows, ld) f32; hist (rows, hist_ld) u32.
+    A single logits row with more than one parameter record is shared by every row
+    (ld = 0), as the C ABI allows.
 
     Returns (tokens u32[rows], infos INFO_DTYPE[rows], new_state u64[rows])."""
+    if logits.ndim == 2 and logits.shape[0] > 1 and logits.strides[0] == 0:
+        logits = logits[:1]  # a broadcast row: share it instead of materialising every copy
     logits = np.ascontiguousarray(logits, np.float32)
     if logits.ndim == 1:
         logits = logits.reshape(1, -1)
     rows, ld = logits.shape[0], logits.shape[1]
-    if logits.strides[0] == 0:
-        ld = 0
+    if rows == 1 and np.size(params) > 1:
+        rows, ld = int(np.size(params)), 0
     if hist is not None:
         hist = np.ascontiguousarray(hist, np.uint32)
         hist_ld = hist.shape[1]

@@ -67,6 +67,9 @@ def test_invalid_arguments_are_rejected(built_lib):
     st = ctypes.c_int(0)
     tok = L.lrs_sampler_sample(None, None, 0, None, None, 0, ctypes.byref(st))
     assert st.value == lrs.LRS_E_INVALID and tok == lrs.TOKEN_NONE
+    assert L.lrs_poll_error(None) == lrs.LRS_E_INVALID
+    assert L.lrs_noalloc_poll_error(-1, None) == lrs.LRS_E_INVALID
+    assert L.lrs_noalloc_poll_error(0, None) == lrs.LRS_OK  # (no set-up yet on device 0: nothing to report)
 
 
 def test_expf_table_matches_this_libm(built_lib):

@@ -14,6 +14,7 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def test_reference_arm_prints_one_contract_line():
+    sys.path.insert(0, REPO)
     out = subprocess.run(
         [sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "1",
          "--ref-rows", "8"],
@@ -26,7 +27,10 @@ def test_reference_arm_prints_one_contract_line():
     assert d["value"] > 0 and d["steps"] == 2 and d["warmup"] == 1
     assert d["cpu_baseline"]["kind"] == "port" and d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"] == {"value": d["value"], "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
-    assert d["config"]["rows_per_step"] == 8
+    assert d["config"]["rows_per_gpu"] == 8
+    # the same config object as the GPU arm's line (same workload, same rows per step)
+    import bench
+    assert d["config"] == bench.headline_config(8, d["config"]["vocab"], d["config"]["window"], 1)
 
 
 def test_cpu_sample_repeats_until_the_time_bound():
