@@ -84,9 +84,11 @@ typedef struct lrs_row_info {
     float    prob;       /* probability of the returned token */
     uint32_t n_cand;     /* candidates examined after the streaming pass (implementation detail) */
     uint32_t events;     /* ordered (exact) steps taken by the sum emulation (implementation detail) */
-    uint32_t cycles[8];  /* SM clock cycles (saturating) by phase: 0 max/filter pass, 1 estimates and
-                            thresholds, 2 softmax-sum pass, 3 top-k/top-p/draw, 4-6 zero,
-                            7 sorting within 3 (implementation detail) */
+    uint32_t cycles[8];  /* rows of the persistent kernel: SM clock cycles (saturating) by phase: 0
+                            max/filter pass, 1 estimates and thresholds, 2 softmax-sum pass, 3
+                            top-k/top-p/draw, 7 sorting within 3; rows finished by the staged
+                            pipeline: 4 is 1, 0-2 the cycles of its prep, sum and finish stages,
+                            5 the blocks its sum walked (implementation detail) */
     uint32_t reserved;
 } lrs_row_info;
 

@@ -56,6 +56,9 @@ struct lrs_ctx {
     uint32_t scratch_ctas = 0;
     uint32_t* d_counter = nullptr;
     uint32_t* d_order = nullptr;  // claim order of a launch (max_rows entries)
+    void* d_stage = nullptr;      // working memory of the staged pipeline
+    lrs_stage_layout_t stage{};
+    bool staged = true;           // the staged pipeline (false: lrs_sample_rows alone, LRS_STAGED=0)
     int32_t* d_err = nullptr;
     // the sticky error word as of the last launch: copied to pinned memory after every
     // launch (err_ev marks the copy), reported by the next call or lrs_poll_error
@@ -209,7 +212,7 @@ int lrs_destroy(lrs_ctx* ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     void* dev[] = {ctx->d_params, ctx->d_state, ctx->d_tokens, ctx->d_probs, ctx->d_status, ctx->d_logits,
                    ctx->d_hist, ctx->d_hist_len, ctx->d_exp_index, ctx->d_exp_entries, ctx->d_scratch,
-                   ctx->d_counter, ctx->d_order, ctx->d_err};
+                   ctx->d_counter, ctx->d_order, ctx->d_err, ctx->d_stage};
     for (void* p : dev)
         if (p) cudaFree(p);
     void* host[] = {ctx->h_logits, ctx->h_hist, ctx->h_hist_len, ctx->h_tokens, ctx->h_probs, ctx->h_status,
@@ -293,6 +296,12 @@ int lrs_create(int device, uint32_t max_rows, uint32_t max_vocab, uint32_t max_h
     CKF(cudaMemset(ctx->d_scratch, 0, (size_t)ctx->scratch_ctas * ctx->scratch_stride * sizeof(unsigned long long)));
     CKF(cudaMalloc(&ctx->d_counter, kLrsRowCounters * sizeof(uint32_t)));
     CKF(cudaMalloc(&ctx->d_order, R * sizeof(uint32_t)));
+    {
+        const char* st = getenv("LRS_STAGED");
+        ctx->staged = !(st && st[0] == '0');
+    }
+    lrs_stage_layout(max_rows, max_vocab, &ctx->stage);
+    CKF(cudaMalloc(&ctx->d_stage, ctx->stage.bytes));
     CKF(cudaMalloc(&ctx->d_err, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_err, 0, sizeof(int32_t)));
     CKF(cudaMemset(ctx->d_state, 0, R * sizeof(unsigned long long)));
@@ -413,11 +422,16 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     args.err_flag = ctx->d_err;
     uint32_t grid = ctx->scratch_ctas;
     if (grid > rows) grid = rows;
-    // the claim order matters only when some CTA takes more than one row: smaller batches
-    // skip the ordering pass (and its launch) and claim by the class sweeps
-    args.order = rows > grid ? ctx->d_order : nullptr;
-    CK(cudaMemsetAsync(ctx->d_counter, 0, kLrsRowCounters * sizeof(uint32_t), s));
-    CK(lrs_kernel_launch(&args, grid, smem, s));
+    if (ctx->staged) {
+        // the staged pipeline; the rows it leaves go to lrs_sample_rows on `grid` CTAs
+        CK(lrs_stage_launch(&args, ctx->d_stage, &ctx->stage, grid, smem, s));
+    } else {
+        // the claim order matters only when some CTA takes more than one row: smaller batches
+        // skip the ordering pass (and its launch) and claim by the class sweeps
+        args.order = rows > grid ? ctx->d_order : nullptr;
+        CK(cudaMemsetAsync(ctx->d_counter, 0, kLrsRowCounters * sizeof(uint32_t), s));
+        CK(lrs_kernel_launch(&args, grid, smem, s));
+    }
     // the error word after this launch, for the next call (no host synchronisation)
     CK(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
     CK(cudaEventRecord(ctx->err_ev, s));

@@ -241,9 +241,10 @@ __device__ __noinline__ void producer(const SampleArgs& a, RowShared& sh, float*
     // next row: sweep c over the rows claims the rows of class c (each sweep has its
     // own counter, so every row is claimed exactly once)
     auto claim = [&]() -> uint32_t {
-        if (a.order) {  // rows in the order of the ordering pass
+        if (a.order) {  // rows in the order of the ordering pass (or a given list of rows)
             const uint32_t i = atomicAdd(a.row_counter, 1u);
-            return i < a.rows ? __ldcg(a.order + i) : a.rows;
+            const uint32_t lim = a.claim_count ? *(volatile const uint32_t*)a.claim_count : a.rows;
+            return i < lim ? __ldcg(a.order + i) : a.rows;
         }
         for (;;) {
             const uint32_t r = atomicAdd(a.row_counter + sweep, 1u);
@@ -2993,6 +2994,8 @@ __global__ void __launch_bounds__(kOrderThreads) lrs_order_rows(const lrs_params
     for (uint32_t r = threadIdx.x; r < rows; r += blockDim.x) order[atomicAdd(&cnt[order_key(params[r], n)], 1u)] = r;
 }
 
+#include "lrs_stages.cuh"
+
 }  // namespace lrs
 
 // ------------------------------------------------------------------ host side ----
@@ -3018,11 +3021,82 @@ cudaError_t lrs_kernel_occupancy(int* ctas_per_sm, size_t smem) {
 cudaError_t lrs_kernel_launch(const lrs_kernel_args_t* args, uint32_t grid, size_t smem, cudaStream_t s) {
     cudaError_t e = lrs_kernel_set_smem(smem);
     if (e != cudaSuccess) return e;
-    if (args->order) {
+    if (args->order && !args->claim_count) {
         lrs::lrs_order_rows<<<1, lrs::kOrderThreads, 0, s>>>(args->params, args->rows, args->n, args->order);
         e = cudaGetLastError();
         if (e != cudaSuccess) return e;
     }
     lrs::lrs_sample_rows<<<grid, lrs::kBlock, smem, s>>>(*args);
     return cudaGetLastError();
+}
+
+void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L) {
+    const uint64_t R = rows ? rows : 1, nt = (uint64_t)(vocab + lrs::kTile - 1) / lrs::kTile + 1;
+    uint64_t off = 0;
+    auto take = [&](uint64_t bytes) {
+        const uint64_t o = off;
+        off = (off + bytes + 255) & ~(uint64_t)255;
+        return o;
+    };
+    L->rows = (uint32_t)R;
+    L->nt = (uint32_t)nt;
+    L->tstat = take(R * nt * sizeof(float4));
+    L->lmax = take(R * nt * 32 * sizeof(float));
+    L->tprep = take(R * nt * sizeof(lrs::TilePrep));
+    L->tres = take(R * nt * sizeof(lrs::TileRes));
+    L->rprep = take(R * sizeof(lrs::RowPrep));
+    L->lists = take(R * lrs::kStageListCap * sizeof(uint2));
+    L->list_n = take(R * sizeof(uint32_t));
+    L->fb_rows = take(R * sizeof(uint32_t));
+    L->fb_count = take(sizeof(uint32_t));
+    L->bytes = off;
+}
+
+cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs_stage_layout_t* L,
+                             uint32_t fallback_grid, size_t smem, cudaStream_t s) {
+    using namespace lrs;
+    static int warps_grid[2] = {0, 0};  // persistent grids of the two per-tile stages (blocks)
+    if (!warps_grid[0]) {
+        int dev = 0, sms = 0, occ0 = 0, occ1 = 0;
+        cudaError_t e = cudaGetDevice(&dev);
+        if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, lrs_stage_stats, kStageThreads, 0);
+        if (e == cudaSuccess)
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, lrs_stage_classify, kStageThreads, 0);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(lrs_stage_finish, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(kStageListCap * sizeof(unsigned long long)));
+        if (e != cudaSuccess) return e;
+        warps_grid[0] = sms * (occ0 > 0 ? occ0 : 1);
+        warps_grid[1] = sms * (occ1 > 0 ? occ1 : 1);
+    }
+    const uint32_t rows = args->rows;
+    char* base = static_cast<char*>(mem);
+    StageArgs S;
+    S.a = *args;
+    S.nt = L->nt;
+    S.tstat = reinterpret_cast<float4*>(base + L->tstat);
+    S.lmax = reinterpret_cast<float*>(base + L->lmax);
+    S.tprep = reinterpret_cast<TilePrep*>(base + L->tprep);
+    S.tres = reinterpret_cast<TileRes*>(base + L->tres);
+    S.rprep = reinterpret_cast<RowPrep*>(base + L->rprep);
+    S.lists = reinterpret_cast<uint2*>(base + L->lists);
+    S.list_n = reinterpret_cast<uint32_t*>(base + L->list_n);
+    S.fb_rows = reinterpret_cast<uint32_t*>(base + L->fb_rows);
+    S.fb_count = reinterpret_cast<uint32_t*>(base + L->fb_count);
+    cudaError_t e = cudaMemsetAsync(S.list_n, 0, (size_t)rows * sizeof(uint32_t), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(S.fb_count, 0, sizeof(uint32_t), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(args->row_counter, 0, kLrsRowCounters * sizeof(uint32_t), s);
+    if (e != cudaSuccess) return e;
+    lrs_stage_stats<<<warps_grid[0], kStageThreads, 0, s>>>(S);
+    lrs_stage_prep<<<rows, kStageThreads, 0, s>>>(S);
+    lrs_stage_classify<<<warps_grid[1], kStageThreads, 0, s>>>(S);
+    lrs_stage_sum<<<(rows + kSumWarps - 1) / kSumWarps, kSumWarps * 32, 0, s>>>(S);
+    lrs_stage_finish<<<rows, kThreads, kStageListCap * sizeof(unsigned long long), s>>>(S);
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    // the rows the stages left: lrs_sample_rows on the list, in list order
+    lrs_kernel_args_t fb = *args;
+    fb.order = S.fb_rows;
+    fb.claim_count = S.fb_count;
+    return lrs_kernel_launch(&fb, fallback_grid, smem, s);
 }

@@ -37,8 +37,21 @@ struct lrs_kernel_args_t {
     uint32_t* row_counter;    // kLrsRowCounters row counters (one per claim class), zeroed before each launch
     uint32_t* order;          // nullable: rows in claim order, written by the launch's ordering pass
                               // (rows entries; then row_counter[0] alone indexes it)
+    const uint32_t* claim_count;  // nullable: `order` is given (no ordering pass) and holds this many rows
     int32_t* err_flag;        // sticky error word
 };
+
+// Working memory of the staged pipeline (lrs_stage_launch) for up to `rows` rows of up to
+// `vocab` entries: byte offsets into one device buffer of `bytes` bytes (256-byte aligned).
+struct lrs_stage_layout_t {
+    uint32_t rows, nt;        // rows and tile slots per row
+    uint64_t tstat, lmax, tprep, tres, rprep, lists, list_n, fb_rows, fb_count, bytes;
+};
+void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L);
+// The staged pipeline on args->rows rows, then lrs_sample_rows on the rows it leaves
+// (fallback_grid CTAs with `smem` bytes; args->row_counter is zeroed here).
+cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs_stage_layout_t* L,
+                             uint32_t fallback_grid, size_t smem, cudaStream_t s);
 
 // Largest distance (in float ulps, plus a margin for the difference between two
 // double-precision exps) of a libm-expf table entry from the rounding midpoint next to

@@ -1,0 +1,1358 @@
+// lrs_stages.cuh — the staged sampling pipeline (sm_100a), included by lrs_kernels.cu.
+//
+// The same computation as lrs_sample_rows (rust-llama src/sampler.rs:56-163 with
+// ops::softmax_inplace, src/ops.rs:397-419), split into five launches whose work items
+// are independent, so that every SM streams, classifies or finishes whatever is ready
+// instead of one CTA carrying one row through every phase:
+//
+//   stats     one warp per tile (1024 floats) of every row: the tile's max of the scaled
+//             logits x' = fl(pen(x) * inv_t) (sampler.rs:82-118), its sum of exp relative to
+//             that max (approximate, for estimates only), the 32 lane maxima, and for greedy
+//             rows the argmax (sampler.rs:62-70, 104-113).
+//   prep      one CTA per row: the row max M; greedy rows and rows whose probabilities are
+//             NaN finish here.  From the tile statistics, an estimate P_t of the sequential
+//             softmax sum at every tile start with a proven relative error bound, hence the
+//             lowest binade grid the exact sum can be on there (dead elements below it add
+//             exactly nothing) and the two grids a tile is classified on.  The candidate
+//             threshold of the finish: from the k-th largest lane maximum for top-k (k <= 128),
+//             or for top-p alone a depth below M that holds the nucleus's mass.
+//   classify  one warp per tile: the increments of the tile's live elements on its two
+//             grids (lrs_grid.h), per block of 128 elements, and the candidates appended to
+//             the row's list.
+//   sum       one warp per row: the exact running sum in tile order, a tile in one step
+//             where the sum stays on a grid it was classified for, else block by block,
+//             walking element by element only a block where the sum crosses a binade or
+//             meets a tie or an element of half a binade.
+//   finish    one CTA per row: the candidates' exact probabilities, sorted (p desc, index
+//             asc), the top-p cut, survivor sum and draw (sampler.rs:122-162).
+//
+// Rows the stages do not take (top-p off with top-k off or above kKMax, rows longer than
+// kStageMaxTiles tiles, a top-k list overflowing with ties, a nucleus larger than the list
+// capacity) are flagged and sampled by lrs_sample_rows afterwards, from the same inputs
+// (its results are the same bits).
+//
+// Tile layout in registers: lane L holds elements 128 j + 4 L + c (block j = 0..7, c = 0..3)
+// of the tile, so every warp-wide 16-byte load is one contiguous 512-byte block.
+
+constexpr int kStageThreads = 256;                 // stats / prep / classify blocks (8 warps)
+constexpr int kStageWarps = kStageThreads / 32;
+constexpr uint32_t kStageListCap = 8192;           // candidate-list entries per row
+constexpr int kStageNucleusBuckets = 580;          // mass buckets of width 1/32 in (M - x')
+constexpr uint32_t kStageNucleusRank = 2048;       // top-p lists reach at least the lane maximum of this rank
+constexpr uint32_t kStageMaxTiles = 256;           // tiles of the longest stochastic row the stages take (n <= 262,144)
+// flags of a row's prep record
+constexpr uint32_t kRowDone = 1u;        // outputs written by the prep (greedy, NaN, n <= 1)
+constexpr uint32_t kRowFallback = 2u;    // sampled by lrs_sample_rows afterwards
+constexpr uint32_t kRowPathK = 4u;       // top-k list (k <= kKMax)
+constexpr uint32_t kRowPathN = 8u;       // top-p nucleus list
+// flags of a tile's prep / result records
+constexpr uint32_t kTileWalk = 1u;       // prep: the estimate allows more than two grids
+constexpr uint32_t kTileOne = 2u;        // prep: the estimate allows grid u0 alone
+constexpr uint32_t kTileLive = 4u;       // result: some element can change the sum
+constexpr uint32_t kTileSp0 = 8u;        // result: a tie or big element on grid u0
+constexpr uint32_t kTileSp1 = 16u;       // ... on grid u0 + 1
+constexpr uint32_t kTileLikelyWalk = 32u;  // prep: the estimate crosses a binade inside the tile
+
+struct RowPrep {            // prep -> classify / sum / finish (64 bytes)
+    uint32_t flags;
+    float M;                // max of the scaled logits (ops.rs:401-406)
+    float inv_t;            // 1 / temperature (sampler.rs:115)
+    float cand;             // path K: scaled-logit threshold of the list; path N: d threshold
+    uint32_t k;             // effective top-k (sampler.rs:122-126)
+    float cand_raw;         // the same threshold on the raw (penalised) logit, for quick tests
+    uint32_t pad[2];        // sum -> finish: the exact softmax sum (bits) and its ordered steps
+    uint32_t cyc_prep;      // diagnostics: SM cycles of the prep and the sum, blocks walked
+    uint32_t cyc_sum;
+    uint32_t walks;
+    uint32_t pad2[5];
+};
+struct TilePrep {           // prep -> classify / sum (16 bytes)
+    int32_t u0;             // lowest grid exponent of the exact sum over the tile (rigorous)
+    uint32_t flags;
+    float xthr;             // raw (penalised) logits at or below this add exactly nothing from this tile on
+    float dthr;             // the same bound on d = fl(x' - M)
+};
+struct TileRes {            // classify -> sum (80 bytes)
+    uint32_t t0, t1;        // increment totals on grids u0 and u0 + 1 (saturating)
+    uint32_t flags;
+    uint32_t bflags;        // per block of 128 elements: bit b live, 8 + b a tie or big element on
+                            // grid u0, 16 + b the same on grid u0 + 1
+    uint32_t b0[8], b1[8];  // per block: increment totals on grids u0 and u0 + 1
+};
+
+struct StageArgs {
+    lrs_kernel_args_t a;    // inputs, outputs and the libm-expf table (shared with lrs_sample_rows)
+    uint32_t nt;            // tile slots per row (>= every row's tile count)
+    float4* tstat;          // [rows][nt]  (mt, pt, greedy value, greedy index bits)
+    float* lmax;            // [rows][nt][32] lane maxima
+    TilePrep* tprep;        // [rows][nt]
+    TileRes* tres;          // [rows][nt]
+    RowPrep* rprep;         // [rows]
+    uint2* lists;           // [rows][kStageListCap] (scaled logit bits, index)
+    uint32_t* list_n;       // [rows] entries appended (may exceed the capacity: overflow)
+    uint32_t* fb_rows;      // rows left to lrs_sample_rows
+    uint32_t* fb_count;
+};
+
+__device__ __forceinline__ void stage_fallback(const StageArgs& S, uint32_t r) {
+    const uint32_t i = atomicAdd(S.fb_count, 1u);
+    S.fb_rows[i] = r;
+}
+
+// The row's window as bits of the tile's elements [g0, g0 + cnt): the penalty set of
+// sampler.rs:82-102 (distinct ids of recent[start..] below n; ids of the tile are below n).
+// Built in the warp's 32 shared words; returns true if any bit is set.
+__device__ __forceinline__ bool tile_window(const uint32_t* hrow, uint32_t hstart, uint32_t hlen, uint32_t g0,
+                                            uint32_t cnt, uint32_t* wb) {
+    const int lane = threadIdx.x & 31;
+    wb[lane] = 0u;
+    __syncwarp();
+    for (uint32_t j = hstart + (uint32_t)lane; j < hlen; j += 32) {
+        const uint32_t o = hrow[j] - g0;
+        if (o < cnt) atomicOr(&wb[o >> 5], 1u << (o & 31));
+    }
+    __syncwarp();
+    return __any_sync(0xFFFFFFFFu, wb[lane] != 0u);
+}
+
+// The warp's tile in the block layout: v[4 j + c] = element 128 j + 4 L + c (-inf past cnt),
+// the penalty applied to the window's elements (sampler.rs:96-100).
+__device__ __forceinline__ void load_tile_blocks(const float* base, uint32_t cnt, bool pen, const uint32_t* wb,
+                                                 float penalty, float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+    const float ninf = __int_as_float(0xFF800000);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t e0 = 128u * j + 4u * lane;
+        float4 q = make_float4(ninf, ninf, ninf, ninf);
+        if (e0 < cnt) q = __ldg(reinterpret_cast<const float4*>(base + e0));
+        v[4 * j + 0] = q.x;
+        v[4 * j + 1] = q.y;
+        v[4 * j + 2] = q.z;
+        v[4 * j + 3] = q.w;
+    }
+    if (pen) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t b4 = (wb[4 * j + (lane >> 3)] >> (4 * (lane & 7))) & 15u;
+            if (b4) {
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                    if ((b4 >> c) & 1u) v[4 * j + c] = penalise(v[4 * j + c], penalty);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t window_start(const lrs_params& P, uint32_t hlen) {
+    return (P.repeat_last_n != 0 && hlen > P.repeat_last_n) ? hlen - P.repeat_last_n : 0u;  // sampler.rs:84-88
+}
+
+// ------------------------------------------------------------------ stats ----
+__global__ void __launch_bounds__(kStageThreads) lrs_stage_stats(const StageArgs S) {
+    __shared__ uint32_t wbits[kStageThreads];
+    const lrs_kernel_args_t& a = S.a;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t* wb = wbits + warp * 32;
+    const float kInf = __int_as_float(0x7F800000);
+    const uint64_t tasks = (uint64_t)a.rows * S.nt;
+    const uint64_t stride = (uint64_t)gridDim.x * kStageWarps;
+    for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
+        const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
+        const Geo g = row_geometry(a, r);
+        if (t >= g.nchunks) continue;
+        const lrs_params P = a.params[r];
+        const bool greedy = P.temperature <= 0.0f;
+        const bool pen_on = !(greedy && P.repetition_penalty == 1.0f) && P.repetition_penalty != 1.0f;
+        if (row_passes(P, g.n) == 2u && g.nchunks > kStageMaxTiles) continue;  // (long rows: lrs_sample_rows)
+        const uint32_t cnt = chunk_count(g, t);
+        const uint32_t g0 = g.head + t * kTile;
+        bool pen = false;
+        if (pen_on && a.hist_len) {
+            const uint32_t hlen = a.hist_len[r];
+            pen = tile_window(a.hist + (uint64_t)r * a.hist_ld, window_start(P, hlen), hlen, g0, cnt, wb);
+        }
+        float v[32];
+        load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+        float4* out = S.tstat + (uint64_t)r * S.nt + t;
+        if (greedy) {
+            // lowest index among the maximal non-NaN values (strict '>' from index 0)
+            float bv = -kInf;
+            uint32_t bi = 0xFFFFFFFFu;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const uint32_t gi = g0 + 128u * (i >> 2) + 4u * lane + (i & 3);
+                if (v[i] > bv || (v[i] == bv && gi < bi && v[i] != -kInf)) {
+                    bv = v[i];
+                    bi = gi;
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+                const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) *out = make_float4(bv, 0.0f, 0.0f, __uint_as_float(bi));
+            continue;
+        }
+        const float inv_t = __fdiv_rn(1.0f, P.temperature);
+        const float2 it2 = make_float2(inv_t, inv_t);
+        float ma = -kInf, mb = -kInf;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const float2 lo = __fmul2_rn(make_float2(v[4 * j], v[4 * j + 1]), it2);
+            const float2 hi = __fmul2_rn(make_float2(v[4 * j + 2], v[4 * j + 3]), it2);
+            v[4 * j] = lo.x;
+            v[4 * j + 1] = lo.y;
+            v[4 * j + 2] = hi.x;
+            v[4 * j + 3] = hi.y;
+            ma = fmax3_nan(ma, lo.x, lo.y);
+            mb = fmax3_nan(mb, hi.x, hi.y);
+        }
+        const float ml = fmax_nan(ma, mb);
+        const float mt = warp_max_nan(ml);
+        // approximate sum of exp(x' - mt) (estimates only; the error is bounded in the prep)
+        float sl = 0.0f;
+        if (mt > -kInf && mt < kInf) {
+            float s2[2] = {0.0f, 0.0f};
+#pragma unroll
+            for (int i = 0; i < 32; ++i) s2[i & 1] += ex2_approx(__fmul_rn(__fsub_rn(v[i], mt), kLog2e));
+            sl = s2[0] + s2[1];
+        }
+        const float pt = warp_sum_f(sl);
+        S.lmax[((uint64_t)r * S.nt + t) * 32u + lane] = ml;
+        if (lane == 0) *out = make_float4(mt, pt, 0.0f, 0.0f);
+    }
+}
+
+// ------------------------------------------------------------------- prep ----
+// Is id gi in the row's window?  (the whole warp looks)
+__device__ __forceinline__ bool in_window(const uint32_t* hrow, uint32_t hstart, uint32_t hlen, uint32_t gi) {
+    bool hit = false;
+    for (uint32_t j = hstart + (threadIdx.x & 31); j < hlen; j += 32) hit |= hrow[j] == gi;
+    return __any_sync(0xFFFFFFFFu, hit);
+}
+
+struct PrepShared {
+    float vals[kStageMaxTiles * 32 + 32];  // the row's lane maxima, then its edge elements (or -inf)
+    uint32_t hist[256];
+    float mass[kStageNucleusBuckets];
+    float xt[kNU];                         // raw dead thresholds by grid exponent (u - umin)
+    double wsum[kStageWarps];
+    float wf[kStageWarps];
+    uint32_t wu[kStageWarps];
+    int wi[2 * kStageWarps];
+    uint32_t bc[4];
+    float bf[4];
+    double bd[2];
+};
+
+// kk-th largest (1-based) of vals[0..cnt) in shared memory, by the block: radix select on
+// order-preserving keys, 8 bits a round, with warp-aggregated counter increments (the
+// values share their high bits).  kk <= cnt.
+__device__ __noinline__ float block_select_desc(const float* vals, uint32_t cnt, uint32_t kk, PrepShared& ps) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint32_t prefix = 0;
+    for (int round = 0; round < 4; ++round) {
+        const int shift = 24 - 8 * round;
+        for (int b = tid; b < 256; b += kStageThreads) ps.hist[b] = 0u;
+        __syncthreads();
+        for (uint32_t i0 = 0; i0 < cnt; i0 += kStageThreads) {
+            const uint32_t i = i0 + (uint32_t)tid;
+            const uint32_t key = i < cnt ? fkey(vals[i]) : 0u;
+            const bool match = i < cnt && (round == 0 || (key >> (shift + 8)) == (prefix >> (shift + 8)));
+            const uint32_t bin = match ? (key >> shift) & 255u : 256u;
+            const unsigned peers = __match_any_sync(0xFFFFFFFFu, bin);
+            if (match && lane == __ffs(peers) - 1) atomicAdd(&ps.hist[bin], (uint32_t)__popc(peers));
+        }
+        __syncthreads();
+        if (tid < 32) {
+            uint32_t d, rem;
+            digit_from_top(ps.hist, kk, d, rem);
+            if (tid == 0) {
+                ps.bc[0] = d;
+                ps.bc[1] = rem;
+            }
+        }
+        __syncthreads();
+        prefix |= ps.bc[0] << shift;
+        kk = ps.bc[1];
+        __syncthreads();
+    }
+    return fkey_inv(prefix);
+}
+
+__device__ __forceinline__ void write_row(const lrs_kernel_args_t& a, uint32_t r, int32_t status, uint32_t token,
+                                          float prob, bool advance, unsigned long long st, const lrs_row_info& inf) {
+    if (status == LRS_OK && advance) a.state[r] = st;
+    a.tokens[r] = token;
+    if (a.probs) a.probs[r] = prob;
+    if (a.status) a.status[r] = status;
+    if (a.info) a.info[r] = inf;
+}
+
+__device__ __forceinline__ lrs_row_info blank_info(uint32_t path, uint32_t k) {
+    lrs_row_info inf;
+    inf.status = LRS_OK;
+    inf.token = 0;
+    inf.path = path;
+    inf.k = k;
+    inf.cutoff = 0;
+    inf.pos = 0;
+    inf.max = 0.0f;
+    inf.sum_exp = 0.0f;
+    inf.surv_sum = 0.0f;
+    inf.r0 = 0.0f;
+    inf.prob = 1.0f;
+    inf.n_cand = 0;
+    inf.events = 0;
+    for (int q = 0; q < 8; ++q) inf.cycles[q] = 0;
+    inf.reserved = 0;
+    return inf;
+}
+
+// One CTA per row.
+__global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs S) {
+    __shared__ PrepShared ps;
+    const lrs_kernel_args_t& a = S.a;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float kInf = __int_as_float(0x7F800000);
+    const uint32_t r = blockIdx.x;
+    const long long t_start = clock64();
+    const lrs_params P = a.params[r];
+    const Geo g = row_geometry(a, r);
+    const uint32_t n = g.n;
+    const bool greedy = P.temperature <= 0.0f;  // sampler.rs:62, 104 (NaN -> stochastic)
+    const bool fast_greedy = greedy && P.repetition_penalty == 1.0f;
+    const bool pen_on = !fast_greedy && P.repetition_penalty != 1.0f;
+    const uint32_t k = (P.top_k == 0 || P.top_k > n) ? n : P.top_k;  // sampler.rs:122-126
+    const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;            // sampler.rs:136
+    const uint32_t path = greedy ? (fast_greedy ? 0u : 1u) : (n == 1 ? 3u : 2u);
+    const uint32_t ntile = g.nchunks;
+    RowPrep rp;
+    rp.flags = 0;
+    rp.M = 0.0f;
+    rp.inv_t = 1.0f;
+    rp.cand = -kInf;
+    rp.k = k;
+    rp.cand_raw = -kInf;
+    rp.pad[0] = rp.pad[1] = 0;
+    rp.cyc_prep = rp.cyc_sum = rp.walks = 0;
+    for (int q = 0; q < 5; ++q) rp.pad2[q] = 0;
+    lrs_row_info inf = blank_info(path, k);
+    auto leave = [&](uint32_t flags) {  // (thread 0 writes the record; every thread returns)
+        if (tid == 0) {
+            rp.flags = flags;
+            S.rprep[r] = rp;
+            if (flags & kRowFallback) stage_fallback(S, r);
+        }
+    };
+    if (n == 0) {  // sampler.rs:57-60
+        if (tid == 0) write_row(a, r, LRS_OK, 0u, 1.0f, false, 0ull, inf);
+        leave(kRowDone);
+        return;
+    }
+    if (row_passes(P, n) == 2u && ntile > kStageMaxTiles) {  // long rows: lrs_sample_rows
+        leave(kRowFallback);
+        return;
+    }
+    const uint32_t hlen = (pen_on && a.hist_len) ? a.hist_len[r] : 0u;
+    const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
+    const uint32_t hstart = window_start(P, hlen);
+    // the unaligned edge elements (at most 3 + 3): warp 0, lanes 0 .. edges-1
+    const uint32_t edges = g.head + g.tail;
+    const bool mine = warp == 0 && (uint32_t)lane < edges;
+    const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+    float ex = -kInf;
+    if (warp == 0) {
+        if (mine) ex = g.row[egi];
+        for (uint32_t e = 0; e < edges; ++e) {  // (penalty: each is looked up in the window by the warp)
+            const uint32_t gi = __shfl_sync(0xFFFFFFFFu, egi, (int)e);
+            const bool hit = pen_on && in_window(hrow, hstart, hlen, gi);
+            if (hit && (uint32_t)lane == e) ex = penalise(ex, P.repetition_penalty);
+        }
+    }
+    if (greedy) {
+        // lowest index among the maximal non-NaN values (sampler.rs:62-70, 104-113)
+        float bv = -kInf;
+        uint32_t bi = 0xFFFFFFFFu;
+        if (mine && ex == ex && ex != -kInf) {
+            bv = ex;
+            bi = egi;
+        }
+        for (uint32_t t = (uint32_t)tid; t < ntile; t += kStageThreads) {
+            const float4 q = S.tstat[(uint64_t)r * S.nt + t];
+            const uint32_t qi = __float_as_uint(q.w);
+            if (q.x > bv || (q.x == bv && qi < bi)) {
+                bv = q.x;
+                bi = qi;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            ps.wf[warp] = bv;
+            ps.wu[warp] = bi;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            for (int w = 1; w < kStageWarps; ++w)
+                if (ps.wf[w] > bv || (ps.wf[w] == bv && ps.wu[w] < bi)) {
+                    bv = ps.wf[w];
+                    bi = ps.wu[w];
+                }
+            const float x0 = g.row[0];  // NaN at index 0 -> 0 (the penalty keeps a NaN a NaN)
+            if (x0 != x0 || bi == 0xFFFFFFFFu) bi = 0;
+            inf.token = bi;
+            inf.cycles[4] = 1u;  // (finished by the staged pipeline)
+            write_row(a, r, LRS_OK, bi, 1.0f, false, 0ull, inf);
+        }
+        leave(kRowDone);
+        return;
+    }
+    const float inv_t = __fdiv_rn(1.0f, P.temperature);  // sampler.rs:115
+    const float exs = mine ? __fmul_rn(ex, inv_t) : -kInf;
+    // the row max (ops.rs:401-406, NaN-propagating)
+    float mx = exs;
+    for (uint32_t t = (uint32_t)tid; t < ntile; t += kStageThreads) mx = fmax_nan(mx, S.tstat[(uint64_t)r * S.nt + t].x);
+    mx = warp_max_nan(mx);
+    if (lane == 0) ps.wf[warp] = mx;
+    __syncthreads();
+    float M = ps.wf[0];
+    for (int w = 1; w < kStageWarps; ++w) M = fmax_nan(M, ps.wf[w]);
+    __syncthreads();
+    inf.max = M;
+    if (n == 1) {  // one uniform is consumed and the token is 0 (sampler.rs:155-162)
+        if (tid == 0) {
+            unsigned long long st = a.state[r];
+            (void)next_f32(&st);
+            inf.cycles[4] = 1u;
+            write_row(a, r, LRS_OK, 0u, 1.0f, true, st, inf);
+        }
+        leave(kRowDone);
+        return;
+    }
+    if (M != M || fabsf(M) == kInf) {  // NaN probabilities: the reference panics (sampler.rs:129/132)
+        if (tid == 0) {
+            inf.status = LRS_E_NAN;
+            inf.token = LRS_TOKEN_NONE;
+            inf.prob = 0.0f;
+            inf.cycles[4] = 1u;
+            write_row(a, r, LRS_E_NAN, LRS_TOKEN_NONE, 0.0f, false, 0ull, inf);
+        }
+        leave(kRowDone);
+        return;
+    }
+    rp.M = M;
+    rp.inv_t = inv_t;
+    const bool pathK = k < n && k <= (uint32_t)kKMax;
+    if (!pathK && !topp_on) {  // every element survives: the survivor sum runs over the whole row
+        leave(kRowFallback);
+        return;
+    }
+    // ---- running-sum estimates and the grids of every tile (one tile a thread) ----
+    // P_t: the head's exp sum plus the tile sums before t, each rescaled to M.  The exact
+    // sequential sum there, S_t, lies within P_t (1 +- delta_t) with delta_t = i 2^-23 +
+    // 2^-13 (i elements before the tile): each of the i f32 roundings moves it by at most
+    // 2^-24 S_t, and P's own error (approximate exps of once-rounded arguments, the f32 tile
+    // sums) is far below 2^-13.  So the exact sum is on grid u0 = grid(P_t (1 - delta_t)) or
+    // above over the whole tile, and elements with d < (u0 - 1) ln 2 - 0.01 add exactly nothing.
+    if (warp == 0) {
+        double eh = 0.0, et = 0.0;
+        if (mine) ((uint32_t)lane < g.head ? eh : et) = exp((double)__fsub_rn(exs, M));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            eh += __shfl_xor_sync(0xFFFFFFFFu, eh, o);
+            et += __shfl_xor_sync(0xFFFFFFFFu, et, o);
+        }
+        if (lane == 0) {
+            ps.bd[0] = eh;
+            ps.bd[1] = et;
+        }
+    }
+    const uint32_t t = (uint32_t)tid;  // (ntile <= kStageMaxTiles == kStageThreads)
+    const bool tin = t < ntile;
+    double c = 0.0;
+    if (tin) {
+        const float4 q = S.tstat[(uint64_t)r * S.nt + t];
+        if (q.x > -kInf) c = (double)q.y * exp((double)q.x - (double)M);
+    }
+    double incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double tv = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if (lane >= o) incl += tv;
+    }
+    if (lane == 31) ps.wsum[warp] = incl;
+    __syncthreads();
+    double before = ps.bd[0];
+    for (int w = 0; w < warp; ++w) before += ps.wsum[w];
+    double s_total = ps.bd[0] + ps.bd[1];
+    for (int w = 0; w < kStageWarps; ++w) s_total += ps.wsum[w];
+    TilePrep tp{0, 0u, 0.0f, 0.0f};
+    int umin = 0x7FFFFFFF, umax = -0x7FFFFFFF;
+    if (tin) {
+        const double pt0 = before + incl - c, pt1 = before + incl;
+        const double i0 = (double)(g.head + t * kTile), i1 = i0 + (double)chunk_count(g, t);
+        const double lo = pt0 * (1.0 - (i0 * 0x1p-23 + 0x1p-13));
+        const double hi = pt1 * (1.0 + (i1 * 0x1p-23 + 0x1p-13));
+        const int u0 = unit_exp(__double2float_rd(lo));
+        const int uh = unit_exp(__double2float_ru(hi));
+        tp.u0 = u0;
+        tp.flags = uh > u0 + 1 ? kTileWalk : (uh == u0 ? kTileOne : 0u);
+        // (a likely walk: the central estimate crosses a binade inside the tile)
+        if (unit_exp((float)pt0) != unit_exp((float)pt1)) tp.flags |= kTileLikelyWalk;
+        tp.dthr = __fsub_rn(__fmul_rn((float)(u0 - 1), 0.69314718f), 0.01f);
+        umin = umax = u0;
+    }
+    umin = __reduce_min_sync(0xFFFFFFFFu, umin);
+    umax = __reduce_max_sync(0xFFFFFFFFu, umax);
+    if (lane == 0) {
+        ps.wi[warp] = umin;
+        ps.wi[kStageWarps + warp] = umax;
+    }
+    __syncthreads();
+    umin = ps.wi[0];
+    umax = ps.wi[kStageWarps];
+    for (int w = 1; w < kStageWarps; ++w) {
+        umin = min(umin, ps.wi[w]);
+        umax = max(umax, ps.wi[kStageWarps + w]);
+    }
+    // the raw dead thresholds, one bisection per distinct grid of the row's tiles
+    for (int u = umin + tid; u <= umax; u += kStageThreads)
+        ps.xt[u - umin] = raw_threshold(__fsub_rn(__fmul_rn((float)(u - 1), 0.69314718f), 0.01f), inv_t, M);
+    // the lane maxima and the edge elements, staged for the selections below
+    const uint32_t nl = ntile * 32u;
+    const float* lm = S.lmax + (uint64_t)r * S.nt * 32u;
+    for (uint32_t i = (uint32_t)tid; i < nl; i += kStageThreads) ps.vals[i] = lm[i];
+    if (warp == 0) ps.vals[nl + lane] = exs;  // (lane e: edge element e, or -inf)
+    __syncthreads();
+    if (tin) {
+        tp.xthr = ps.xt[tp.u0 - umin];
+        S.tprep[(uint64_t)r * S.nt + t] = tp;
+    }
+    const uint32_t nv = nl + 32u;
+    // ---- the candidate threshold of the finish ----
+    if (pathK) {
+        // k-th largest of the lane maxima (k <= kKMax of them are distinct elements at or
+        // above it, so it bounds the row's k-th largest scaled logit from below); less the
+        // tie margin (generous for both the bound and the final k-th value), every element
+        // whose probability can reach the k-th probability lies above it.
+        const float th = block_select_desc(ps.vals, nv, k, ps);
+        float cand = -kInf;
+        if (th > -kInf) cand = __fsub_rn(th, __fmul_rn(__fadd_rn(__fadd_rn(fabsf(th), fabsf(M)), 1.0f), 0x1p-17f));
+        rp.flags = kRowPathK;
+        rp.cand = cand;
+        rp.cand_raw = cand > -kInf ? raw_threshold(cand, inv_t, 0.0f) : -kInf;
+    } else {
+        // The nucleus (sampler.rs:135-146) is the head of the sorted probabilities up to mass
+        // top_p.  The list takes every element with d >= theta, theta the shallower of two
+        // guesses: the first bucket edge (width 1/32) where the mass of the lane maxima above
+        // it reaches (top_p + 2^-16) times the estimated sum (lane maxima are distinct
+        // elements, so the mass of all elements there is at least that), and the depth of
+        // the kStageNucleusRank-th largest lane maximum (a list of a few thousand entries).
+        // The finish checks that the cut lies inside the list, and gathers a deeper list
+        // from the row where it does not.
+        for (int b = tid; b < kStageNucleusBuckets; b += kStageThreads) ps.mass[b] = 0.0f;
+        __syncthreads();
+        for (uint32_t i = (uint32_t)tid; i < nv; i += kStageThreads) {
+            const float d = __fsub_rn(ps.vals[i], M);
+            if (d >= -(float)(kStageNucleusBuckets - 1) / 32.0f)
+                atomicAdd(&ps.mass[(int)fminf(-d * 32.0f, (float)(kStageNucleusBuckets - 2))], expf(d));
+        }
+        __syncthreads();
+        if (warp == 0) {
+            const double target = ((double)P.top_p + 0x1p-16) * s_total;
+            double acc = 0.0;
+            int found = -1;
+            for (int base = 0; base < kStageNucleusBuckets - 1 && found < 0; base += 32) {
+                const int b = base + lane;
+                double m = b < kStageNucleusBuckets - 1 ? (double)ps.mass[b] : 0.0;
+                double mi = m;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const double tv = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+                    if (lane >= o) mi += tv;
+                }
+                const unsigned hit = __ballot_sync(0xFFFFFFFFu, b < kStageNucleusBuckets - 1 && acc + mi >= target);
+                if (hit) found = base + __ffs(hit) - 1;
+                acc += __shfl_sync(0xFFFFFFFFu, mi, 31);
+            }
+            if (lane == 0) ps.bf[0] = found >= 0 ? -(float)(found + 1) / 32.0f : -kInf;
+        }
+        __syncthreads();
+        const float th_mass = ps.bf[0];
+        const float x_rank = block_select_desc(ps.vals, nv, kStageNucleusRank < nv ? kStageNucleusRank : nv, ps);
+        const float th_rank = x_rank > -kInf ? __fsub_rn(x_rank, M) : -kInf;
+        rp.flags = kRowPathN;
+        rp.cand = fmaxf(th_mass, th_rank);  // elements with d >= this (d = fl(x' - M))
+        rp.cand_raw = rp.cand > -kInf ? raw_threshold(rp.cand, inv_t, M) : -kInf;  // largest raw x with d below it
+    }
+    if (warp == 0) {
+        // the edge elements that qualify join the list (the tiles' candidates come from classify)
+        const bool cq = mine && ((rp.flags & kRowPathK) ? exs >= rp.cand : __fsub_rn(exs, M) >= rp.cand);
+        const unsigned cm = __ballot_sync(0xFFFFFFFFu, cq);
+        uint32_t base = 0;
+        if (lane == 0 && cm) base = atomicAdd(S.list_n + r, (uint32_t)__popc(cm));
+        base = __shfl_sync(0xFFFFFFFFu, base, 0) + (uint32_t)__popc(cm & ((1u << lane) - 1u));
+        if (cq && base < kStageListCap) S.lists[(uint64_t)r * kStageListCap + base] = make_uint2(__float_as_uint(exs), egi);
+    }
+    if (tid == 0) {
+        const long long dt = clock64() - t_start;
+        rp.cyc_prep = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
+        S.rprep[r] = rp;
+    }
+}
+
+// --------------------------------------------------------------- classify ----
+// One element's increments (integer units) on grids u0 and u0 + 1 (unit 2^u0, binade base
+// bm0 = 2^(u0 + 23), half unit h0; the same for u0 + 1), from CUDA's expf where it cannot
+// round differently from libm's (within 2 ulp: more than 2^-21 e from every rounding boundary
+// of either grid), else from libm's value; sp: a tie (exact half unit) or an element of half a
+// binade or more on that grid (an ordered step).  one: grid u0 alone (channel 1 is flagged).
+struct ElemCls {
+    uint32_t c0, c1;
+    bool sp0, sp1;
+};
+__device__ __forceinline__ ElemCls classify_units(float d, int u0, float bm0, float bm1, float h0, float h1, bool one,
+                                                  const ExpTable tab) {
+    ElemCls r{0u, 0u, false, one};
+    bool ex = d == 0.0f;
+    float e = ex ? 1.0f : expf(d);
+    float i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);  // RN(e / U) U below bm0
+    float i1 = one ? 0.0f : __fsub_rn(__fadd_rn(bm1, e), bm1);
+    if (!ex) {
+        const float tol = __fmul_rn(e, 4.76837158203125e-07f);  // 2^-21 e > 2 ulp
+        bool amb = e < 7.8886091e-31f || fabsf(__fsub_rn(e, bm0)) <= tol ||
+                   (e < bm0 && fabsf(__fsub_rn(e, i0)) >= __fsub_rn(h0, tol));
+        if (!one)
+            amb = amb || fabsf(__fsub_rn(e, bm1)) <= tol || (e < bm1 && fabsf(__fsub_rn(e, i1)) >= __fsub_rn(h1, tol));
+        if (amb) {
+            e = exact_expf(d, tab);
+            ex = true;
+            i0 = __fsub_rn(__fadd_rn(bm0, e), bm0);
+            i1 = one ? 0.0f : __fsub_rn(__fadd_rn(bm1, e), bm1);
+        }
+    }
+    if (e >= bm0) {
+        r.sp0 = true;
+    } else {
+        r.c0 = grid_units(i0, -u0);
+        if (ex && h0 > 0.0f && fabsf(__fsub_rn(e, i0)) == h0) r.sp0 = true;
+    }
+    if (!one) {
+        if (e >= bm1) {
+            r.sp1 = true;
+        } else {
+            r.c1 = grid_units(i1, -(u0 + 1));
+            if (ex && fabsf(__fsub_rn(e, i1)) == h1) r.sp1 = true;
+        }
+    }
+    return r;
+}
+
+__global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageArgs S) {
+    __shared__ uint32_t wbits[kStageThreads];
+    __shared__ float stage[kStageWarps * kTile];    // per warp: the live elements' d values
+    __shared__ uint8_t sblock[kStageWarps * kTile];  // ... and their blocks
+    __shared__ uint32_t bcount[kStageWarps * 17];    // ... per block increment totals (2 grids) and flags
+    const lrs_kernel_args_t& a = S.a;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t* wb = wbits + warp * 32;
+    float* st = stage + warp * kTile;
+    uint8_t* sbk = sblock + warp * kTile;
+    uint32_t* bc = bcount + warp * 17;
+    uint32_t* bfl = bc + 16;
+    const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
+    const uint64_t tasks = (uint64_t)a.rows * S.nt;
+    const uint64_t stride = (uint64_t)gridDim.x * kStageWarps;
+    for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
+        const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
+        const RowPrep rp = S.rprep[r];
+        if (rp.flags & (kRowDone | kRowFallback)) continue;
+        const Geo g = row_geometry(a, r);
+        if (t >= g.nchunks) continue;
+        const uint64_t ti = (uint64_t)r * S.nt + t;
+        const TilePrep tp = S.tprep[ti];
+        const float mt = S.tstat[ti].x;
+        const float M = rp.M, inv_t = rp.inv_t;
+        const bool pathK = rp.flags & kRowPathK;
+        const float dmax = __fsub_rn(mt, M);
+        const bool sum_live = !(dmax < tp.dthr);
+        const bool cand_live = pathK ? !(mt < rp.cand) : !(dmax < rp.cand);
+        TileRes res;
+        res.t0 = res.t1 = 0u;
+        res.flags = 0u;
+        res.bflags = 0u;
+        if (!sum_live && !cand_live) {
+            if (lane == 0) {
+                S.tres[ti].flags = 0u;
+                S.tres[ti].bflags = 0u;
+            }
+            continue;
+        }
+        const lrs_params P = a.params[r];
+        const bool pen_on = P.repetition_penalty != 1.0f;
+        const uint32_t cnt = chunk_count(g, t);
+        const uint32_t g0 = g.head + t * kTile;
+        bool pen = false;
+        if (pen_on && a.hist_len) {
+            const uint32_t hlen = a.hist_len[r];
+            pen = tile_window(a.hist + (uint64_t)r * a.hist_ld, window_start(P, hlen), hlen, g0, cnt, wb);
+        }
+        float v[32];
+        load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+        // ---- candidates: appended to the row's list (any order; the finish sorts them)
+        if (cand_live) {
+            uint32_t cm = 0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (!(v[i] > rp.cand_raw)) continue;  // (quick reject on the raw value)
+                const float xs = __fmul_rn(v[i], inv_t);
+                const bool c = pathK ? xs >= rp.cand : __fsub_rn(xs, M) >= rp.cand;
+                if (c) cm |= 1u << i;
+            }
+            const uint32_t nc = (uint32_t)__popc(cm);
+            const uint32_t incl = warp_incl_scan_plain(nc);
+            const uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            if (tot) {
+                uint32_t base = 0;
+                if (lane == 31) base = atomicAdd(S.list_n + r, tot);
+                base = __shfl_sync(0xFFFFFFFFu, base, 31) + incl - nc;
+                uint2* lst = S.lists + (uint64_t)r * kStageListCap;
+                for (uint32_t m = cm; m; m &= m - 1u) {
+                    const int i = __ffs(m) - 1;
+                    if (base < kStageListCap)
+                        lst[base] = make_uint2(__float_as_uint(__fmul_rn(v[i], inv_t)),
+                                               g0 + 128u * (i >> 2) + 4u * lane + (i & 3));
+                    ++base;
+                }
+            }
+        }
+        // ---- increments of the live elements on grids u0 and u0 + 1, per block of 128, from
+        // their d values compacted into the warp's staging area (a lane classifies total / 32)
+        if (sum_live) {
+            const int u0 = tp.u0;
+            const bool one = tp.flags & kTileOne;
+            uint32_t lm = 0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) lm |= (uint32_t)(v[i] > tp.xthr) << i;
+            const uint32_t nc = (uint32_t)__popc(lm);
+            const uint32_t incl = warp_incl_scan_plain(nc);
+            const uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+            uint32_t o = incl - nc;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if ((lm >> i) & 1u) {
+                    st[o] = d_of(v[i], inv_t, M);
+                    sbk[o] = (uint8_t)(i >> 2);
+                    ++o;
+                }
+            if (lane < 16) bc[lane] = 0u;
+            if (lane == 0) bfl[0] = 0u;
+            __syncwarp();
+            const float bm0 = grid_value(u0, kTwo23), bm1 = __fadd_rn(bm0, bm0);
+            const float h0 = u0 > -149 ? pow2f(u0 - 1) : 0.0f, h1 = pow2f(u0);
+            for (uint32_t j = (uint32_t)lane; j < tot; j += 32) {
+                const ElemCls c = classify_units(st[j], u0, bm0, bm1, h0, h1, one, exptab);
+                const uint32_t b = sbk[j];
+                if (c.c0) atomicAdd(&bc[b], c.c0);
+                if (c.c1) atomicAdd(&bc[8 + b], c.c1);
+                const uint32_t f = (1u << b) | (c.sp0 ? 0x100u << b : 0u) | (c.sp1 ? 0x10000u << b : 0u);
+                atomicOr(&bfl[0], f);
+            }
+            __syncwarp();
+            // (a block's count is at most 128 * 2^23 < 2^32; saturated where it leaves the grid)
+            const uint32_t c0 = lane < 8 ? min(bc[lane], kSat) : 0u, c1 = lane < 8 ? min(bc[8 + lane], kSat) : 0u;
+            const uint32_t bf = bfl[0];
+            res.t0 = min(__reduce_add_sync(0xFFFFFFFFu, c0), kSat);
+            res.t1 = min(__reduce_add_sync(0xFFFFFFFFu, c1), kSat);
+            res.bflags = bf;
+            res.flags = (tot ? kTileLive : 0u) | ((bf >> 8) & 0xFFu ? kTileSp0 : 0u) | ((bf >> 16) & 0xFFu ? kTileSp1 : 0u);
+            if (lane < 8) {
+                res.b0[lane] = c0;
+                res.b1[lane] = c1;
+            }
+            __syncwarp();  // (the staging area is reused by the next tile)
+        }
+        if (lane == 0) {
+            TileRes* out = S.tres + ti;
+            out->t0 = res.t0;
+            out->t1 = res.t1;
+            out->flags = res.flags;
+            out->bflags = res.bflags;
+        }
+        if (sum_live && lane < 8) {
+            S.tres[ti].b0[lane] = res.b0[lane];
+            S.tres[ti].b1[lane] = res.b1[lane];
+        }
+    }
+}
+
+// ----------------------------------------------------------------- walks ----
+// Exact sequential sum s <- fl(s + e) (ops.rs:408-411) over one block of 128 elements in
+// index order, by one warp: lane L holds positions 4 L .. 4 L + 3, with libm's values.  A
+// round classifies the remaining positions on the grid of the running sum and the next one
+// (lrs_grid.h); ordered steps (a binade crossing, a tie, an element of half a binade or
+// more) are found by prefix sums on the channel of the sum's current grid and added
+// exactly; only a sum that leaves both grids is classified again.  A sum that starts from
+// zero crosses many binades in its first elements: such a block is added one by one.
+__device__ __noinline__ float warp_walk_block(const float* bbase, uint32_t bcnt, uint32_t pen4, float penalty,
+                                              float inv_t, float M, float xthr, float s, const ExpTable tab,
+                                              uint32_t* events) {
+    const int lane = threadIdx.x & 31;
+    float e[4];
+    {
+        const float ninf = __int_as_float(0xFF800000);
+        float4 q = make_float4(ninf, ninf, ninf, ninf);
+        if (4u * (uint32_t)lane < bcnt) q = __ldg(reinterpret_cast<const float4*>(bbase + 4 * lane));
+        float x[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if ((pen4 >> c) & 1u) x[c] = penalise(x[c], penalty);
+            e[c] = 0.0f;
+            if (x[c] > xthr) {
+                const float d = d_of(x[c], inv_t, M);
+                e[c] = d == 0.0f ? 1.0f : exact_expf(d, tab);
+            }
+        }
+    }
+    if (s == 0.0f) {  // (every lane adds all 128 in order: the same sum everywhere)
+#pragma unroll 4
+        for (int L = 0; L < 32; ++L)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e[c], L));
+        if (lane == 0) *events += 128u;
+        return s;
+    }
+    int consumed = -1;
+    for (int round = 0; round < 129; ++round) {
+        const int uu = unit_exp(s), u1 = uu + 1;  // (the sum only grows)
+        uint32_t a0[4], a1[4], sp0 = 0, sp1 = 0, t0 = 0, t1 = 0;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            a0[c] = a1[c] = 0u;
+            if (4 * lane + c > consumed && e[c] != 0.0f) {
+                const Cls2 k = classify2(__float_as_uint(e[c]), uu, +1);
+                a0[c] = k.inc0;
+                a1[c] = k.inc1;
+                sp0 |= (uint32_t)k.spec0 << c;
+                sp1 |= (uint32_t)k.spec1 << c;
+            }
+            t0 = sat_add(t0, a0[c]);
+            t1 = sat_add(t1, a1[c]);
+        }
+        const uint32_t l0 = warp_incl_scan(t0), l1 = warp_incl_scan(t1);
+        uint32_t x0 = __shfl_up_sync(0xFFFFFFFFu, l0, 1), x1 = __shfl_up_sync(0xFFFFFFFFu, l1, 1);
+        if (lane == 0) x0 = x1 = 0u;  // (not l - t: the scans saturate)
+        const uint32_t tot0 = __shfl_sync(0xFFFFFFFFu, l0, 31), tot1 = __shfl_sync(0xFFFFFFFFu, l1, 31);
+        uint32_t base0 = 0, base1 = 0;  // channel prefixes at the last ordered step
+        bool again = false;
+        for (int step = 0; step < 129; ++step) {
+            const int uc = unit_exp(s);
+            const int ch = uc == uu ? 0 : (uc == u1 ? 1 : -1);
+            if (ch < 0) {  // a second grid change: classify the rest again
+                again = true;
+                break;
+            }
+            const uint32_t A = grid_count(s, uc);
+            const uint32_t bse = ch ? base1 : base0;
+            const uint32_t spm = ch ? sp1 : sp0;
+            uint32_t run = ch ? x1 : x0, r0 = x0, r1 = x1;
+            uint32_t cand = 0xFFFFFFFFu, pre = 0, cb0 = 0, cb1 = 0;
+            float val = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const uint32_t pr = run;
+                run = sat_add(run, ch ? a1[c] : a0[c]);
+                r0 = sat_add(r0, a0[c]);
+                r1 = sat_add(r1, a1[c]);
+                if (cand == 0xFFFFFFFFu && 4 * lane + c > consumed &&
+                    (((spm >> c) & 1u) || A + (run - bse) >= kTwo24)) {
+                    cand = (uint32_t)(4 * lane + c);
+                    pre = pr;
+                    cb0 = r0;
+                    cb1 = r1;
+                    val = e[c];
+                }
+            }
+            const uint32_t first = __reduce_min_sync(0xFFFFFFFFu, cand);
+            if (first == 0xFFFFFFFFu) {
+                s = grid_value(uc, A + ((ch ? tot1 : tot0) - bse));  // (below 2^24: no crossing)
+                break;
+            }
+            const int owner = (int)(first >> 2);
+            const float after = __fadd_rn(grid_value(uc, A + (pre - bse)), val);  // (meaningful in the owner)
+            s = __shfl_sync(0xFFFFFFFFu, after, owner);
+            base0 = __shfl_sync(0xFFFFFFFFu, cb0, owner);
+            base1 = __shfl_sync(0xFFFFFFFFu, cb1, owner);
+            consumed = (int)first;
+            if (lane == 0) ++*events;
+        }
+        if (!again) break;
+    }
+    return s;
+}
+
+// ------------------------------------------------------------------- sum ----
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+constexpr int kSumWarps = 4;  // rows per block of the sum stage (one warp each)
+
+// The running sum over tile t (its grid records from classify): block by block, each block
+// added in one step where the sum stays on a grid it was classified for, else walked.
+__device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g, uint32_t r, uint32_t t, float s,
+                                               const lrs_params& P, float inv_t, float M, const uint32_t* hrow,
+                                               uint32_t hstart, uint32_t hlen, uint32_t* wb, const ExpTable tab,
+                                               uint32_t* events, uint32_t* walks) {
+    const int lane = threadIdx.x & 31;
+    const uint64_t ti = (uint64_t)r * S.nt + t;
+    const TilePrep tp = S.tprep[ti];
+    const uint32_t bflags = S.tres[ti].bflags;
+    uint32_t c0 = 0, c1 = 0;
+    if (lane < 8) {
+        c0 = S.tres[ti].b0[lane];
+        c1 = S.tres[ti].b1[lane];
+    }
+    const uint32_t cnt = chunk_count(g, t);
+    const uint32_t g0 = g.head + t * kTile;
+    const bool pen_on = P.repetition_penalty != 1.0f;
+    bool pen = false;
+    if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
+    const uint32_t nb = (cnt + 127u) / 128u;
+    for (uint32_t b0 = 0; b0 < nb;) {
+        const uint32_t b = (uint32_t)lane;
+        const bool in = b >= b0 && b < nb;
+        const bool live = in && ((bflags >> b) & 1u);
+        const int uu = unit_exp(s);
+        const uint32_t A = grid_count(s, uu);
+        uint32_t inc = 0;
+        bool ok = !live;
+        if (live) {
+            if (uu == tp.u0 && !((bflags >> (8 + b)) & 1u)) {
+                inc = c0;
+                ok = true;
+            } else if (uu == tp.u0 + 1 && !((bflags >> (16 + b)) & 1u)) {
+                inc = c1;
+                ok = true;
+            }
+        }
+        const uint32_t incl = warp_incl_scan(inc);
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, in && (!ok || A + incl >= kTwo24));
+        if (!m) {
+            s = grid_value(uu, A + __shfl_sync(0xFFFFFFFFu, incl, 31));
+            break;
+        }
+        const int L = __ffs(m) - 1;
+        uint32_t excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+        if (lane == 0) excl = 0u;
+        s = grid_value(uu, A + __shfl_sync(0xFFFFFFFFu, excl, L));
+        const uint32_t bw = (uint32_t)L;
+        const uint32_t pen4 = pen ? (wb[4 * bw + (lane >> 3)] >> (4 * (lane & 7))) & 15u : 0u;
+        const uint32_t bcnt = cnt - 128u * bw < 128u ? cnt - 128u * bw : 128u;
+        s = warp_walk_block(g.row + g0 + 128u * bw, bcnt, pen4, P.repetition_penalty, inv_t, M, tp.xthr, s, tab, events);
+        ++*walks;
+        b0 = bw + 1;
+    }
+    return s;
+}
+
+// One warp per row: the exact softmax denominator (ops.rs:408-411) in index order, from the
+// tile results where the running sum stays on a grid a tile was classified for, stepping
+// through the tile's blocks otherwise.  Writes S (or a failed bound: the row goes to
+// lrs_sample_rows).
+__global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs S) {
+    __shared__ uint32_t wbits[kSumWarps * 32];
+    const lrs_kernel_args_t& a = S.a;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t r = blockIdx.x * kSumWarps + warp;
+    if (r >= a.rows) return;
+    RowPrep* rpp = S.rprep + r;
+    const uint32_t flags = rpp->flags;
+    if (flags & (kRowDone | kRowFallback)) return;
+    const long long t_start = clock64();
+    uint32_t walks = 0, events = 0;
+    const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
+    const lrs_params P = a.params[r];
+    const Geo g = row_geometry(a, r);
+    const float M = rpp->M, inv_t = rpp->inv_t;
+    const bool pen_on = P.repetition_penalty != 1.0f;
+    const uint32_t hlen = (pen_on && a.hist_len) ? a.hist_len[r] : 0u;
+    const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
+    const uint32_t hstart = window_start(P, hlen);
+    uint32_t* wb = wbits + warp * 32;
+    const uint32_t edges = g.head + g.tail;
+    const bool mine = (uint32_t)lane < edges;
+    const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+    float ex = mine ? g.row[egi] : 0.0f;
+    for (uint32_t e = 0; e < edges; ++e) {
+        const uint32_t gi = __shfl_sync(0xFFFFFFFFu, egi, (int)e);
+        const bool hit = pen_on && in_window(hrow, hstart, hlen, gi);
+        if (hit && (uint32_t)lane == e) ex = penalise(ex, P.repetition_penalty);
+    }
+    float de = 0.0f, ee = 0.0f;
+    bool exe = true;
+    if (mine) {
+        de = d_of(ex, inv_t, M);
+        exe = de == 0.0f;
+        ee = exe ? 1.0f : expf(de);
+    }
+    const uint32_t nt = g.nchunks;
+    // the tiles likely to be stepped through, brought into L2 ahead of the scan (a lane a 128-byte line)
+    for (uint32_t t0 = 0; t0 < nt; t0 += 32) {
+        const uint32_t t = t0 + (uint32_t)lane;
+        bool want = false;
+        if (t < nt) {
+            const uint32_t pf = S.tprep[(uint64_t)r * S.nt + t].flags, rf = S.tres[(uint64_t)r * S.nt + t].flags;
+            want = t == 0 || (pf & (kTileWalk | kTileLikelyWalk)) ||
+                   ((rf & kTileLive) && (rf & (kTileSp0 | kTileSp1)) == (kTileSp0 | kTileSp1));
+        }
+        for (unsigned m = __ballot_sync(0xFFFFFFFFu, want); m; m &= m - 1u) {
+            const uint32_t tw = t0 + (uint32_t)(__ffs(m) - 1);
+            if ((uint32_t)lane * 32u < chunk_count(g, tw)) prefetch_l2(g.row + g.head + tw * kTile + lane * 32u);
+        }
+    }
+    // the head opens the sum
+    float s = warp_serial_add(0.0f, ee, de, exe, 0, (int)g.head, exptab);
+    bool bad = false;
+    for (uint32_t t0 = 0; t0 < nt;) {
+        const uint32_t t = t0 + (uint32_t)lane;
+        const bool in = t < nt;
+        uint32_t rflags = 0, rt0 = 0, rt1 = 0;
+        int u0 = 0;
+        if (in) {
+            const TileRes* rs = S.tres + (uint64_t)r * S.nt + t;
+            rflags = rs->flags;
+            rt0 = rs->t0;
+            rt1 = rs->t1;
+            u0 = S.tprep[(uint64_t)r * S.nt + t].u0;
+        }
+        const int uu = unit_exp(s);
+        const uint32_t A = grid_count(s, uu);
+        // a tile applies in one step when the running sum stays on a grid it was classified for
+        uint32_t inc = 0;
+        bool ok = !in || !(rflags & kTileLive);
+        if (in && (rflags & kTileLive)) {
+            if (uu == u0 && !(rflags & kTileSp0)) {
+                inc = rt0;
+                ok = true;
+            } else if (uu == u0 + 1 && !(rflags & kTileSp1)) {
+                inc = rt1;
+                ok = true;
+            }
+        }
+        const uint32_t incl = warp_incl_scan(inc);
+        // a tile whose rigorous lower grid lies above the running sum's breaks the bound that
+        // made its dead elements dead: checked below with the exact sum
+        const bool stop = in && (!ok || A + incl >= kTwo24 || u0 > uu);
+        const unsigned m = __ballot_sync(0xFFFFFFFFu, stop);
+        if (!m) {
+            s = grid_value(uu, A + __shfl_sync(0xFFFFFFFFu, incl, 31));
+            t0 += 32;
+            continue;
+        }
+        const int L = __ffs(m) - 1;
+        uint32_t excl = __shfl_up_sync(0xFFFFFFFFu, incl, 1);
+        if (lane == 0) excl = 0u;
+        s = grid_value(uu, A + __shfl_sync(0xFFFFFFFFu, excl, L));
+        const uint32_t tw = t0 + (uint32_t)L;
+        if (unit_exp(s) < __shfl_sync(0xFFFFFFFFu, u0, L)) {  // the estimate's lower bound failed
+            bad = true;
+            break;
+        }
+        s = warp_tile_blocks(S, g, r, tw, s, P, inv_t, M, hrow, hstart, hlen, wb, exptab, &events, &walks);
+        t0 = tw + 1;
+    }
+    // the tail closes the sum
+    if (!bad) s = warp_serial_add(s, ee, de, exe, (int)g.head, (int)g.tail, exptab);
+    if (lane == 0) {
+        if (bad) {
+            rpp->flags = flags | kRowFallback;
+            stage_fallback(S, r);
+        } else {
+            rpp->pad[0] = __float_as_uint(s);
+            rpp->pad[1] = events;
+        }
+        const long long dt = clock64() - t_start;
+        rpp->cyc_sum = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
+        rpp->walks = walks;
+    }
+}
+
+// ----------------------------------------------------------------- finish ----
+// A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA histograms
+// d = fl(x' - M) over the whole row in buckets of 1/32 (counts and approximate masses), takes
+// the deepest bucket edge whose elements fit in the list's capacity (if their mass can reach
+// top_p), and gathers those elements' exact keys (p desc, index asc) into keys.  Returns their
+// number (cand: the edge), or 0xFFFFFFFF if the nucleus cannot fit.
+__device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r, const lrs_params& P, float M, float inv,
+                                                  const ExpTable tab, unsigned long long* keys, RowShared& sh,
+                                                  float& cand) {
+    const lrs_kernel_args_t& a = S.a;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const Geo g = row_geometry(a, r);
+    const float inv_t = __fdiv_rn(1.0f, P.temperature);
+    const bool pen_on = P.repetition_penalty != 1.0f;
+    const uint32_t hlen = (pen_on && a.hist_len) ? a.hist_len[r] : 0u;
+    const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
+    const uint32_t hstart = window_start(P, hlen);
+    // counts and approximate masses in the keys area (their first 2 x 580 words)
+    uint32_t* cnts = reinterpret_cast<uint32_t*>(keys);
+    float* mass = reinterpret_cast<float*>(keys) + kStageNucleusBuckets;
+    for (int b = tid; b < kStageNucleusBuckets; b += kThreads) {
+        cnts[b] = 0u;
+        mass[b] = 0.0f;
+    }
+    csync();
+    auto visit = [&](bool gather, float th, uint32_t* nkeys) {
+        // edge elements (warp 0) and the tiles (warp w: tiles w, w + 7, ...)
+        if (warp == 0) {
+            const uint32_t edges = g.head + g.tail;
+            const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+            float x = (uint32_t)lane < edges ? g.row[egi] : __int_as_float(0xFF800000);
+            for (uint32_t e = 0; e < edges; ++e) {
+                const uint32_t gi = __shfl_sync(0xFFFFFFFFu, egi, (int)e);
+                const bool hit = pen_on && in_window(hrow, hstart, hlen, gi);
+                if (hit && (uint32_t)lane == e) x = penalise(x, P.repetition_penalty);
+            }
+            if ((uint32_t)lane < edges) {
+                const float d = d_of(x, inv_t, M);
+                if (!gather) {
+                    if (d >= -(float)(kStageNucleusBuckets - 1) / 32.0f) {
+                        const int b = (int)fminf(-d * 32.0f, (float)(kStageNucleusBuckets - 2));
+                        atomicAdd(&cnts[b], 1u);
+                        atomicAdd(&mass[b], expf(d));
+                    }
+                } else if (d >= th) {
+                    const uint32_t o = atomicAdd(nkeys, 1u);
+                    if (o < kStageListCap) {
+                        const float p = __fmul_rn(exact_expf(d, tab), inv);
+                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) | egi;
+                    }
+                }
+            }
+        }
+        uint32_t* wb = sh.hist256 + warp * 32;  // (the warp's window words)
+        for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
+            const uint32_t cnt = chunk_count(g, t);
+            const uint32_t g0 = g.head + t * kTile;
+            bool pen = false;
+            if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
+            float v[32];
+            load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+#pragma unroll 4
+            for (int i = 0; i < 32; ++i) {
+                const float d = d_of(v[i], inv_t, M);
+                if (!gather) {
+                    if (d >= -(float)(kStageNucleusBuckets - 1) / 32.0f) {
+                        const int b = (int)fminf(-d * 32.0f, (float)(kStageNucleusBuckets - 2));
+                        atomicAdd(&cnts[b], 1u);
+                        atomicAdd(&mass[b], expf(d));
+                    }
+                } else if (d >= th) {
+                    const uint32_t o = atomicAdd(nkeys, 1u);
+                    if (o < kStageListCap) {
+                        const float p = __fmul_rn(exact_expf(d, tab), inv);
+                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) |
+                                  (g0 + 128u * (i >> 2) + 4u * lane + (i & 3));
+                    }
+                }
+            }
+        }
+    };
+    visit(false, 0.0f, nullptr);
+    csync();
+    if (warp == 0) {
+        // the deepest bucket whose prefix count fits; its prefix mass must reach top_p
+        uint32_t acc = 0;
+        float am = 0.0f;
+        int best = -1;
+        float best_mass = 0.0f;
+        for (int base = 0; base < kStageNucleusBuckets - 1; base += 32) {
+            const int b = base + lane;
+            const uint32_t c = b < kStageNucleusBuckets - 1 ? cnts[b] : 0u;
+            const float m = b < kStageNucleusBuckets - 1 ? mass[b] : 0.0f;
+            const uint32_t ci = warp_incl_scan_plain(c) + acc;
+            const float mi = warp_incl_scan_f(m) + am;
+            const unsigned fit = __ballot_sync(0xFFFFFFFFu, b < kStageNucleusBuckets - 1 && ci <= kStageListCap);
+            if (fit) {
+                const int L = 31 - __clz(fit);
+                best = base + L;
+                best_mass = __shfl_sync(0xFFFFFFFFu, mi, L);
+            }
+            acc = __shfl_sync(0xFFFFFFFFu, ci, 31);
+            am = __shfl_sync(0xFFFFFFFFu, mi, 31);
+            if (acc > kStageListCap) break;
+        }
+        if (lane == 0) {
+            const bool ok = best >= 0 && (double)best_mass * (double)inv >= (double)P.top_p + 0x1p-16;
+            sh.misc[0] = ok ? (uint32_t)best : 0xFFFFFFFFu;
+            sh.misc[1] = 0u;  // (the gather's key counter)
+        }
+    }
+    csync();
+    const uint32_t best = sh.misc[0];
+    if (best == 0xFFFFFFFFu) return 0xFFFFFFFFu;
+    cand = -(float)(best + 1) / 32.0f;
+    visit(true, cand, &sh.misc[1]);
+    csync();
+    const uint32_t nkeys = sh.misc[1];
+    csync();
+    return nkeys <= kStageListCap ? nkeys : 0xFFFFFFFFu;
+}
+
+// Sequential f32 run over sorted probabilities keys[0..cnt) (sampler.rs:137-139 / 148-151 /
+// 156-158): dir > 0 adds until s >= thr, dir < 0 subtracts until s <= 0.  Short runs go one
+// by one on thread 0; long ones chunk by chunk with the block's exact emulation (acc_tile).
+// Returns the stop position or -1; every thread gets the same s.
+__device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t cnt, int dir, float& s, float thr,
+                                       RowShared& sh) {
+    if (cnt <= 512u) {
+        if (threadIdx.x == 0) {
+            float cur = s;
+            int stop = -1;
+            for (uint32_t i = 0; i < cnt; ++i) {
+                const float p = __uint_as_float(~(uint32_t)(keys[i] >> 32));
+                cur = dir > 0 ? __fadd_rn(cur, p) : __fsub_rn(cur, p);
+                if (dir > 0 ? cur >= thr : cur <= 0.0f) {
+                    stop = (int)i;
+                    break;
+                }
+            }
+            sh.fstate = cur;
+            sh.stop = stop;
+        }
+        csync();
+        s = sh.fstate;
+        const int st = sh.stop;
+        csync();
+        return st;
+    }
+    for (uint32_t b = 0; b < cnt; b += kChunk) {
+        const uint32_t tc = cnt - b < (uint32_t)kChunk ? cnt - b : (uint32_t)kChunk;
+        float v[kVpt];
+        load_sorted_tile(keys + b, tc, v);
+        uint32_t ex = 0xFFFFFFFFu;
+        const int st = acc_tile(v, ex, (int)tc, dir, s, thr, NoExact(), sh);
+        if (st >= 0) return (int)b + st;
+    }
+    return -1;
+}
+
+// One CTA per row: the candidates' exact probabilities p = fl(libm expf(d) * (1 / S))
+// (sampler.rs:129-131, ops.rs:409-416), sorted (p desc, index asc), then top-k, the top-p
+// cut, the survivor sum and the draw (sampler.rs:122-162).
+__global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) {
+    extern __shared__ __align__(16) unsigned long long keys[];  // kStageListCap
+    __shared__ RowShared sh;
+    const lrs_kernel_args_t& a = S.a;
+    const uint32_t r = blockIdx.x;
+    const int tid = threadIdx.x;
+    const RowPrep rp = S.rprep[r];
+    if (rp.flags & (kRowDone | kRowFallback)) return;
+    const long long t_start = clock64();
+    const uint32_t nk = S.list_n[r];
+    if (nk > kStageListCap && (rp.flags & kRowPathK)) {  // a top-k list overflow (ties): lrs_sample_rows
+        if (tid == 0) stage_fallback(S, r);
+        return;
+    }
+    const float kInf = __int_as_float(0x7F800000);
+    const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
+    const lrs_params P = a.params[r];
+    const float M = rp.M;
+    const float Ssum = __uint_as_float(rp.pad[0]);
+    const float inv = __fdiv_rn(1.0f, Ssum);  // ops.rs:413
+    const bool topp_on = P.top_p > 0.0f && P.top_p < 1.0f;
+    if (tid == 0) {
+        sh.misc[7] = 0u;
+        sh.events = 0u;
+    }
+    uint32_t n_keys = nk;
+    float cand = rp.cand;
+    float cum = 0.0f;
+    int stp = -1;
+    uint32_t kk = 0, cut = 0;
+    for (int attempt = nk > kStageListCap ? 1 : 0; attempt < 2; ++attempt) {
+        if (attempt == 0) {
+            const uint2* lst = S.lists + (uint64_t)r * kStageListCap;
+            for (uint32_t i = tid; i < nk; i += kThreads) {
+                const uint2 e = lst[i];
+                const float p = __fmul_rn(exact_expf(__fsub_rn(__uint_as_float(e.x), M), exptab), inv);
+                keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | e.y;
+            }
+        } else {
+            // The nucleus reaches deeper than the list: gather it from the row, at the deepest
+            // bucket edge (width 1/32 in d) whose elements fit in the list's capacity.
+            csync();
+            n_keys = regather_nucleus(S, r, P, M, inv, exptab, keys, sh, cand);
+            if (n_keys == 0xFFFFFFFFu) {
+                if (tid == 0) stage_fallback(S, r);
+                return;
+            }
+        }
+        csync();
+        bitonic_sort_u64(keys, n_keys);  // (p desc, index asc): the reference's order (see the oracle on ties)
+        kk = rp.k < n_keys ? rp.k : n_keys;  // (path K: the list holds the top k; path N: the nucleus)
+        // top-p over the first kk (sampler.rs:135-146); the survivor sum is the same sequence up
+        // to the cutoff (sampler.rs:148-151)
+        cum = 0.0f;
+        stp = sorted_run(keys, kk, +1, cum, topp_on ? P.top_p : kInf, sh);
+        cut = stp >= 0 ? (uint32_t)stp + 1 : kk;
+        // path N: the list holds every element with d >= cand, so its sorted order is the row's
+        // as far as its probabilities exceed the largest one an element outside can have; the
+        // cut (top_p reached, or k reached) must lie there, unless the list is the whole row
+        if ((rp.flags & kRowPathK) || n_keys >= a.n) break;
+        const float p_out = __fmul_rn(exact_expf(cand, exptab), inv);
+        const bool inside = (stp >= 0 || kk == rp.k) && cut > 0 &&
+                            __uint_as_float(~(uint32_t)(keys[cut - 1] >> 32)) > p_out;
+        if (inside) break;
+        if (attempt == 1) {
+            if (tid == 0) stage_fallback(S, r);
+            return;
+        }
+    }
+    unsigned long long st = a.state[r];
+    uint32_t ps = 0;
+    float r0 = 0.0f;
+    if (cum > 0.0f) {
+        r0 = __fmul_rn(next_f32(&st), cum);  // sampler.rs:155
+        float rv = r0;
+        const int w = sorted_run(keys, cut, -1, rv, 0.0f, sh);
+        ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
+    }
+    if (tid != 0) return;
+    if (sh.misc[7]) {  // (an internal bound of the exact emulation failed: should not happen)
+        stage_fallback(S, r);
+        return;
+    }
+    const unsigned long long chosen = keys[ps];
+    lrs_row_info inf = blank_info(2u, rp.k);
+    inf.token = (uint32_t)(chosen & 0xFFFFFFFFu);
+    inf.prob = __uint_as_float(~(uint32_t)(chosen >> 32));
+    inf.cutoff = cut;
+    inf.pos = ps;
+    inf.max = M;
+    inf.sum_exp = Ssum;
+    inf.surv_sum = cum;
+    inf.r0 = r0;
+    inf.n_cand = n_keys;
+    inf.events = rp.pad[1];
+    inf.cycles[0] = rp.cyc_prep;  // (implementation detail: the stages' SM cycles and walked blocks)
+    inf.cycles[1] = rp.cyc_sum;
+    const long long dt = clock64() - t_start;
+    inf.cycles[2] = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
+    inf.cycles[4] = 1u;  // (finished by the staged pipeline)
+    inf.cycles[5] = rp.walks;
+    write_row(a, r, LRS_OK, inf.token, inf.prob, true, st, inf);
+}

@@ -24,7 +24,7 @@ NVCC_FLAGS = [
     "-Xptxas", "-warn-spills",
 ]
 SOURCES = ["lrs_kernels.cu", "lrs_api.cu", "lrs_noalloc.cu"]
-HEADERS = ["lrs_device.cuh", "lrs_grid.h", "lrs_kernels_decl.cuh"]
+HEADERS = ["lrs_device.cuh", "lrs_grid.h", "lrs_kernels_decl.cuh", "lrs_stages.cuh"]
 
 
 def _newer(target: str, deps: list[str]) -> bool:
