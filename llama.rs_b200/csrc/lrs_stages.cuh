@@ -40,6 +40,7 @@ constexpr uint32_t kStageListCap = 8192;           // candidate-list entries per
 constexpr int kStageNucleusBuckets = 580;          // mass buckets of width 1/32 in (M - x')
 constexpr uint32_t kStageNucleusRank = 2048;       // top-p lists reach at least the lane maximum of this rank
 constexpr uint32_t kStageMaxTiles = 256;           // tiles of the longest stochastic row the stages take (n <= 262,144)
+constexpr uint32_t kClassifyGroup = 8;             // consecutive tiles of a row per classify task
 // flags of a row's prep record
 constexpr uint32_t kRowDone = 1u;        // outputs written by the prep (greedy, NaN, n <= 1)
 constexpr uint32_t kRowFallback = 2u;    // sampled by lrs_sample_rows afterwards
@@ -143,6 +144,8 @@ __device__ __forceinline__ void load_tile_blocks(const float* base, uint32_t cnt
         }
     }
 }
+
+__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 __device__ __forceinline__ uint32_t window_start(const lrs_params& P, uint32_t hlen) {
     return (P.repeat_last_n != 0 && hlen > P.repeat_last_n) ? hlen - P.repeat_last_n : 0u;  // sampler.rs:84-88
@@ -675,19 +678,46 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageA
     uint32_t* bc = bcount + warp * 17;
     uint32_t* bfl = bc + 16;
     const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
-    const uint64_t tasks = (uint64_t)a.rows * S.nt;
+    // a warp's task: kClassifyGroup consecutive tiles of one row (one read of the row's record,
+    // the tiles' records in one round trip, the tiles that need their data brought into L2
+    // before the first is read)
+    const uint32_t groups = (S.nt + kClassifyGroup - 1) / kClassifyGroup;
+    const uint64_t tasks = (uint64_t)a.rows * groups;
     const uint64_t stride = (uint64_t)gridDim.x * kStageWarps;
     for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
-        const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
+        const uint32_t r = (uint32_t)(task / groups), t0 = (uint32_t)(task % groups) * kClassifyGroup;
         const RowPrep rp = S.rprep[r];
         if (rp.flags & (kRowDone | kRowFallback)) continue;
         const Geo g = row_geometry(a, r);
-        if (t >= g.nchunks) continue;
-        const uint64_t ti = (uint64_t)r * S.nt + t;
-        const TilePrep tp = S.tprep[ti];
-        const float mt = S.tstat[ti].x;
+        if (t0 >= g.nchunks) continue;
+        const uint32_t tn = min((uint32_t)kClassifyGroup, g.nchunks - t0);
         const float M = rp.M, inv_t = rp.inv_t;
         const bool pathK = rp.flags & kRowPathK;
+        // lane j < tn: tile t0 + j's records and whether it needs its data
+        TilePrep tpl{0, 0u, 0.0f, 0.0f};
+        float mtl = 0.0f;
+        bool need = false;
+        if ((uint32_t)lane < tn) {
+            const uint64_t tj = (uint64_t)r * S.nt + t0 + lane;
+            tpl = S.tprep[tj];
+            mtl = S.tstat[tj].x;
+            const float dm = __fsub_rn(mtl, M);
+            need = !(dm < tpl.dthr) || (pathK ? !(mtl < rp.cand) : !(dm < rp.cand));
+        }
+        const unsigned needm = __ballot_sync(0xFFFFFFFFu, need);
+        for (unsigned m = needm; m; m &= m - 1u) {
+            const uint32_t tw = t0 + (uint32_t)(__ffs(m) - 1);
+            if ((uint32_t)lane * 32u < chunk_count(g, tw)) prefetch_l2(g.row + g.head + tw * kTile + lane * 32u);
+        }
+        for (uint32_t j = 0; j < tn; ++j) {
+        const uint32_t t = t0 + j;
+        const uint64_t ti = (uint64_t)r * S.nt + t;
+        TilePrep tp;
+        tp.u0 = __shfl_sync(0xFFFFFFFFu, tpl.u0, (int)j);
+        tp.flags = __shfl_sync(0xFFFFFFFFu, tpl.flags, (int)j);
+        tp.xthr = __shfl_sync(0xFFFFFFFFu, tpl.xthr, (int)j);
+        tp.dthr = __shfl_sync(0xFFFFFFFFu, tpl.dthr, (int)j);
+        const float mt = __shfl_sync(0xFFFFFFFFu, mtl, (int)j);
         const float dmax = __fsub_rn(mt, M);
         const bool sum_live = !(dmax < tp.dthr);
         const bool cand_live = pathK ? !(mt < rp.cand) : !(dmax < rp.cand);
@@ -796,6 +826,7 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageA
         if (sum_live && lane < 8) {
             S.tres[ti].b0[lane] = res.b0[lane];
             S.tres[ti].b1[lane] = res.b1[lane];
+        }
         }
     }
 }
@@ -906,7 +937,6 @@ __device__ __noinline__ float warp_walk_block(const float* bbase, uint32_t bcnt,
 }
 
 // ------------------------------------------------------------------- sum ----
-__device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
 
 constexpr int kSumWarps = 4;  // rows per block of the sum stage (one warp each)
 
@@ -1091,11 +1121,12 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
 }
 
 // ----------------------------------------------------------------- finish ----
-// A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA histograms
-// d = fl(x' - M) over the whole row in buckets of 1/32 (counts and approximate masses), takes
-// the deepest bucket edge whose elements fit in the list's capacity (if their mass can reach
-// top_p), and gathers those elements' exact keys (p desc, index asc) into keys.  Returns their
-// number (cand: the edge), or 0xFFFFFFFF if the nucleus cannot fit.
+// A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA counts the
+// row's elements by d = fl(x' - M) in buckets of 1/32 (a histogram per warp, increments
+// aggregated over the lanes that share a bucket), takes the deepest bucket edge whose
+// elements fit in the list's capacity, and gathers those elements' exact keys (p desc, index
+// asc) into keys.  Returns their number (cand: the edge), or 0xFFFFFFFF if none fits.  The
+// finish checks that the nucleus lies inside them.
 __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r, const lrs_params& P, float M, float inv,
                                                   const ExpTable tab, unsigned long long* keys, RowShared& sh,
                                                   float& cand) {
@@ -1107,105 +1138,97 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     const uint32_t hlen = (pen_on && a.hist_len) ? a.hist_len[r] : 0u;
     const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
     const uint32_t hstart = window_start(P, hlen);
-    // counts and approximate masses in the keys area (their first 2 x 580 words)
+    constexpr int kB = kStageNucleusBuckets;
+    // per-warp counts in the keys area (kWarps x kB words), summed into warp 0's row below
     uint32_t* cnts = reinterpret_cast<uint32_t*>(keys);
-    float* mass = reinterpret_cast<float*>(keys) + kStageNucleusBuckets;
-    for (int b = tid; b < kStageNucleusBuckets; b += kThreads) {
-        cnts[b] = 0u;
-        mass[b] = 0.0f;
-    }
+    for (int b = tid; b < kWarps * kB; b += kThreads) cnts[b] = 0u;
+    if (tid == 0) sh.misc[1] = 0u;  // (the gather's key counter)
     csync();
-    auto visit = [&](bool gather, float th, uint32_t* nkeys) {
-        // edge elements (warp 0) and the tiles (warp w: tiles w, w + 7, ...)
-        if (warp == 0) {
-            const uint32_t edges = g.head + g.tail;
-            const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
-            float x = (uint32_t)lane < edges ? g.row[egi] : __int_as_float(0xFF800000);
-            for (uint32_t e = 0; e < edges; ++e) {
-                const uint32_t gi = __shfl_sync(0xFFFFFFFFu, egi, (int)e);
-                const bool hit = pen_on && in_window(hrow, hstart, hlen, gi);
-                if (hit && (uint32_t)lane == e) x = penalise(x, P.repetition_penalty);
-            }
-            if ((uint32_t)lane < edges) {
-                const float d = d_of(x, inv_t, M);
-                if (!gather) {
-                    if (d >= -(float)(kStageNucleusBuckets - 1) / 32.0f) {
-                        const int b = (int)fminf(-d * 32.0f, (float)(kStageNucleusBuckets - 2));
-                        atomicAdd(&cnts[b], 1u);
-                        atomicAdd(&mass[b], expf(d));
-                    }
-                } else if (d >= th) {
-                    const uint32_t o = atomicAdd(nkeys, 1u);
-                    if (o < kStageListCap) {
-                        const float p = __fmul_rn(exact_expf(d, tab), inv);
-                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) | egi;
-                    }
-                }
-            }
-        }
-        uint32_t* wb = sh.hist256 + warp * 32;  // (the warp's window words)
-        for (uint32_t t = (uint32_t)warp; t < g.nchunks; t += kWarps) {
-            const uint32_t cnt = chunk_count(g, t);
-            const uint32_t g0 = g.head + t * kTile;
-            bool pen = false;
-            if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
+    uint32_t* wc = cnts + warp * kB;
+    uint32_t* wb = sh.hist256 + warp * 32;  // (the warp's window words)
+    auto bucket_of = [](float d) -> int {   // kB - 1: below the histogram's range
+        return d >= -(float)(kB - 1) / 32.0f ? (int)fminf(-d * 32.0f, (float)(kB - 2)) : kB - 1;
+    };
+    auto visit = [&](bool gather, float th) {
+        // edge elements (warp 0, lanes 0 .. edges-1), then the tiles (warp w: tiles w, w + 7, ...)
+        const uint32_t edges = g.head + g.tail;
+        for (uint32_t t = (uint32_t)warp; t < g.nchunks + (warp == 0 ? 1u : 0u); t += kWarps) {
+            const bool edge = t == g.nchunks;  // (warp 0's last item)
             float v[32];
-            load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+            uint32_t g0 = 0;
+            if (!edge) {
+                const uint32_t cnt = chunk_count(g, t);
+                g0 = g.head + t * kTile;
+                bool pen = false;
+                if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
+                load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+            } else {
+                const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+                float x = (uint32_t)lane < edges ? g.row[egi] : __int_as_float(0xFF800000);
+                for (uint32_t e = 0; e < edges; ++e) {
+                    const uint32_t gi = __shfl_sync(0xFFFFFFFFu, egi, (int)e);
+                    const bool hit = pen_on && in_window(hrow, hstart, hlen, gi);
+                    if (hit && (uint32_t)lane == e) x = penalise(x, P.repetition_penalty);
+                }
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0xFF800000);
+                v[0] = x;
+            }
 #pragma unroll 4
             for (int i = 0; i < 32; ++i) {
                 const float d = d_of(v[i], inv_t, M);
+                uint32_t gi;
+                if (!edge)
+                    gi = g0 + 128u * (i >> 2) + 4u * lane + (i & 3);
+                else
+                    gi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
                 if (!gather) {
-                    if (d >= -(float)(kStageNucleusBuckets - 1) / 32.0f) {
-                        const int b = (int)fminf(-d * 32.0f, (float)(kStageNucleusBuckets - 2));
-                        atomicAdd(&cnts[b], 1u);
-                        atomicAdd(&mass[b], expf(d));
-                    }
-                } else if (d >= th) {
-                    const uint32_t o = atomicAdd(nkeys, 1u);
-                    if (o < kStageListCap) {
+                    const int b = bucket_of(d);
+                    const unsigned peers = __match_any_sync(0xFFFFFFFFu, b);
+                    if (b < kB - 1 && lane == __ffs(peers) - 1) atomicAdd(&wc[b], (uint32_t)__popc(peers));
+                } else {
+                    const bool take = d >= th;
+                    const unsigned m = __ballot_sync(0xFFFFFFFFu, take);
+                    uint32_t o = 0;
+                    if (m && lane == 0) o = atomicAdd(&sh.misc[1], (uint32_t)__popc(m));
+                    o = __shfl_sync(0xFFFFFFFFu, o, 0) + (uint32_t)__popc(m & ((1u << lane) - 1u));
+                    if (take && o < kStageListCap) {
                         const float p = __fmul_rn(exact_expf(d, tab), inv);
-                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) |
-                                  (g0 + 128u * (i >> 2) + 4u * lane + (i & 3));
+                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) | gi;
                     }
                 }
             }
         }
     };
-    visit(false, 0.0f, nullptr);
+    visit(false, 0.0f);
+    csync();
+    for (int b = tid; b < kB; b += kThreads) {
+        uint32_t c = 0;
+        for (int w = 0; w < kWarps; ++w) c += cnts[w * kB + b];
+        cnts[b] = c;  // (row 0 holds the totals: its own entry is read before it is written)
+    }
     csync();
     if (warp == 0) {
-        // the deepest bucket whose prefix count fits; its prefix mass must reach top_p
+        // the deepest bucket whose prefix count fits in the list
         uint32_t acc = 0;
-        float am = 0.0f;
         int best = -1;
-        float best_mass = 0.0f;
-        for (int base = 0; base < kStageNucleusBuckets - 1; base += 32) {
+        for (int base = 0; base < kB - 1; base += 32) {
             const int b = base + lane;
-            const uint32_t c = b < kStageNucleusBuckets - 1 ? cnts[b] : 0u;
-            const float m = b < kStageNucleusBuckets - 1 ? mass[b] : 0.0f;
+            const uint32_t c = b < kB - 1 ? cnts[b] : 0u;
             const uint32_t ci = warp_incl_scan_plain(c) + acc;
-            const float mi = warp_incl_scan_f(m) + am;
-            const unsigned fit = __ballot_sync(0xFFFFFFFFu, b < kStageNucleusBuckets - 1 && ci <= kStageListCap);
-            if (fit) {
-                const int L = 31 - __clz(fit);
-                best = base + L;
-                best_mass = __shfl_sync(0xFFFFFFFFu, mi, L);
-            }
+            const unsigned fit = __ballot_sync(0xFFFFFFFFu, b < kB - 1 && ci <= kStageListCap);
+            if (fit) best = base + 31 - __clz(fit);
             acc = __shfl_sync(0xFFFFFFFFu, ci, 31);
-            am = __shfl_sync(0xFFFFFFFFu, mi, 31);
             if (acc > kStageListCap) break;
         }
-        if (lane == 0) {
-            const bool ok = best >= 0 && (double)best_mass * (double)inv >= (double)P.top_p + 0x1p-16;
-            sh.misc[0] = ok ? (uint32_t)best : 0xFFFFFFFFu;
-            sh.misc[1] = 0u;  // (the gather's key counter)
-        }
+        if (lane == 0) sh.misc[0] = best >= 0 ? (uint32_t)best : 0xFFFFFFFFu;
     }
     csync();
     const uint32_t best = sh.misc[0];
     if (best == 0xFFFFFFFFu) return 0xFFFFFFFFu;
     cand = -(float)(best + 1) / 32.0f;
-    visit(true, cand, &sh.misc[1]);
+    csync();
+    visit(true, cand);
     csync();
     const uint32_t nkeys = sh.misc[1];
     csync();
