@@ -3062,7 +3062,7 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
         if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ0, lrs_stage_stats, kStageThreads, 0);
         if (e == cudaSuccess)
-            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, lrs_stage_classify, kStageThreads, 0);
+            e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, lrs_stage_classify, kClassifyWarps * 32, 0);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(lrs_stage_finish, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)(kStageListCap * sizeof(unsigned long long)));
@@ -3090,7 +3090,7 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     if (e != cudaSuccess) return e;
     lrs_stage_stats<<<warps_grid[0], kStageThreads, 0, s>>>(S);
     lrs_stage_prep<<<rows, kStageThreads, 0, s>>>(S);
-    lrs_stage_classify<<<warps_grid[1], kStageThreads, 0, s>>>(S);
+    lrs_stage_classify<<<warps_grid[1], kClassifyWarps * 32, 0, s>>>(S);
     lrs_stage_sum<<<(rows + kSumWarps - 1) / kSumWarps, kSumWarps * 32, 0, s>>>(S);
     lrs_stage_finish<<<rows, kThreads, kStageListCap * sizeof(unsigned long long), s>>>(S);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;

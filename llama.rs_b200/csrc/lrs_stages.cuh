@@ -40,7 +40,6 @@ constexpr uint32_t kStageListCap = 8192;           // candidate-list entries per
 constexpr int kStageNucleusBuckets = 580;          // mass buckets of width 1/32 in (M - x')
 constexpr uint32_t kStageNucleusRank = 2048;       // top-p lists reach at least the lane maximum of this rank
 constexpr uint32_t kStageMaxTiles = 256;           // tiles of the longest stochastic row the stages take (n <= 262,144)
-constexpr uint32_t kClassifyGroup = 8;             // consecutive tiles of a row per classify task
 // flags of a row's prep record
 constexpr uint32_t kRowDone = 1u;        // outputs written by the prep (greedy, NaN, n <= 1)
 constexpr uint32_t kRowFallback = 2u;    // sampled by lrs_sample_rows afterwards
@@ -665,66 +664,63 @@ __device__ __forceinline__ ElemCls classify_units(float d, int u0, float bm0, fl
     return r;
 }
 
-__global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageArgs S) {
-    __shared__ uint32_t wbits[kStageThreads];
-    __shared__ float stage[kStageWarps * kTile];    // per warp: the live elements' d values
-    __shared__ uint8_t sblock[kStageWarps * kTile];  // ... and their blocks
-    __shared__ uint32_t bcount[kStageWarps * 17];    // ... per block increment totals (2 grids) and flags
+// The warp's tile in index order in its shared staging area (x[q] = element g0 + q, -inf
+// past cnt), the penalty applied to the window's elements (sampler.rs:96-100).
+__device__ __forceinline__ void stage_tile(const float* base, uint32_t cnt, bool pen, const uint32_t* wb, float penalty,
+                                           float* x) {
+    const int lane = threadIdx.x & 31;
+    const float ninf = __int_as_float(0xFF800000);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t e0 = 128u * j + 4u * lane;
+        float4 q = make_float4(ninf, ninf, ninf, ninf);
+        if (e0 < cnt) q = __ldg(reinterpret_cast<const float4*>(base + e0));
+        *reinterpret_cast<float4*>(x + e0) = q;
+    }
+    __syncwarp();
+    if (pen) {
+        for (uint32_t m = wb[lane]; m; m &= m - 1u) {  // (lane L: elements 32 L .. 32 L + 31)
+            const uint32_t q = 32u * lane + (uint32_t)(__ffs(m) - 1);
+            x[q] = penalise(x[q], penalty);
+        }
+        __syncwarp();
+    }
+}
+
+constexpr int kClassifyWarps = 4;  // warps per block of the classify stage
+
+__global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const StageArgs S) {
+    __shared__ uint32_t wbits[kClassifyWarps * 32];
+    __shared__ __align__(16) float tile[kClassifyWarps * kTile];  // per warp: the tile in index order
+    __shared__ float stage[kClassifyWarps * kTile];               // ... the live elements' d values
+    __shared__ uint8_t sblock[kClassifyWarps * kTile];            // ... and their blocks
+    __shared__ uint32_t bcount[kClassifyWarps * 17];              // ... per block increment totals and flags
     const lrs_kernel_args_t& a = S.a;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* wb = wbits + warp * 32;
+    float* x = tile + warp * kTile;
     float* st = stage + warp * kTile;
     uint8_t* sbk = sblock + warp * kTile;
     uint32_t* bc = bcount + warp * 17;
     uint32_t* bfl = bc + 16;
+    const unsigned lt = (1u << lane) - 1u;
     const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
-    // a warp's task: kClassifyGroup consecutive tiles of one row (one read of the row's record,
-    // the tiles' records in one round trip, the tiles that need their data brought into L2
-    // before the first is read)
-    const uint32_t groups = (S.nt + kClassifyGroup - 1) / kClassifyGroup;
-    const uint64_t tasks = (uint64_t)a.rows * groups;
-    const uint64_t stride = (uint64_t)gridDim.x * kStageWarps;
-    for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
-        const uint32_t r = (uint32_t)(task / groups), t0 = (uint32_t)(task % groups) * kClassifyGroup;
+    const uint64_t tasks = (uint64_t)a.rows * S.nt;
+    const uint64_t stride = (uint64_t)gridDim.x * kClassifyWarps;
+    for (uint64_t task = (uint64_t)blockIdx.x * kClassifyWarps + warp; task < tasks; task += stride) {
+        const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
         const RowPrep rp = S.rprep[r];
         if (rp.flags & (kRowDone | kRowFallback)) continue;
         const Geo g = row_geometry(a, r);
-        if (t0 >= g.nchunks) continue;
-        const uint32_t tn = min((uint32_t)kClassifyGroup, g.nchunks - t0);
+        if (t >= g.nchunks) continue;
+        const uint64_t ti = (uint64_t)r * S.nt + t;
+        const TilePrep tp = S.tprep[ti];
+        const float mt = S.tstat[ti].x;
         const float M = rp.M, inv_t = rp.inv_t;
         const bool pathK = rp.flags & kRowPathK;
-        // lane j < tn: tile t0 + j's records and whether it needs its data
-        TilePrep tpl{0, 0u, 0.0f, 0.0f};
-        float mtl = 0.0f;
-        bool need = false;
-        if ((uint32_t)lane < tn) {
-            const uint64_t tj = (uint64_t)r * S.nt + t0 + lane;
-            tpl = S.tprep[tj];
-            mtl = S.tstat[tj].x;
-            const float dm = __fsub_rn(mtl, M);
-            need = !(dm < tpl.dthr) || (pathK ? !(mtl < rp.cand) : !(dm < rp.cand));
-        }
-        const unsigned needm = __ballot_sync(0xFFFFFFFFu, need);
-        for (unsigned m = needm; m; m &= m - 1u) {
-            const uint32_t tw = t0 + (uint32_t)(__ffs(m) - 1);
-            if ((uint32_t)lane * 32u < chunk_count(g, tw)) prefetch_l2(g.row + g.head + tw * kTile + lane * 32u);
-        }
-        for (uint32_t j = 0; j < tn; ++j) {
-        const uint32_t t = t0 + j;
-        const uint64_t ti = (uint64_t)r * S.nt + t;
-        TilePrep tp;
-        tp.u0 = __shfl_sync(0xFFFFFFFFu, tpl.u0, (int)j);
-        tp.flags = __shfl_sync(0xFFFFFFFFu, tpl.flags, (int)j);
-        tp.xthr = __shfl_sync(0xFFFFFFFFu, tpl.xthr, (int)j);
-        tp.dthr = __shfl_sync(0xFFFFFFFFu, tpl.dthr, (int)j);
-        const float mt = __shfl_sync(0xFFFFFFFFu, mtl, (int)j);
         const float dmax = __fsub_rn(mt, M);
         const bool sum_live = !(dmax < tp.dthr);
         const bool cand_live = pathK ? !(mt < rp.cand) : !(dmax < rp.cand);
-        TileRes res;
-        res.t0 = res.t1 = 0u;
-        res.flags = 0u;
-        res.bflags = 0u;
         if (!sum_live && !cand_live) {
             if (lane == 0) {
                 S.tres[ti].flags = 0u;
@@ -741,54 +737,42 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageA
             const uint32_t hlen = a.hist_len[r];
             pen = tile_window(a.hist + (uint64_t)r * a.hist_ld, window_start(P, hlen), hlen, g0, cnt, wb);
         }
-        float v[32];
-        load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
-        // ---- candidates: appended to the row's list (any order; the finish sorts them)
-        if (cand_live) {
-            uint32_t cm = 0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                if (!(v[i] > rp.cand_raw)) continue;  // (quick reject on the raw value)
-                const float xs = __fmul_rn(v[i], inv_t);
-                const bool c = pathK ? xs >= rp.cand : __fsub_rn(xs, M) >= rp.cand;
-                if (c) cm |= 1u << i;
+        stage_tile(g.row + g0, cnt, pen, wb, P.repetition_penalty, x);
+        // one pass over 32-element slices (lane L: element 32 i + L): the candidates go to the
+        // row's list, the live elements' d values are compacted in index order
+        const float xthr = sum_live ? tp.xthr : __int_as_float(0x7F800000);
+        const float craw = cand_live ? rp.cand_raw : __int_as_float(0x7F800000);
+        uint32_t tot = 0;
+        uint2* lst = S.lists + (uint64_t)r * kStageListCap;
+#pragma unroll 4
+        for (int i = 0; i < 32; ++i) {
+            const uint32_t q = 32u * i + lane;
+            const float v = x[q];
+            const unsigned lm = __ballot_sync(0xFFFFFFFFu, v > xthr);
+            if (v > xthr) {
+                const uint32_t o = tot + (uint32_t)__popc(lm & lt);
+                st[o] = d_of(v, inv_t, M);
+                sbk[o] = (uint8_t)(q >> 7);
             }
-            const uint32_t nc = (uint32_t)__popc(cm);
-            const uint32_t incl = warp_incl_scan_plain(nc);
-            const uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
-            if (tot) {
-                uint32_t base = 0;
-                if (lane == 31) base = atomicAdd(S.list_n + r, tot);
-                base = __shfl_sync(0xFFFFFFFFu, base, 31) + incl - nc;
-                uint2* lst = S.lists + (uint64_t)r * kStageListCap;
-                for (uint32_t m = cm; m; m &= m - 1u) {
-                    const int i = __ffs(m) - 1;
-                    if (base < kStageListCap)
-                        lst[base] = make_uint2(__float_as_uint(__fmul_rn(v[i], inv_t)),
-                                               g0 + 128u * (i >> 2) + 4u * lane + (i & 3));
-                    ++base;
+            tot += (uint32_t)__popc(lm);
+            if (__any_sync(0xFFFFFFFFu, v > craw)) {  // (rare: the candidates of the finish)
+                const float xs = __fmul_rn(v, inv_t);
+                const bool c = v > craw && (pathK ? xs >= rp.cand : __fsub_rn(xs, M) >= rp.cand);
+                const unsigned cm = __ballot_sync(0xFFFFFFFFu, c);
+                if (cm) {
+                    uint32_t base = 0;
+                    if (lane == 0) base = atomicAdd(S.list_n + r, (uint32_t)__popc(cm));
+                    base = __shfl_sync(0xFFFFFFFFu, base, 0) + (uint32_t)__popc(cm & lt);
+                    if (c && base < kStageListCap) lst[base] = make_uint2(__float_as_uint(xs), g0 + q);
                 }
             }
         }
-        // ---- increments of the live elements on grids u0 and u0 + 1, per block of 128, from
-        // their d values compacted into the warp's staging area (a lane classifies total / 32)
+        uint32_t t0v = 0, t1v = 0, fl = 0, bf = 0;
         if (sum_live) {
+            // increments of the live elements on grids u0 and u0 + 1, per block of 128 (a lane
+            // classifies total / 32 of them)
             const int u0 = tp.u0;
             const bool one = tp.flags & kTileOne;
-            uint32_t lm = 0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i) lm |= (uint32_t)(v[i] > tp.xthr) << i;
-            const uint32_t nc = (uint32_t)__popc(lm);
-            const uint32_t incl = warp_incl_scan_plain(nc);
-            const uint32_t tot = __shfl_sync(0xFFFFFFFFu, incl, 31);
-            uint32_t o = incl - nc;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if ((lm >> i) & 1u) {
-                    st[o] = d_of(v[i], inv_t, M);
-                    sbk[o] = (uint8_t)(i >> 2);
-                    ++o;
-                }
             if (lane < 16) bc[lane] = 0u;
             if (lane == 0) bfl[0] = 0u;
             __syncwarp();
@@ -805,29 +789,23 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_classify(const StageA
             __syncwarp();
             // (a block's count is at most 128 * 2^23 < 2^32; saturated where it leaves the grid)
             const uint32_t c0 = lane < 8 ? min(bc[lane], kSat) : 0u, c1 = lane < 8 ? min(bc[8 + lane], kSat) : 0u;
-            const uint32_t bf = bfl[0];
-            res.t0 = min(__reduce_add_sync(0xFFFFFFFFu, c0), kSat);
-            res.t1 = min(__reduce_add_sync(0xFFFFFFFFu, c1), kSat);
-            res.bflags = bf;
-            res.flags = (tot ? kTileLive : 0u) | ((bf >> 8) & 0xFFu ? kTileSp0 : 0u) | ((bf >> 16) & 0xFFu ? kTileSp1 : 0u);
+            bf = bfl[0];
+            t0v = min(__reduce_add_sync(0xFFFFFFFFu, c0), kSat);
+            t1v = min(__reduce_add_sync(0xFFFFFFFFu, c1), kSat);
+            fl = (tot ? kTileLive : 0u) | ((bf >> 8) & 0xFFu ? kTileSp0 : 0u) | ((bf >> 16) & 0xFFu ? kTileSp1 : 0u);
             if (lane < 8) {
-                res.b0[lane] = c0;
-                res.b1[lane] = c1;
+                S.tres[ti].b0[lane] = c0;
+                S.tres[ti].b1[lane] = c1;
             }
-            __syncwarp();  // (the staging area is reused by the next tile)
         }
         if (lane == 0) {
             TileRes* out = S.tres + ti;
-            out->t0 = res.t0;
-            out->t1 = res.t1;
-            out->flags = res.flags;
-            out->bflags = res.bflags;
+            out->t0 = t0v;
+            out->t1 = t1v;
+            out->flags = fl;
+            out->bflags = bf;
         }
-        if (sum_live && lane < 8) {
-            S.tres[ti].b0[lane] = res.b0[lane];
-            S.tres[ti].b1[lane] = res.b1[lane];
-        }
-        }
+        __syncwarp();  // (the staging areas are reused by the next tile)
     }
 }
 
@@ -1122,8 +1100,8 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
 
 // ----------------------------------------------------------------- finish ----
 // A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA counts the
-// row's elements by d = fl(x' - M) in buckets of 1/32 (a histogram per warp, increments
-// aggregated over the lanes that share a bucket), takes the deepest bucket edge whose
+// row's elements by d = fl(x' - M) in buckets of 1/32 (a histogram per warp), takes the
+// deepest bucket edge whose
 // elements fit in the list's capacity, and gathers those elements' exact keys (p desc, index
 // asc) into keys.  Returns their number (cand: the edge), or 0xFFFFFFFF if none fits.  The
 // finish checks that the nucleus lies inside them.
@@ -1146,6 +1124,8 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     csync();
     uint32_t* wc = cnts + warp * kB;
     uint32_t* wb = sh.hist256 + warp * 32;  // (the warp's window words)
+    // the whole row into L2 ahead of the two passes (a thread a 128-byte line at a time)
+    for (uint64_t q = (uint64_t)tid * 32u; q < g.n; q += (uint64_t)kThreads * 32u) prefetch_l2(g.row + q);
     auto bucket_of = [](float d) -> int {   // kB - 1: below the histogram's range
         return d >= -(float)(kB - 1) / 32.0f ? (int)fminf(-d * 32.0f, (float)(kB - 2)) : kB - 1;
     };
@@ -1184,8 +1164,7 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
                     gi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
                 if (!gather) {
                     const int b = bucket_of(d);
-                    const unsigned peers = __match_any_sync(0xFFFFFFFFu, b);
-                    if (b < kB - 1 && lane == __ffs(peers) - 1) atomicAdd(&wc[b], (uint32_t)__popc(peers));
+                    if (b < kB - 1) atomicAdd(&wc[b], 1u);
                 } else {
                     const bool take = d >= th;
                     const unsigned m = __ballot_sync(0xFFFFFFFFu, take);
