@@ -691,15 +691,16 @@ constexpr int kClassifyWarps = 4;  // warps per block of the classify stage
 
 __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const StageArgs S) {
     __shared__ uint32_t wbits[kClassifyWarps * 32];
-    __shared__ __align__(16) float tile[kClassifyWarps * kTile];  // per warp: the tile in index order
-    __shared__ float stage[kClassifyWarps * kTile];               // ... the live elements' d values
-    __shared__ uint8_t sblock[kClassifyWarps * kTile];            // ... and their blocks
+    // per warp: the tile in index order; the live elements' d values are written over its
+    // part already read (the compacted position never passes the slice being read)
+    __shared__ __align__(16) float tile[kClassifyWarps * kTile];
+    __shared__ uint8_t sblock[kClassifyWarps * kTile];            // ... and the live elements' blocks
     __shared__ uint32_t bcount[kClassifyWarps * 17];              // ... per block increment totals and flags
     const lrs_kernel_args_t& a = S.a;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* wb = wbits + warp * 32;
     float* x = tile + warp * kTile;
-    float* st = stage + warp * kTile;
+    float* st = x;
     uint8_t* sbk = sblock + warp * kTile;
     uint32_t* bc = bcount + warp * 17;
     uint32_t* bfl = bc + 16;
@@ -749,6 +750,7 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
             const uint32_t q = 32u * i + lane;
             const float v = x[q];
             const unsigned lm = __ballot_sync(0xFFFFFFFFu, v > xthr);
+            __syncwarp();  // (the slice is read before any d value lands on it)
             if (v > xthr) {
                 const uint32_t o = tot + (uint32_t)__popc(lm & lt);
                 st[o] = d_of(v, inv_t, M);
@@ -1215,16 +1217,20 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
 }
 
 // Sequential f32 run over sorted probabilities keys[0..cnt) (sampler.rs:137-139 / 148-151 /
-// 156-158): dir > 0 adds until s >= thr, dir < 0 subtracts until s <= 0.  Short runs go one
-// by one on thread 0; long ones chunk by chunk with the block's exact emulation (acc_tile).
+// 156-158): dir > 0 adds until s >= thr, dir < 0 subtracts until s <= 0.  The first 512
+// positions go one by one on thread 0, the rest chunk by chunk with the block's exact
+// emulation (acc_tile).
 // Returns the stop position or -1; every thread gets the same s.
 __device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t cnt, int dir, float& s, float thr,
                                        RowShared& sh) {
-    if (cnt <= 512u) {
+    // (the head of a sorted run holds its largest elements, nearly every one an ordered step
+    // of the emulation: it goes one by one; the emulation takes the rest)
+    const uint32_t head = cnt < 512u ? cnt : 512u;
+    {
         if (threadIdx.x == 0) {
             float cur = s;
             int stop = -1;
-            for (uint32_t i = 0; i < cnt; ++i) {
+            for (uint32_t i = 0; i < head; ++i) {
                 const float p = __uint_as_float(~(uint32_t)(keys[i] >> 32));
                 cur = dir > 0 ? __fadd_rn(cur, p) : __fsub_rn(cur, p);
                 if (dir > 0 ? cur >= thr : cur <= 0.0f) {
@@ -1239,9 +1245,9 @@ __device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t 
         s = sh.fstate;
         const int st = sh.stop;
         csync();
-        return st;
+        if (st >= 0 || head == cnt) return st;
     }
-    for (uint32_t b = 0; b < cnt; b += kChunk) {
+    for (uint32_t b = head; b < cnt; b += kChunk) {
         const uint32_t tc = cnt - b < (uint32_t)kChunk ? cnt - b : (uint32_t)kChunk;
         float v[kVpt];
         load_sorted_tile(keys + b, tc, v);
