@@ -88,6 +88,7 @@ typedef struct lrs_row_info {
                             max/filter pass, 1 estimates and thresholds, 2 softmax-sum pass, 3
                             top-k/top-p/draw, 7 sorting within 3; rows finished by the staged
                             pipeline: 4 is 1, 0-2 the cycles of its prep, sum and finish stages,
+                            3, 6 and 7 those of the finish's regather, sorts and sequential runs,
                             5 the blocks its sum walked (implementation detail) */
     uint32_t reserved;
 } lrs_row_info;

@@ -1173,10 +1173,8 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
                     uint32_t o = 0;
                     if (m && lane == 0) o = atomicAdd(&sh.misc[1], (uint32_t)__popc(m));
                     o = __shfl_sync(0xFFFFFFFFu, o, 0) + (uint32_t)__popc(m & ((1u << lane) - 1u));
-                    if (take && o < kStageListCap) {
-                        const float p = __fmul_rn(exact_expf(d, tab), inv);
-                        keys[o] = ((unsigned long long)(~__float_as_uint(p)) << 32) | gi;
-                    }
+                    if (take && o < kStageListCap)  // (d now; its key once every element is in)
+                        keys[o] = ((unsigned long long)__float_as_uint(d) << 32) | gi;
                 }
             }
         }
@@ -1212,8 +1210,43 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     visit(true, cand);
     csync();
     const uint32_t nkeys = sh.misc[1];
+    if (nkeys > kStageListCap) return 0xFFFFFFFFu;
+    // the keys (p desc, index asc) from the gathered d values, p = fl(libm expf(d) * inv)
+    for (uint32_t i = tid; i < nkeys; i += kThreads) {
+        const unsigned long long k = keys[i];
+        const float p = __fmul_rn(exact_expf(__uint_as_float((uint32_t)(k >> 32)), tab), inv);
+        keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (k & 0xFFFFFFFFull);
+    }
     csync();
-    return nkeys <= kStageListCap ? nkeys : 0xFFFFFFFFu;
+    return nkeys;
+}
+
+// All-ascending bitonic sort of n 64-bit keys in shared memory by the block (virtual +inf
+// padding to a power of two), with shift and mask indexing (strides are powers of two).
+__device__ __noinline__ void stage_sort_u64(unsigned long long* keys, uint32_t n) {
+    if (n < 2) return;
+    uint32_t lg = 1;
+    while ((1u << lg) < n) ++lg;
+    const uint32_t half = 1u << (lg - 1);
+    for (uint32_t ls = 1; ls <= lg; ++ls) {          // merge size 2^ls
+        for (uint32_t lt = ls; lt-- > 0;) {           // stride 2^lt
+            const uint32_t stride = 1u << lt, mask = stride - 1u;
+            const bool first = lt == ls - 1;           // first step of a merge: the mirrored partner
+            for (uint32_t t = threadIdx.x; t < half; t += kThreads) {
+                const uint32_t off = t & mask, grp = t >> lt;
+                const uint32_t i = (grp << (lt + 1)) + off;
+                const uint32_t j = first ? i + ((stride - off) << 1) - 1u : i + stride;
+                if (j < n) {
+                    const unsigned long long a = keys[i], b = keys[j];
+                    if (a > b) {
+                        keys[i] = b;
+                        keys[j] = a;
+                    }
+                }
+            }
+            csync();
+        }
+    }
 }
 
 // Sequential f32 run over sorted probabilities keys[0..cnt) (sampler.rs:137-139 / 148-151 /
@@ -1230,12 +1263,17 @@ __device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t 
         if (threadIdx.x == 0) {
             float cur = s;
             int stop = -1;
-            for (uint32_t i = 0; i < head; ++i) {
-                const float p = __uint_as_float(~(uint32_t)(keys[i] >> 32));
-                cur = dir > 0 ? __fadd_rn(cur, p) : __fsub_rn(cur, p);
-                if (dir > 0 ? cur >= thr : cur <= 0.0f) {
-                    stop = (int)i;
-                    break;
+            // (eight values loaded at a time: the loads do not wait for the sum)
+            for (uint32_t i0 = 0; i0 < head && stop < 0; i0 += 8) {
+                float v[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    v[j] = i0 + j < head ? __uint_as_float(~(uint32_t)(keys[i0 + j] >> 32)) : 0.0f;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (i0 + j >= head || stop >= 0) break;
+                    cur = dir > 0 ? __fadd_rn(cur, v[j]) : __fsub_rn(cur, v[j]);
+                    if (dir > 0 ? cur >= thr : cur <= 0.0f) stop = (int)(i0 + j);
                 }
             }
             sh.fstate = cur;
@@ -1291,6 +1329,7 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
     float cum = 0.0f;
     int stp = -1;
     uint32_t kk = 0, cut = 0;
+    long long c_regather = 0, c_sort = 0, c_runs = 0, tm = 0;  // (diagnostics: cycles by phase)
     for (int attempt = nk > kStageListCap ? 1 : 0; attempt < 2; ++attempt) {
         if (attempt == 0) {
             const uint2* lst = S.lists + (uint64_t)r * kStageListCap;
@@ -1303,19 +1342,25 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
             // The nucleus reaches deeper than the list: gather it from the row, at the deepest
             // bucket edge (width 1/32 in d) whose elements fit in the list's capacity.
             csync();
+            tm = clock64();
             n_keys = regather_nucleus(S, r, P, M, inv, exptab, keys, sh, cand);
+            c_regather += clock64() - tm;
             if (n_keys == 0xFFFFFFFFu) {
                 if (tid == 0) stage_fallback(S, r);
                 return;
             }
         }
         csync();
-        bitonic_sort_u64(keys, n_keys);  // (p desc, index asc): the reference's order (see the oracle on ties)
+        tm = clock64();
+        stage_sort_u64(keys, n_keys);  // (p desc, index asc): the reference's order (see the oracle on ties)
+        c_sort += clock64() - tm;
         kk = rp.k < n_keys ? rp.k : n_keys;  // (path K: the list holds the top k; path N: the nucleus)
         // top-p over the first kk (sampler.rs:135-146); the survivor sum is the same sequence up
         // to the cutoff (sampler.rs:148-151)
         cum = 0.0f;
+        tm = clock64();
         stp = sorted_run(keys, kk, +1, cum, topp_on ? P.top_p : kInf, sh);
+        c_runs += clock64() - tm;
         cut = stp >= 0 ? (uint32_t)stp + 1 : kk;
         // path N: the list holds every element with d >= cand, so its sorted order is the row's
         // as far as its probabilities exceed the largest one an element outside can have; the
@@ -1336,7 +1381,9 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
     if (cum > 0.0f) {
         r0 = __fmul_rn(next_f32(&st), cum);  // sampler.rs:155
         float rv = r0;
+        tm = clock64();
         const int w = sorted_run(keys, cut, -1, rv, 0.0f, sh);
+        c_runs += clock64() - tm;
         ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
     }
     if (tid != 0) return;
@@ -1362,5 +1409,9 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
     inf.cycles[2] = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
     inf.cycles[4] = 1u;  // (finished by the staged pipeline)
     inf.cycles[5] = rp.walks;
+    auto sat = [](long long v) -> uint32_t { return v > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)v; };
+    inf.cycles[3] = sat(c_regather);
+    inf.cycles[6] = sat(c_sort);
+    inf.cycles[7] = sat(c_runs);
     write_row(a, r, LRS_OK, inf.token, inf.prob, true, st, inf);
 }
