@@ -3065,7 +3065,7 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
             e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ1, lrs_stage_classify, kClassifyWarps * 32, 0);
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(lrs_stage_finish, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)(kStageListCap * sizeof(unsigned long long)));
+                                     (int)kStageFinishSmem);
         if (e != cudaSuccess) return e;
         warps_grid[0] = sms * (occ0 > 0 ? occ0 : 1);
         warps_grid[1] = sms * (occ1 > 0 ? occ1 : 1);
@@ -3092,7 +3092,7 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     lrs_stage_prep<<<rows, kStageThreads, 0, s>>>(S);
     lrs_stage_classify<<<warps_grid[1], kClassifyWarps * 32, 0, s>>>(S);
     lrs_stage_sum<<<(rows + kSumWarps - 1) / kSumWarps, kSumWarps * 32, 0, s>>>(S);
-    lrs_stage_finish<<<rows, kThreads, kStageListCap * sizeof(unsigned long long), s>>>(S);
+    lrs_stage_finish<<<rows, kThreads, kStageFinishSmem, s>>>(S);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // the rows the stages left: lrs_sample_rows on the list, in list order
     lrs_kernel_args_t fb = *args;

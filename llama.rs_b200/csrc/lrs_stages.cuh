@@ -37,6 +37,8 @@
 constexpr int kStageThreads = 256;                 // stats / prep / classify blocks (8 warps)
 constexpr int kStageWarps = kStageThreads / 32;
 constexpr uint32_t kStageListCap = 8192;           // candidate-list entries per row
+// the finish's dynamic shared memory: the keys, then the sort's two 16-bit permutations
+constexpr size_t kStageFinishSmem = kStageListCap * sizeof(unsigned long long) + 2 * kStageListCap * sizeof(uint16_t);
 constexpr int kStageNucleusBuckets = 580;          // mass buckets of width 1/32 in (M - x')
 constexpr uint32_t kStageNucleusRank = 2048;       // top-p lists reach at least the lane maximum of this rank
 constexpr uint32_t kStageMaxTiles = 256;           // tiles of the longest stochastic row the stages take (n <= 262,144)
@@ -1102,14 +1104,19 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
 
 // ----------------------------------------------------------------- finish ----
 // A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA counts the
-// row's elements by d = fl(x' - M) in buckets of 1/32 (a histogram per warp), takes the
-// deepest bucket edge whose
-// elements fit in the list's capacity, and gathers those elements' exact keys (p desc, index
-// asc) into keys.  Returns their number (cand: the edge), or 0xFFFFFFFF if none fits.  The
-// finish checks that the nucleus lies inside them.
+// row's elements by d = fl(x' - M) in buckets of 1/4 over d in (-18, 0] and gathers the exact
+// keys (p desc, index asc) of every element above the deepest bucket edge whose elements fit
+// in the list's capacity (level 0).  If the nucleus reaches past that edge, level 1 counts the
+// next bucket in steps of 1/32 and gathers down to the deepest of those edges that fits.
+// Returns the number of keys (cand: the edge), or 0xFFFFFFFF if no deeper edge fits.  The
+// finish checks that the nucleus lies inside them.  The counts are private to each thread (a
+// column of the keys area per thread, no atomics); split and base (the bucket that overflows
+// and the count above it) carry from level 0 to level 1.
+constexpr int kRgCoarse = 72;  // buckets of 1/4: d in (-18, 0]
 __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r, const lrs_params& P, float M, float inv,
                                                   const ExpTable tab, unsigned long long* keys, RowShared& sh,
-                                                  float& cand) {
+                                                  float& cand, int level, int& split, uint32_t& base) {
+    static_assert(kRgCoarse * kThreads + kRgCoarse + 8 <= 2 * (int)kStageListCap, "regather counts fit the keys");
     const lrs_kernel_args_t& a = S.a;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const Geo g = row_geometry(a, r);
@@ -1118,20 +1125,20 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     const uint32_t hlen = (pen_on && a.hist_len) ? a.hist_len[r] : 0u;
     const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
     const uint32_t hstart = window_start(P, hlen);
-    constexpr int kB = kStageNucleusBuckets;
-    // per-warp counts in the keys area (kWarps x kB words), summed into warp 0's row below
-    uint32_t* cnts = reinterpret_cast<uint32_t*>(keys);
-    for (int b = tid; b < kWarps * kB; b += kThreads) cnts[b] = 0u;
-    if (tid == 0) sh.misc[1] = 0u;  // (the gather's key counter)
-    csync();
-    uint32_t* wc = cnts + warp * kB;
-    uint32_t* wb = sh.hist256 + warp * 32;  // (the warp's window words)
-    // the whole row into L2 ahead of the two passes (a thread a 128-byte line at a time)
-    for (uint64_t q = (uint64_t)tid * 32u; q < g.n; q += (uint64_t)kThreads * 32u) prefetch_l2(g.row + q);
-    auto bucket_of = [](float d) -> int {   // kB - 1: below the histogram's range
-        return d >= -(float)(kB - 1) / 32.0f ? (int)fminf(-d * 32.0f, (float)(kB - 2)) : kB - 1;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(keys);  // [bucket][kThreads]
+    uint32_t* tot = cnt + kRgCoarse * kThreads;          // [kRgCoarse] coarse totals, then [8] fine
+    uint32_t* wb = sh.hist256 + warp * 32;                // (the warp's window words)
+    if (level == 0) {
+        // the whole row into L2 ahead of the passes (a thread a 128-byte line at a time)
+        for (uint64_t q = (uint64_t)tid * 32u; q < g.n; q += (uint64_t)kThreads * 32u) prefetch_l2(g.row + q);
+    }
+    // floor(-d * sc) for d in (-18, 0] (sc a power of two: the product is exact), from the
+    // bits of fl_rd(-d * sc + 2^23); 0xFFFF past -18 and for NaN
+    auto bucket = [](float d, float sc) -> uint32_t {
+        return d > -18.0f ? (__float_as_uint(__fadd_rd(__fmul_rn(d, -sc), 8388608.0f)) & 0x7FFFFFu) : 0xFFFFu;
     };
-    auto visit = [&](bool gather, float th) {
+    // mode 0: coarse counts; mode 1: fine counts in coarse bucket cb; mode 2: gather d >= th
+    auto visit = [&](int mode, uint32_t cb, float th) {
         // edge elements (warp 0, lanes 0 .. edges-1), then the tiles (warp w: tiles w, w + 7, ...)
         const uint32_t edges = g.head + g.tail;
         for (uint32_t t = (uint32_t)warp; t < g.nchunks + (warp == 0 ? 1u : 0u); t += kWarps) {
@@ -1139,11 +1146,15 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
             float v[32];
             uint32_t g0 = 0;
             if (!edge) {
-                const uint32_t cnt = chunk_count(g, t);
+                // the warp's next tile into L1 while this one is counted (a line per lane)
+                const uint32_t tn = t + kWarps;
+                if (tn < g.nchunks && (uint32_t)lane * 32u < chunk_count(g, tn))
+                    asm volatile("prefetch.global.L1 [%0];" ::"l"(g.row + g.head + tn * kTile + lane * 32u));
+                const uint32_t c = chunk_count(g, t);
                 g0 = g.head + t * kTile;
                 bool pen = false;
-                if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
-                load_tile_blocks(g.row + g0, cnt, pen, wb, P.repetition_penalty, v);
+                if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, c, wb);
+                load_tile_blocks(g.row + g0, c, pen, wb, P.repetition_penalty, v);
             } else {
                 const uint32_t egi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
                 float x = (uint32_t)lane < edges ? g.row[egi] : __int_as_float(0xFF800000);
@@ -1156,58 +1167,121 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
                 for (int i = 0; i < 32; ++i) v[i] = __int_as_float(0xFF800000);
                 v[0] = x;
             }
-#pragma unroll 4
-            for (int i = 0; i < 32; ++i) {
-                const float d = d_of(v[i], inv_t, M);
-                uint32_t gi;
-                if (!edge)
-                    gi = g0 + 128u * (i >> 2) + 4u * lane + (i & 3);
-                else
-                    gi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
-                if (!gather) {
-                    const int b = bucket_of(d);
-                    if (b < kB - 1) atomicAdd(&wc[b], 1u);
-                } else {
-                    const bool take = d >= th;
-                    const unsigned m = __ballot_sync(0xFFFFFFFFu, take);
-                    uint32_t o = 0;
-                    if (m && lane == 0) o = atomicAdd(&sh.misc[1], (uint32_t)__popc(m));
-                    o = __shfl_sync(0xFFFFFFFFu, o, 0) + (uint32_t)__popc(m & ((1u << lane) - 1u));
-                    if (take && o < kStageListCap)  // (d now; its key once every element is in)
-                        keys[o] = ((unsigned long long)__float_as_uint(d) << 32) | gi;
+            if (mode == 0) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const uint32_t b = bucket(d_of(v[i], inv_t, M), 4.0f);
+                    if (b < (uint32_t)kRgCoarse) ++cnt[b * kThreads + tid];
+                }
+            } else if (mode == 1) {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const uint32_t b = bucket(d_of(v[i], inv_t, M), 32.0f);
+                    if ((b >> 3) == cb) ++cnt[(b & 7u) * kThreads + tid];
+                }
+            } else {
+                // count, one reservation per warp and tile, then the writes in the lane's order
+                uint32_t mine = 0;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    v[i] = d_of(v[i], inv_t, M);
+                    mine += v[i] >= th ? 1u : 0u;
+                }
+                const uint32_t incl = warp_incl_scan_plain(mine);
+                const uint32_t wtot = __shfl_sync(0xFFFFFFFFu, incl, 31);
+                if (wtot == 0u) continue;
+                uint32_t wbase = 0;
+                if (lane == 31) wbase = atomicAdd(&sh.misc[1], wtot);
+                uint32_t o = __shfl_sync(0xFFFFFFFFu, wbase, 31) + incl - mine;
+                if (mine == 0u) continue;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    if (v[i] >= th) {
+                        uint32_t gi;
+                        if (!edge)
+                            gi = g0 + 128u * (i >> 2) + 4u * lane + (i & 3);
+                        else
+                            gi = (uint32_t)lane < g.head ? (uint32_t)lane : g.head + g.body + ((uint32_t)lane - g.head);
+                        if (o < kStageListCap)  // (d now; its key once every element is in)
+                            keys[o] = ((unsigned long long)__float_as_uint(v[i]) << 32) | gi;
+                        ++o;
+                    }
                 }
             }
         }
     };
-    visit(false, 0.0f);
-    csync();
-    for (int b = tid; b < kB; b += kThreads) {
-        uint32_t c = 0;
-        for (int w = 0; w < kWarps; ++w) c += cnts[w * kB + b];
-        cnts[b] = c;  // (row 0 holds the totals: its own entry is read before it is written)
-    }
-    csync();
-    if (warp == 0) {
-        // the deepest bucket whose prefix count fits in the list
-        uint32_t acc = 0;
+    // the totals of nb private columns into out[0 .. nb) (a warp per bucket)
+    auto reduce = [&](int nb, uint32_t* out) {
+        for (int b = warp; b < nb; b += kWarps) {
+            uint32_t c = 0;
+#pragma unroll
+            for (int q = 0; q < kWarps; ++q) c += cnt[b * kThreads + lane + 32 * q];
+            c = __reduce_add_sync(0xFFFFFFFFu, c);
+            if (lane == 0) out[b] = c;
+        }
+    };
+    // warp 0: the deepest bucket of c[0 .. nb) whose prefix count, from base0, fits in the list
+    auto deepest = [&](const uint32_t* c, int nb, uint32_t base0) -> int {
+        uint32_t acc = base0;
         int best = -1;
-        for (int base = 0; base < kB - 1; base += 32) {
-            const int b = base + lane;
-            const uint32_t c = b < kB - 1 ? cnts[b] : 0u;
-            const uint32_t ci = warp_incl_scan_plain(c) + acc;
-            const unsigned fit = __ballot_sync(0xFFFFFFFFu, b < kB - 1 && ci <= kStageListCap);
-            if (fit) best = base + 31 - __clz(fit);
+        for (int b0 = 0; b0 < nb; b0 += 32) {
+            const int b = b0 + lane;
+            const uint32_t ci = warp_incl_scan_plain(b < nb ? c[b] : 0u) + acc;
+            const unsigned fit = __ballot_sync(0xFFFFFFFFu, b < nb && ci <= kStageListCap);
+            if (fit) best = b0 + 31 - __clz(fit);
             acc = __shfl_sync(0xFFFFFFFFu, ci, 31);
             if (acc > kStageListCap) break;
         }
-        if (lane == 0) sh.misc[0] = best >= 0 ? (uint32_t)best : 0xFFFFFFFFu;
+        return best;
+    };
+    if (tid == 0) sh.misc[1] = 0u;  // (the gather's key counter)
+    int edge_b;  // the deepest fine bucket (1/32) above the edge
+    if (level == 0) {
+#pragma unroll
+        for (int b = 0; b < kRgCoarse; ++b) cnt[b * kThreads + tid] = 0u;  // (its own column)
+        visit(0, 0u, 0.0f);
+        csync();
+        reduce(kRgCoarse, tot);
+        csync();
+        if (warp == 0) {
+            const int cb = deepest(tot, kRgCoarse, 0u);  // buckets 0 .. cb fit
+            uint32_t bs = 0;
+            for (int b = lane; b <= cb; b += 32) bs += tot[b];
+            bs = __reduce_add_sync(0xFFFFFFFFu, bs);
+            if (lane == 0) {
+                sh.misc[0] = (uint32_t)(cb + 1);  // the coarse bucket that overflows (kRgCoarse: none)
+                sh.misc[2] = bs;
+            }
+        }
+        csync();
+        split = (int)sh.misc[0];
+        base = sh.misc[2];
+        edge_b = split * 8 - 1;
+    } else {
+        edge_b = -1;
     }
-    csync();
-    const uint32_t best = sh.misc[0];
-    if (best == 0xFFFFFFFFu) return 0xFFFFFFFFu;
-    cand = -(float)(best + 1) / 32.0f;
-    csync();
-    visit(true, cand);
+    // level 1, or level 0 when no coarse bucket fits: split the overflowing bucket by 1/32
+    if (edge_b < 0 || level == 1) {
+        if (split >= kRgCoarse) return 0xFFFFFFFFu;
+#pragma unroll
+        for (int b = 0; b < 8; ++b) cnt[b * kThreads + tid] = 0u;
+        visit(1, (uint32_t)split, 0.0f);
+        csync();
+        reduce(8, tot + kRgCoarse);
+        csync();
+        if (warp == 0) {
+            const int f = deepest(tot + kRgCoarse, 8, base);
+            if (lane == 0) sh.misc[3] = (uint32_t)(f + 1);
+        }
+        csync();
+        const int f = (int)sh.misc[3] - 1;
+        if (f < 0) return 0xFFFFFFFFu;  // (no edge deeper than level 0's)
+        edge_b = split * 8 + f;
+        if (level == 0) split = kRgCoarse;  // (level 0 took the fine edge: level 1 has none deeper)
+    }
+    cand = -(float)(edge_b + 1) / 32.0f;
+    csync();  // (the counts are dead: the gather writes keys)
+    visit(2, 0u, cand);
     csync();
     const uint32_t nkeys = sh.misc[1];
     if (nkeys > kStageListCap) return 0xFFFFFFFFu;
@@ -1221,32 +1295,278 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     return nkeys;
 }
 
-// All-ascending bitonic sort of n 64-bit keys in shared memory by the block (virtual +inf
-// padding to a power of two), with shift and mask indexing (strides are powers of two).
-__device__ __noinline__ void stage_sort_u64(unsigned long long* keys, uint32_t n) {
-    if (n < 2) return;
-    uint32_t lg = 1;
-    while ((1u << lg) < n) ++lg;
-    const uint32_t half = 1u << (lg - 1);
-    for (uint32_t ls = 1; ls <= lg; ++ls) {          // merge size 2^ls
-        for (uint32_t lt = ls; lt-- > 0;) {           // stride 2^lt
-            const uint32_t stride = 1u << lt, mask = stride - 1u;
-            const bool first = lt == ls - 1;           // first step of a merge: the mirrored partner
-            for (uint32_t t = threadIdx.x; t < half; t += kThreads) {
-                const uint32_t off = t & mask, grp = t >> lt;
-                const uint32_t i = (grp << (lt + 1)) + off;
-                const uint32_t j = first ? i + ((stride - off) << 1) - 1u : i + stride;
-                if (j < n) {
-                    const unsigned long long a = keys[i], b = keys[j];
-                    if (a > b) {
-                        keys[i] = b;
-                        keys[j] = a;
-                    }
-                }
+// ------------------------------------------------------------------ sort ----
+// Ascending sort of n <= kStageListCap 64-bit keys in shared memory by the block.  A warp
+// sorts runs of 32 * KPL keys in registers with a bitonic network (lane L holds keys
+// KPL L .. KPL L + KPL - 1; every compare-exchange pairs i with i ^ m, m = 2^ls - 1 opening the
+// merge of size 2^ls with the mirrored partner, m = 2^lt cleaning; m < KPL pairs registers of
+// a lane, larger m pairs lanes by shuffles).  Runs of 256 are then merged pairwise by merge
+// path into 16-bit permutations, and the final order is written back through global scratch.
+__host__ __device__ constexpr int hibit(int x) { return x >= 2 ? 2 * hibit(x >> 1) : x; }
+
+template <int M, int KPL>
+__device__ __forceinline__ void seg_stage(unsigned long long (&k)[KPL], uint32_t lane) {
+    if constexpr (M >= KPL) {
+        constexpr int mL = M / KPL, mj = M % KPL;      // partner lane lane ^ mL, register j ^ mj
+        constexpr uint32_t h = (uint32_t)hibit(mL);    // the lane bit that decides the pair
+        const bool lower = (lane & h) == 0u;
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            if constexpr (mj == 0) {
+                const unsigned long long o = __shfl_xor_sync(0xFFFFFFFFu, k[j], mL), x = k[j];
+                k[j] = lower ? (o < x ? o : x) : (o < x ? x : o);
+            } else if (j < (j ^ mj)) {  // (both registers of a pair are read before either is written)
+                const unsigned long long o1 = __shfl_xor_sync(0xFFFFFFFFu, k[j ^ mj], mL);
+                const unsigned long long o2 = __shfl_xor_sync(0xFFFFFFFFu, k[j], mL);
+                const unsigned long long x1 = k[j], x2 = k[j ^ mj];
+                k[j] = lower ? (o1 < x1 ? o1 : x1) : (o1 < x1 ? x1 : o1);
+                k[j ^ mj] = lower ? (o2 < x2 ? o2 : x2) : (o2 < x2 ? x2 : o2);
             }
-            csync();
+        }
+    } else {
+        constexpr int H = hibit(M);
+#pragma unroll
+        for (int j = 0; j < KPL; ++j) {
+            if (!(j & H)) {
+                const unsigned long long x = k[j], y = k[j ^ M];
+                k[j] = x < y ? x : y;
+                k[j ^ M] = x < y ? y : x;
+            }
         }
     }
+}
+
+template <int LT, int KPL>
+__device__ __forceinline__ void seg_clean(unsigned long long (&k)[KPL], uint32_t lane) {
+    if constexpr (LT >= 0) {
+        seg_stage<(1 << LT), KPL>(k, lane);
+        seg_clean<LT - 1, KPL>(k, lane);
+    }
+}
+
+// The merges of sizes 2^LS .. 32 KPL: a full sort of the run from LS = 1.
+template <int LS, int KPL>
+__device__ __forceinline__ void seg_sort(unsigned long long (&k)[KPL], uint32_t lane) {
+    if constexpr ((1 << LS) <= 32 * KPL) {
+        seg_stage<(1 << LS) - 1, KPL>(k, lane);
+        seg_clean<LS - 2, KPL>(k, lane);
+        seg_sort<LS + 1, KPL>(k, lane);
+    }
+}
+
+// The warp sorts keys[b, b + 32 KPL) in place; positions at or past n read as ~0 and are
+// written back only below `store`.
+template <int KPL>
+__device__ __forceinline__ void warp_sort_run(unsigned long long* keys, uint32_t b, uint32_t n, uint32_t store) {
+    const uint32_t lane = threadIdx.x & 31u;
+    unsigned long long k[KPL];
+#pragma unroll
+    for (int j = 0; j < KPL; ++j) {
+        const uint32_t i = b + KPL * lane + (uint32_t)j;
+        k[j] = i < n ? keys[i] : ~0ull;
+    }
+    seg_sort<1, KPL>(k, lane);
+#pragma unroll
+    for (int j = 0; j < KPL; ++j) {
+        const uint32_t i = b + KPL * lane + (uint32_t)j;
+        if (i < store) keys[i] = k[j];
+    }
+}
+
+// The sorted order: position i holds keys[perm[i]] (keys[i] when perm is null).
+struct SortedKeys {
+    const unsigned long long* keys;
+    const uint16_t* perm;
+    __device__ __forceinline__ unsigned long long operator[](uint32_t i) const { return keys[perm ? (uint32_t)perm[i] : i]; }
+    __device__ __forceinline__ float p(uint32_t i) const { return __uint_as_float(~(uint32_t)((*this)[i] >> 32)); }
+};
+
+// Sorts keys[0, n) (p desc, index asc as an ascending key): returns the order as a view.
+__device__ __noinline__ SortedKeys stage_sort_u64(unsigned long long* keys, uint32_t n, uint16_t* pa, uint16_t* pb) {
+    const int tid = threadIdx.x, warp = tid >> 5;
+    if (n <= 256u) {
+        if (n >= 2u && warp == 0) {
+            if (n <= 64u)
+                warp_sort_run<2>(keys, 0u, n, n);
+            else
+                warp_sort_run<8>(keys, 0u, n, n);
+        }
+        csync();
+        return SortedKeys{keys, nullptr};
+    }
+    const uint32_t n2 = (n + 255u) & ~255u;  // (runs of 256; the pads sort last)
+    for (uint32_t sg = (uint32_t)warp; sg < (n2 >> 8); sg += kWarps) warp_sort_run<8>(keys, sg << 8, n, n2);
+    csync();
+    // Merge levels: runs of L into runs of 2L.  A thread writes E consecutive outputs, E odd
+    // so that the threads' positions fall in different shared-memory banks (a thread's range
+    // may cross from one pair of runs into the next).
+    uint32_t E = (n2 + kThreads - 1) / kThreads;
+    E |= 1u;
+    const uint16_t* src = nullptr;  // (level 1 reads the runs in place)
+    uint16_t* dst = pa;
+    for (uint32_t L = 256; L < n2; L <<= 1) {
+        auto key_at = [&](uint32_t q) -> unsigned long long { return keys[src ? (uint32_t)src[q] : q]; };
+        const uint32_t q_begin = (uint32_t)tid * E, q_end = q_begin + E < n2 ? q_begin + E : n2;
+        for (uint32_t q = q_begin; q < q_end;) {
+            const uint32_t base = q & ~(2u * L - 1u), k0 = q - base;
+            const uint32_t len = n2 - base < 2u * L ? n2 - base : 2u * L;
+            const uint32_t lenA = len < L ? len : L, lenB = len - lenA;
+            const uint32_t A = base, B = base + lenA;
+            const uint32_t cnt = (q_end < base + len ? q_end : base + len) - q;
+            // merge path: i elements of A among the first k0 outputs of the pair (ties: A first)
+            uint32_t lo = k0 > lenB ? k0 - lenB : 0u, hi = k0 < lenA ? k0 : lenA;
+            while (lo < hi) {
+                const uint32_t mid = (lo + hi) >> 1;
+                if (key_at(A + mid) <= key_at(B + k0 - 1u - mid)) lo = mid + 1u; else hi = mid;
+            }
+            uint32_t i = lo, j = k0 - lo;
+            unsigned long long ka = i < lenA ? key_at(A + i) : 0ull, kb = j < lenB ? key_at(B + j) : 0ull;
+            for (uint32_t e = 0; e < cnt; ++e) {
+                const bool takeA = i < lenA && (j >= lenB || ka <= kb);
+                const uint32_t qq = takeA ? A + i : B + j;
+                dst[q + e] = (uint16_t)(src ? (uint32_t)src[qq] : qq);
+                if (takeA) {
+                    ++i;
+                    ka = i < lenA ? key_at(A + i) : 0ull;
+                } else {
+                    ++j;
+                    kb = j < lenB ? key_at(B + j) : 0ull;
+                }
+            }
+            q += cnt;
+        }
+        csync();
+        src = dst;
+        dst = dst == pa ? pb : pa;
+    }
+    // the order into place: every thread holds its keys in registers across the barrier
+    constexpr int kPer = (int)((kStageListCap + kThreads - 1) / kThreads);
+    unsigned long long v[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = (uint32_t)tid + (uint32_t)j * kThreads;
+        v[j] = i < n ? keys[src[i]] : 0ull;
+    }
+    csync();
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+        const uint32_t i = (uint32_t)tid + (uint32_t)j * kThreads;
+        if (i < n) keys[i] = v[j];
+    }
+    csync();
+    return SortedKeys{keys, nullptr};
+}
+
+// Exclusive prefix of small per-thread counts in thread order over the block; total: the sum.
+__device__ __forceinline__ uint32_t block_excl_scan(uint32_t c, uint32_t* shw, uint32_t& total) {
+    const uint32_t incl = warp_incl_scan_plain(c);
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    csync();
+    if (l == 31) shw[w] = incl;
+    csync();
+    uint32_t before = 0, tot = 0;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) {
+        const uint32_t x = shw[i];
+        before += i < w ? x : 0u;
+        tot += x;
+    }
+    total = tot;
+    return before + incl - c;
+}
+
+// A long top-p list (sampler.rs:135-146) before its sort: the mass of its keys by probability
+// bucket (1/8 binade below the row's largest probability inv), the first bucket where the
+// mass reaches top_p + 2^-8, and the keys of the buckets down to the next one moved to the
+// front (in no particular order).  Returns their number m (n: every key stays), and in
+// p_left the largest probability of a key left out.  The finish checks that the cut lies
+// among the first m in sorted order, above p_left; the buckets only choose m.  hist: 7 x 256
+// floats of shared memory.
+constexpr uint32_t kPrefilterMin = 512;  // lists shorter than this are sorted whole
+__device__ __noinline__ uint32_t nucleus_prefilter(unsigned long long* keys, uint32_t n, float top_p, float inv,
+                                                   float* hist, RowShared& sh, float& p_left) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t ib = __float_as_uint(inv);
+    auto bucket = [ib](unsigned long long k) -> uint32_t {
+        const uint32_t pb = ~(uint32_t)(k >> 32);
+        const uint32_t b = ib > pb ? (ib - pb) >> 20 : 0u;
+        return b < 255u ? b : 255u;
+    };
+    for (int i = tid; i < kWarps * 256; i += kThreads) hist[i] = 0.0f;
+    csync();
+    float* wh = hist + warp * 256;
+    for (uint32_t i = tid; i < n; i += kThreads) {
+        const unsigned long long k = keys[i];
+        atomicAdd(&wh[bucket(k)], __uint_as_float(~(uint32_t)(k >> 32)));
+    }
+    csync();
+    for (int b = tid; b < 256; b += kThreads) {  // (column b: only this thread reads or writes it)
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) t += hist[w * 256 + b];
+        hist[b] = t;
+    }
+    csync();
+    if (warp == 0) {
+        const double target = (double)top_p + 0x1p-8;
+        double acc = 0.0;
+        int found = 255;
+        for (int b0 = 0; b0 < 256; b0 += 32) {
+            double mi = (double)hist[b0 + lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double tv = __shfl_up_sync(0xFFFFFFFFu, mi, o);
+                if (lane >= o) mi += tv;
+            }
+            const unsigned hit = __ballot_sync(0xFFFFFFFFu, acc + mi >= target);
+            if (hit) {
+                found = b0 + __ffs(hit) - 1;
+                break;
+            }
+            acc += __shfl_sync(0xFFFFFFFFu, mi, 31);
+        }
+        if (lane == 0) sh.misc[4] = (uint32_t)(found + 1);  // (one bucket of margin)
+    }
+    csync();
+    const uint32_t bsel = sh.misc[4];
+    if (bsel >= 255u) return n;
+    // compaction in waves of 8 keys a thread: every key of a wave is read before any is
+    // written, and a wave writes only below its own end
+    uint32_t m = 0, pl = 0;
+    for (uint32_t w0 = 0; w0 < n; w0 += 8u * kThreads) {
+        unsigned long long v[8];
+        uint32_t c = 0, selm = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const uint32_t i = w0 + 8u * tid + (uint32_t)j;
+            v[j] = i < n ? keys[i] : 0ull;
+            const bool in = i < n;
+            const bool sel = in && bucket(v[j]) <= bsel;
+            if (sel) {
+                selm |= 1u << j;
+                ++c;
+            } else if (in) {
+                const uint32_t pb = ~(uint32_t)(v[j] >> 32);
+                pl = pb > pl ? pb : pl;
+            }
+        }
+        uint32_t total;
+        uint32_t o = m + block_excl_scan(c, sh.red, total);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (selm & (1u << j)) keys[o++] = v[j];
+        m += total;
+        csync();
+    }
+    pl = __reduce_max_sync(0xFFFFFFFFu, pl);
+    if (lane == 0) sh.red2[warp] = pl;
+    csync();
+    uint32_t r = 0;
+#pragma unroll
+    for (int i = 0; i < kWarps; ++i) r = sh.red2[i] > r ? sh.red2[i] : r;
+    csync();
+    p_left = __uint_as_float(r);  // (positive floats order as their bits)
+    return m;
 }
 
 // Sequential f32 run over sorted probabilities keys[0..cnt) (sampler.rs:137-139 / 148-151 /
@@ -1254,27 +1574,46 @@ __device__ __noinline__ void stage_sort_u64(unsigned long long* keys, uint32_t n
 // positions go one by one on thread 0, the rest chunk by chunk with the block's exact
 // emulation (acc_tile).
 // Returns the stop position or -1; every thread gets the same s.
-__device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t cnt, int dir, float& s, float thr,
+__device__ __noinline__ int sorted_run(const SortedKeys keys, uint32_t cnt, int dir, float& s, float thr,
                                        RowShared& sh) {
     // (the head of a sorted run holds its largest elements, nearly every one an ordered step
     // of the emulation: it goes one by one; the emulation takes the rest)
     const uint32_t head = cnt < 512u ? cnt : 512u;
     {
         if (threadIdx.x == 0) {
+            // Groups of eight: the sum steps through a group with no branch, and the stop test
+            // runs once per group (the run is monotone: p >= 0), then finds the first position
+            // inside it.  Positions past the head add 0, which neither moves s nor stops it.
+            auto p_at = [&](uint32_t i) -> float {
+                return i < head ? keys.p(i) : 0.0f;
+            };
             float cur = s;
             int stop = -1;
-            // (eight values loaded at a time: the loads do not wait for the sum)
-            for (uint32_t i0 = 0; i0 < head && stop < 0; i0 += 8) {
-                float v[8];
+            float v[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
-                    v[j] = i0 + j < head ? __uint_as_float(~(uint32_t)(keys[i0 + j] >> 32)) : 0.0f;
+            for (int j = 0; j < 8; ++j) v[j] = p_at((uint32_t)j);
+            for (uint32_t i0 = 0; i0 < head; i0 += 8) {
+                float nv[8], c[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    if (i0 + j >= head || stop >= 0) break;
-                    cur = dir > 0 ? __fadd_rn(cur, v[j]) : __fsub_rn(cur, v[j]);
-                    if (dir > 0 ? cur >= thr : cur <= 0.0f) stop = (int)(i0 + j);
+                for (int j = 0; j < 8; ++j) nv[j] = p_at(i0 + 8u + (uint32_t)j);  // (the next group)
+                if (dir > 0) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) c[j] = cur = __fadd_rn(cur, v[j]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) c[j] = cur = __fsub_rn(cur, v[j]);
                 }
+                if (dir > 0 ? cur >= thr : cur <= 0.0f) {
+                    int j = 7;
+#pragma unroll
+                    for (int q = 6; q >= 0; --q)
+                        if (dir > 0 ? c[q] >= thr : c[q] <= 0.0f) j = q;
+                    stop = (int)i0 + j;
+                    cur = c[j];
+                    break;
+                }
+#pragma unroll
+                for (int j = 0; j < 8; ++j) v[j] = nv[j];
             }
             sh.fstate = cur;
             sh.stop = stop;
@@ -1288,7 +1627,11 @@ __device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t 
     for (uint32_t b = head; b < cnt; b += kChunk) {
         const uint32_t tc = cnt - b < (uint32_t)kChunk ? cnt - b : (uint32_t)kChunk;
         float v[kVpt];
-        load_sorted_tile(keys + b, tc, v);
+#pragma unroll
+        for (int i = 0; i < kVpt; ++i) {  // (load_sorted_tile's layout, through the order)
+            const int li = li_of(i);
+            v[i] = (uint32_t)li < tc ? keys.p(b + (uint32_t)li) : 0.0f;
+        }
         uint32_t ex = 0xFFFFFFFFu;
         const int st = acc_tile(v, ex, (int)tc, dir, s, thr, NoExact(), sh);
         if (st >= 0) return (int)b + st;
@@ -1299,8 +1642,9 @@ __device__ __noinline__ int sorted_run(const unsigned long long* keys, uint32_t 
 // One CTA per row: the candidates' exact probabilities p = fl(libm expf(d) * (1 / S))
 // (sampler.rs:129-131, ops.rs:409-416), sorted (p desc, index asc), then top-k, the top-p
 // cut, the survivor sum and the draw (sampler.rs:122-162).
-__global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) {
-    extern __shared__ __align__(16) unsigned long long keys[];  // kStageListCap
+__global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CTAs of kThreads per SM)
+    extern __shared__ __align__(16) unsigned long long keys[];  // kStageListCap, then the sort's permutations
+    uint16_t* perm = reinterpret_cast<uint16_t*>(keys + kStageListCap);  // 2 x kStageListCap
     __shared__ RowShared sh;
     const lrs_kernel_args_t& a = S.a;
     const uint32_t r = blockIdx.x;
@@ -1330,7 +1674,11 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
     int stp = -1;
     uint32_t kk = 0, cut = 0;
     long long c_regather = 0, c_sort = 0, c_runs = 0, tm = 0;  // (diagnostics: cycles by phase)
-    for (int attempt = nk > kStageListCap ? 1 : 0; attempt < 2; ++attempt) {
+    SortedKeys sk{keys, nullptr};
+    int split = 0;       // (the regather's levels: the coarse bucket that overflows the list ...)
+    uint32_t above = 0;  // (... and the count above it)
+    // attempt 0: the list; 1: the regather at a coarse edge; 2: at a fine edge
+    for (int attempt = nk > kStageListCap ? 1 : 0; attempt < 3; ++attempt) {
         if (attempt == 0) {
             const uint2* lst = S.lists + (uint64_t)r * kStageListCap;
             for (uint32_t i = tid; i < nk; i += kThreads) {
@@ -1339,38 +1687,60 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
                 keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | e.y;
             }
         } else {
-            // The nucleus reaches deeper than the list: gather it from the row, at the deepest
-            // bucket edge (width 1/32 in d) whose elements fit in the list's capacity.
+            // The nucleus reaches deeper than the list: gather it from the row down to a bucket
+            // edge whose elements fit in the list's capacity.
             csync();
             tm = clock64();
-            n_keys = regather_nucleus(S, r, P, M, inv, exptab, keys, sh, cand);
+            n_keys = regather_nucleus(S, r, P, M, inv, exptab, keys, sh, cand, attempt - 1, split, above);
             c_regather += clock64() - tm;
             if (n_keys == 0xFFFFFFFFu) {
                 if (tid == 0) stage_fallback(S, r);
                 return;
             }
         }
-        csync();
-        tm = clock64();
-        stage_sort_u64(keys, n_keys);  // (p desc, index asc): the reference's order (see the oracle on ties)
-        c_sort += clock64() - tm;
-        kk = rp.k < n_keys ? rp.k : n_keys;  // (path K: the list holds the top k; path N: the nucleus)
-        // top-p over the first kk (sampler.rs:135-146); the survivor sum is the same sequence up
-        // to the cutoff (sampler.rs:148-151)
-        cum = 0.0f;
-        tm = clock64();
-        stp = sorted_run(keys, kk, +1, cum, topp_on ? P.top_p : kInf, sh);
-        c_runs += clock64() - tm;
-        cut = stp >= 0 ? (uint32_t)stp + 1 : kk;
-        // path N: the list holds every element with d >= cand, so its sorted order is the row's
-        // as far as its probabilities exceed the largest one an element outside can have; the
-        // cut (top_p reached, or k reached) must lie there, unless the list is the whole row
-        if ((rp.flags & kRowPathK) || n_keys >= a.n) break;
-        const float p_out = __fmul_rn(exact_expf(cand, exptab), inv);
-        const bool inside = (stp >= 0 || kk == rp.k) && cut > 0 &&
-                            __uint_as_float(~(uint32_t)(keys[cut - 1] >> 32)) > p_out;
+        // pass 0 of a long top-p list sorts only the head the prefilter keeps; pass 1 the
+        // whole list again (from its copy in the row's list area) if the cut is not inside it
+        bool inside = false;
+        for (int pass = 0; pass < 2 && !inside; ++pass) {
+            uint32_t m_keys = n_keys;
+            float p_left = 0.0f;
+            unsigned long long* backup = reinterpret_cast<unsigned long long*>(S.lists + (uint64_t)r * kStageListCap);
+            csync();
+            if (pass == 0 && (rp.flags & kRowPathN) && topp_on && n_keys >= kPrefilterMin) {
+                for (uint32_t i = tid; i < n_keys; i += kThreads) __stcg(backup + i, keys[i]);
+                m_keys = nucleus_prefilter(keys, n_keys, P.top_p, inv, reinterpret_cast<float*>(perm), sh, p_left);
+            } else if (pass == 1) {
+                for (uint32_t i = tid; i < n_keys; i += kThreads) keys[i] = __ldcg(backup + i);
+            }
+            csync();
+            tm = clock64();
+            sk = stage_sort_u64(keys, m_keys, perm, perm + kStageListCap);  // (p desc, index asc): the reference's order
+            c_sort += clock64() - tm;
+            kk = rp.k < m_keys ? rp.k : m_keys;  // (path K: the list holds the top k; path N: the nucleus)
+            // top-p over the first kk (sampler.rs:135-146); the survivor sum is the same sequence
+            // up to the cutoff (sampler.rs:148-151)
+            cum = 0.0f;
+            tm = clock64();
+            stp = sorted_run(sk, kk, +1, cum, topp_on ? P.top_p : kInf, sh);
+            c_runs += clock64() - tm;
+            cut = stp >= 0 ? (uint32_t)stp + 1 : kk;
+            if (rp.flags & kRowPathK) {
+                inside = true;
+                break;
+            }
+            // path N: the list holds every element with d >= cand (every element, when it is the
+            // whole row), so its sorted order is the row's as far as its probabilities exceed the
+            // largest one an element outside can have (p_out), and the largest one the prefilter
+            // left out; the cut (top_p reached, or k reached) must lie there
+            const bool whole = n_keys >= a.n;
+            const float p_out = whole ? 0.0f : __fmul_rn(exact_expf(cand, exptab), inv);
+            const float p_lim = fmaxf(p_out, p_left);
+            const bool complete = whole && m_keys == n_keys;
+            inside = complete || ((stp >= 0 || kk == rp.k) && cut > 0 && sk.p(cut - 1) > p_lim);
+            if (m_keys == n_keys) break;  // (no second pass without a prefilter)
+        }
         if (inside) break;
-        if (attempt == 1) {
+        if (attempt == 2) {
             if (tid == 0) stage_fallback(S, r);
             return;
         }
@@ -1382,7 +1752,7 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
         r0 = __fmul_rn(next_f32(&st), cum);  // sampler.rs:155
         float rv = r0;
         tm = clock64();
-        const int w = sorted_run(keys, cut, -1, rv, 0.0f, sh);
+        const int w = sorted_run(sk, cut, -1, rv, 0.0f, sh);
         c_runs += clock64() - tm;
         ps = w >= 0 ? (uint32_t)w : cut - 1;  // sampler.rs:156-162
     }
@@ -1391,7 +1761,7 @@ __global__ void __launch_bounds__(kThreads) lrs_stage_finish(const StageArgs S) 
         stage_fallback(S, r);
         return;
     }
-    const unsigned long long chosen = keys[ps];
+    const unsigned long long chosen = sk[ps];
     lrs_row_info inf = blank_info(2u, rp.k);
     inf.token = (uint32_t)(chosen & 0xFFFFFFFFu);
     inf.prob = __uint_as_float(~(uint32_t)(chosen >> 32));
