@@ -40,7 +40,7 @@ constexpr uint32_t kStageListCap = 8192;           // candidate-list entries per
 // the finish's dynamic shared memory: the keys, then the sort's two 16-bit permutations
 constexpr size_t kStageFinishSmem = kStageListCap * sizeof(unsigned long long) + 2 * kStageListCap * sizeof(uint16_t);
 constexpr int kStageNucleusBuckets = 580;          // mass buckets of width 1/32 in (M - x')
-constexpr uint32_t kStageNucleusRank = 2048;       // top-p lists reach at least the lane maximum of this rank
+constexpr float kStageNucleusFill = 0.73f;         // top-p lists: the share of the capacity aimed at
 constexpr uint32_t kStageMaxTiles = 256;           // tiles of the longest stochastic row the stages take (n <= 262,144)
 // flags of a row's prep record
 constexpr uint32_t kRowDone = 1u;        // outputs written by the prep (greedy, NaN, n <= 1)
@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         // guesses: the first bucket edge (width 1/32) where the mass of the lane maxima above
         // it reaches (top_p + 2^-16) times the estimated sum (lane maxima are distinct
         // elements, so the mass of all elements there is at least that), and the depth of
-        // the kStageNucleusRank-th largest lane maximum (a list of a few thousand entries).
+        // the lane maximum of a rank that fills about kStageNucleusFill of the list.
         // The finish checks that the cut lies inside the list, and gathers a deeper list
         // from the row where it does not.
         for (int b = tid; b < kStageNucleusBuckets; b += kStageThreads) ps.mass[b] = 0.0f;
@@ -597,7 +597,15 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         }
         __syncthreads();
         const float th_mass = ps.bf[0];
-        const float x_rank = block_select_desc(ps.vals, nv, kStageNucleusRank < nv ? kStageNucleusRank : nv, ps);
+        // The rank: with the elements of a row in no particular order, a fraction f of the lanes
+        // (32 elements each) whose maximum is at or above a threshold means about
+        // 32 nl (1 - (1 - f)^(1/32)) elements there; the rank is the f that makes that
+        // kStageNucleusFill of the list's capacity.
+        const double fill = (double)kStageNucleusFill * kStageListCap;
+        const double f = fill >= 32.0 * nl ? 1.0 : 1.0 - pow(1.0 - fill / (32.0 * nl), 32.0);
+        uint32_t rank = (uint32_t)(f * nl);
+        rank = rank < 1u ? 1u : (rank > nv ? nv : rank);
+        const float x_rank = block_select_desc(ps.vals, nv, rank, ps);
         const float th_rank = x_rank > -kInf ? __fsub_rn(x_rank, M) : -kInf;
         rp.flags = kRowPathN;
         rp.cand = fmaxf(th_mass, th_rank);  // elements with d >= this (d = fl(x' - M))
@@ -1477,7 +1485,7 @@ __device__ __forceinline__ uint32_t block_excl_scan(uint32_t c, uint32_t* shw, u
 
 // A long top-p list (sampler.rs:135-146) before its sort: the mass of its keys by probability
 // bucket (1/8 binade below the row's largest probability inv), the first bucket where the
-// mass reaches top_p + 2^-8, and the keys of the buckets down to the next one moved to the
+// mass reaches top_p + 2^-11, and the keys of the buckets down to the next one moved to the
 // front (in no particular order).  Returns their number m (n: every key stays), and in
 // p_left the largest probability of a key left out.  The finish checks that the cut lies
 // among the first m in sorted order, above p_left; the buckets only choose m.  hist: 7 x 256
@@ -1508,7 +1516,7 @@ __device__ __noinline__ uint32_t nucleus_prefilter(unsigned long long* keys, uin
     }
     csync();
     if (warp == 0) {
-        const double target = (double)top_p + 0x1p-8;
+        const double target = (double)top_p + 0x1p-11;
         double acc = 0.0;
         int found = 255;
         for (int b0 = 0; b0 < 256; b0 += 32) {
