@@ -117,6 +117,20 @@ __device__ __forceinline__ bool tile_window(const uint32_t* hrow, uint32_t hstar
     return __any_sync(0xFFFFFFFFu, wb[lane] != 0u);
 }
 
+// The penalty on the window's elements of a tile in the block layout (wb: the window's bits).
+__device__ __forceinline__ void penalise_tile_blocks(const uint32_t* wb, float penalty, float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t b4 = (wb[4 * j + (lane >> 3)] >> (4 * (lane & 7))) & 15u;
+        if (b4) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+                if ((b4 >> c) & 1u) v[4 * j + c] = penalise(v[4 * j + c], penalty);
+        }
+    }
+}
+
 // The warp's tile in the block layout: v[4 j + c] = element 128 j + 4 L + c (-inf past cnt),
 // the penalty applied to the window's elements (sampler.rs:96-100).
 __device__ __forceinline__ void load_tile_blocks(const float* base, uint32_t cnt, bool pen, const uint32_t* wb,
@@ -133,17 +147,7 @@ __device__ __forceinline__ void load_tile_blocks(const float* base, uint32_t cnt
         v[4 * j + 2] = q.z;
         v[4 * j + 3] = q.w;
     }
-    if (pen) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t b4 = (wb[4 * j + (lane >> 3)] >> (4 * (lane & 7))) & 15u;
-            if (b4) {
-#pragma unroll
-                for (int c = 0; c < 4; ++c)
-                    if ((b4 >> c) & 1u) v[4 * j + c] = penalise(v[4 * j + c], penalty);
-            }
-        }
-    }
+    if (pen) penalise_tile_blocks(wb, penalty, v);
 }
 
 __device__ __forceinline__ void prefetch_l2(const void* p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
@@ -674,59 +678,59 @@ __device__ __forceinline__ ElemCls classify_units(float d, int u0, float bm0, fl
     return r;
 }
 
-// The warp's tile in index order in its shared staging area (x[q] = element g0 + q, -inf
-// past cnt), the penalty applied to the window's elements (sampler.rs:96-100).
-__device__ __forceinline__ void stage_tile(const float* base, uint32_t cnt, bool pen, const uint32_t* wb, float penalty,
-                                           float* x) {
-    const int lane = threadIdx.x & 31;
-    const float ninf = __int_as_float(0xFF800000);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t e0 = 128u * j + 4u * lane;
-        float4 q = make_float4(ninf, ninf, ninf, ninf);
-        if (e0 < cnt) q = __ldg(reinterpret_cast<const float4*>(base + e0));
-        *reinterpret_cast<float4*>(x + e0) = q;
-    }
-    __syncwarp();
-    if (pen) {
-        for (uint32_t m = wb[lane]; m; m &= m - 1u) {  // (lane L: elements 32 L .. 32 L + 31)
-            const uint32_t q = 32u * lane + (uint32_t)(__ffs(m) - 1);
-            x[q] = penalise(x[q], penalty);
-        }
-        __syncwarp();
-    }
-}
-
 constexpr int kClassifyWarps = 4;  // warps per block of the classify stage
 
+// One warp per tile (grid-stride over every row's tiles).  The tile stays in registers in the
+// block layout (lane L: elements 128 j + 4 L + c, j the block of 128); a lane queues its live
+// elements' d values (x' > xthr) with their blocks in shared memory, then classifies its queue
+// in block order, adding each block's increments once per change of block.  Candidates of the
+// finish go to the row's list under one reservation per warp.
 __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const StageArgs S) {
     __shared__ uint32_t wbits[kClassifyWarps * 32];
-    // per warp: the tile in index order; the live elements' d values are written over its
-    // part already read (the compacted position never passes the slice being read)
-    __shared__ __align__(16) float tile[kClassifyWarps * kTile];
-    __shared__ uint8_t sblock[kClassifyWarps * kTile];            // ... and the live elements' blocks
-    __shared__ uint32_t bcount[kClassifyWarps * 17];              // ... per block increment totals and flags
+    __shared__ float qd[kClassifyWarps * 32 * 32];    // per warp: queue slot k of lane L at 32 k + L
+    __shared__ uint8_t qb[kClassifyWarps * 32 * 32];  // ... and the element's block
+    __shared__ uint32_t bcount[kClassifyWarps * 16];  // per warp: block increment totals (grids u0, u0 + 1)
     const lrs_kernel_args_t& a = S.a;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     uint32_t* wb = wbits + warp * 32;
-    float* x = tile + warp * kTile;
-    float* st = x;
-    uint8_t* sbk = sblock + warp * kTile;
-    uint32_t* bc = bcount + warp * 17;
-    uint32_t* bfl = bc + 16;
-    const unsigned lt = (1u << lane) - 1u;
+    float* wq = qd + warp * 1024;
+    uint8_t* wqb = qb + warp * 1024;
+    uint32_t* bc = bcount + warp * 16;
     const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
     const uint64_t tasks = (uint64_t)a.rows * S.nt;
     const uint64_t stride = (uint64_t)gridDim.x * kClassifyWarps;
-    for (uint64_t task = (uint64_t)blockIdx.x * kClassifyWarps + warp; task < tasks; task += stride) {
-        const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
-        const RowPrep rp = S.rprep[r];
-        if (rp.flags & (kRowDone | kRowFallback)) continue;
+    uint64_t task = (uint64_t)blockIdx.x * kClassifyWarps + warp;
+    uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);  // (then stepped)
+    const uint32_t sq = (uint32_t)(stride / S.nt), sr = (uint32_t)(stride % S.nt);
+    for (; task < tasks; task += stride, r += sq, t += sr) {
+        if (t >= S.nt) {
+            t -= S.nt;
+            ++r;
+        }
         const Geo g = row_geometry(a, r);
         if (t >= g.nchunks) continue;
+        const uint32_t cnt = chunk_count(g, t);
+        const uint32_t g0 = g.head + t * kTile;
+        // the tile's raw values first: their latency overlaps the records' (nearly every tile
+        // of a row holds live elements)
+        float v[32];
+        load_tile_blocks(g.row + g0, cnt, false, wb, 1.0f, v);
+        {  // (the warp's next tile into L2, a line per lane)
+            uint32_t tn = t + sr, rn = r + sq;
+            if (tn >= S.nt) {
+                tn -= S.nt;
+                ++rn;
+            }
+            if (task + stride < tasks && tn < g.nchunks && (uint32_t)lane * 32u < chunk_count(g, tn))
+                prefetch_l2(a.logits + (uint64_t)rn * a.ld + g.head + tn * kTile + lane * 32u);
+        }
         const uint64_t ti = (uint64_t)r * S.nt + t;
+        const RowPrep rp = S.rprep[r];
         const TilePrep tp = S.tprep[ti];
         const float mt = S.tstat[ti].x;
+        const lrs_params P = a.params[r];
+        const uint32_t hlen = a.hist_len ? a.hist_len[r] : 0u;
+        if (rp.flags & (kRowDone | kRowFallback)) continue;
         const float M = rp.M, inv_t = rp.inv_t;
         const bool pathK = rp.flags & kRowPathK;
         const float dmax = __fsub_rn(mt, M);
@@ -739,72 +743,77 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
             }
             continue;
         }
-        const lrs_params P = a.params[r];
-        const bool pen_on = P.repetition_penalty != 1.0f;
-        const uint32_t cnt = chunk_count(g, t);
-        const uint32_t g0 = g.head + t * kTile;
-        bool pen = false;
-        if (pen_on && a.hist_len) {
-            const uint32_t hlen = a.hist_len[r];
-            pen = tile_window(a.hist + (uint64_t)r * a.hist_ld, window_start(P, hlen), hlen, g0, cnt, wb);
+        if (P.repetition_penalty != 1.0f && hlen) {
+            if (tile_window(a.hist + (uint64_t)r * a.hist_ld, window_start(P, hlen), hlen, g0, cnt, wb))
+                penalise_tile_blocks(wb, P.repetition_penalty, v);
         }
-        stage_tile(g.row + g0, cnt, pen, wb, P.repetition_penalty, x);
-        // one pass over 32-element slices (lane L: element 32 i + L): the candidates go to the
-        // row's list, the live elements' d values are compacted in index order
         const float xthr = sum_live ? tp.xthr : __int_as_float(0x7F800000);
         const float craw = cand_live ? rp.cand_raw : __int_as_float(0x7F800000);
-        uint32_t tot = 0;
-        uint2* lst = S.lists + (uint64_t)r * kStageListCap;
-#pragma unroll 4
+        // the lane's live elements (x' > xthr) into its queue (in block order); its candidates
+        // (x' > craw: d, or the scaled logit, at or above the list threshold)
+        uint32_t nq = 0, cm = 0;
+#pragma unroll
         for (int i = 0; i < 32; ++i) {
-            const uint32_t q = 32u * i + lane;
-            const float v = x[q];
-            const unsigned lm = __ballot_sync(0xFFFFFFFFu, v > xthr);
-            __syncwarp();  // (the slice is read before any d value lands on it)
-            if (v > xthr) {
-                const uint32_t o = tot + (uint32_t)__popc(lm & lt);
-                st[o] = d_of(v, inv_t, M);
-                sbk[o] = (uint8_t)(q >> 7);
+            cm |= (v[i] > craw ? 1u : 0u) << i;
+            if (v[i] > xthr) {
+                wq[nq * 32u + lane] = d_of(v[i], inv_t, M);
+                wqb[nq * 32u + lane] = (uint8_t)(i >> 2);
+                ++nq;
             }
-            tot += (uint32_t)__popc(lm);
-            if (__any_sync(0xFFFFFFFFu, v > craw)) {  // (rare: the candidates of the finish)
-                const float xs = __fmul_rn(v, inv_t);
-                const bool c = v > craw && (pathK ? xs >= rp.cand : __fsub_rn(xs, M) >= rp.cand);
-                const unsigned cm = __ballot_sync(0xFFFFFFFFu, c);
-                if (cm) {
-                    uint32_t base = 0;
-                    if (lane == 0) base = atomicAdd(S.list_n + r, (uint32_t)__popc(cm));
-                    base = __shfl_sync(0xFFFFFFFFu, base, 0) + (uint32_t)__popc(cm & lt);
-                    if (c && base < kStageListCap) lst[base] = make_uint2(__float_as_uint(xs), g0 + q);
+        }
+        if (__any_sync(0xFFFFFFFFu, cm != 0u)) {  // the candidates: one reservation per warp
+            const uint32_t nc = (uint32_t)__popc(cm);
+            const uint32_t incl = warp_incl_scan_plain(nc);
+            uint32_t base = 0;
+            if (lane == 31) base = atomicAdd(S.list_n + r, incl);
+            base = __shfl_sync(0xFFFFFFFFu, base, 31) + incl - nc;
+            uint2* lst = S.lists + (uint64_t)r * kStageListCap;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if ((cm >> i) & 1u) {
+                    const uint32_t gi = g0 + 128u * (uint32_t)(i >> 2) + 4u * (uint32_t)lane + (uint32_t)(i & 3);
+                    if (base < kStageListCap) lst[base] = make_uint2(__float_as_uint(__fmul_rn(v[i], inv_t)), gi);
+                    ++base;
                 }
             }
         }
         uint32_t t0v = 0, t1v = 0, fl = 0, bf = 0;
-        if (sum_live) {
-            // increments of the live elements on grids u0 and u0 + 1, per block of 128 (a lane
-            // classifies total / 32 of them)
+        if (__any_sync(0xFFFFFFFFu, nq != 0u)) {
+            // increments of the live elements on grids u0 and u0 + 1, per block of 128
             const int u0 = tp.u0;
             const bool one = tp.flags & kTileOne;
             if (lane < 16) bc[lane] = 0u;
-            if (lane == 0) bfl[0] = 0u;
             __syncwarp();
             const float bm0 = grid_value(u0, kTwo23), bm1 = __fadd_rn(bm0, bm0);
             const float h0 = u0 > -149 ? pow2f(u0 - 1) : 0.0f, h1 = pow2f(u0);
-            for (uint32_t j = (uint32_t)lane; j < tot; j += 32) {
-                const ElemCls c = classify_units(st[j], u0, bm0, bm1, h0, h1, one, exptab);
-                const uint32_t b = sbk[j];
-                if (c.c0) atomicAdd(&bc[b], c.c0);
-                if (c.c1) atomicAdd(&bc[8 + b], c.c1);
-                const uint32_t f = (1u << b) | (c.sp0 ? 0x100u << b : 0u) | (c.sp1 ? 0x10000u << b : 0u);
-                atomicOr(&bfl[0], f);
+            uint32_t cb = 8u, a0 = 0u, a1 = 0u, bfl = 0u;
+            for (uint32_t k = 0; k < nq; ++k) {
+                const float d = wq[k * 32u + lane];
+                const uint32_t b = wqb[k * 32u + lane];
+                if (b != cb) {
+                    if (cb < 8u) {
+                        atomicAdd(&bc[cb], a0);
+                        atomicAdd(&bc[8u + cb], a1);
+                    }
+                    cb = b;
+                    a0 = a1 = 0u;
+                }
+                const ElemCls c = classify_units(d, u0, bm0, bm1, h0, h1, one, exptab);
+                a0 += c.c0;  // (a block's count is at most 128 * 2^23 < 2^32)
+                a1 += c.c1;
+                bfl |= (1u << b) | (c.sp0 ? 0x100u << b : 0u) | (c.sp1 ? 0x10000u << b : 0u);
+            }
+            if (cb < 8u) {
+                atomicAdd(&bc[cb], a0);
+                atomicAdd(&bc[8u + cb], a1);
             }
             __syncwarp();
-            // (a block's count is at most 128 * 2^23 < 2^32; saturated where it leaves the grid)
+            // (saturated where a block leaves the grid)
             const uint32_t c0 = lane < 8 ? min(bc[lane], kSat) : 0u, c1 = lane < 8 ? min(bc[8 + lane], kSat) : 0u;
-            bf = bfl[0];
+            bf = __reduce_or_sync(0xFFFFFFFFu, bfl);
             t0v = min(__reduce_add_sync(0xFFFFFFFFu, c0), kSat);
             t1v = min(__reduce_add_sync(0xFFFFFFFFu, c1), kSat);
-            fl = (tot ? kTileLive : 0u) | ((bf >> 8) & 0xFFu ? kTileSp0 : 0u) | ((bf >> 16) & 0xFFu ? kTileSp1 : 0u);
+            fl = kTileLive | ((bf >> 8) & 0xFFu ? kTileSp0 : 0u) | ((bf >> 16) & 0xFFu ? kTileSp1 : 0u);
             if (lane < 8) {
                 S.tres[ti].b0[lane] = c0;
                 S.tres[ti].b1[lane] = c1;
@@ -817,7 +826,7 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
             out->flags = fl;
             out->bflags = bf;
         }
-        __syncwarp();  // (the staging areas are reused by the next tile)
+        __syncwarp();  // (the queue and counts are reused by the next tile)
     }
 }
 
