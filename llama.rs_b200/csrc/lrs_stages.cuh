@@ -605,12 +605,16 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         // (32 elements each) whose maximum is at or above a threshold means about
         // 32 nl (1 - (1 - f)^(1/32)) elements there; the rank is the f that makes that
         // kStageNucleusFill of the list's capacity.
+        // (A row that fits whole takes every element.)
         const double fill = (double)kStageNucleusFill * kStageListCap;
-        const double f = fill >= 32.0 * nl ? 1.0 : 1.0 - pow(1.0 - fill / (32.0 * nl), 32.0);
-        uint32_t rank = (uint32_t)(f * nl);
-        rank = rank < 1u ? 1u : (rank > nv ? nv : rank);
-        const float x_rank = block_select_desc(ps.vals, nv, rank, ps);
-        const float th_rank = x_rank > -kInf ? __fsub_rn(x_rank, M) : -kInf;
+        float th_rank = -kInf;
+        if (fill < 32.0 * nl) {
+            const double f = 1.0 - pow(1.0 - fill / (32.0 * nl), 32.0);
+            uint32_t rank = (uint32_t)(f * nl);
+            rank = rank < 1u ? 1u : (rank > nv ? nv : rank);
+            const float x_rank = block_select_desc(ps.vals, nv, rank, ps);
+            th_rank = x_rank > -kInf ? __fsub_rn(x_rank, M) : -kInf;
+        }
         rp.flags = kRowPathN;
         rp.cand = fmaxf(th_mass, th_rank);  // elements with d >= this (d = fl(x' - M))
         rp.cand_raw = rp.cand > -kInf ? raw_threshold(rp.cand, inv_t, M) : -kInf;  // largest raw x with d below it
@@ -1156,10 +1160,11 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     };
     // mode 0: coarse counts; mode 1: fine counts in coarse bucket cb; mode 2: gather d >= th
     auto visit = [&](int mode, uint32_t cb, float th) {
-        // edge elements (warp 0, lanes 0 .. edges-1), then the tiles (warp w: tiles w, w + 7, ...)
+        // the tiles, then the edge elements as item nchunks (lanes 0 .. edges-1); warp w takes
+        // items w, w + 7, ...
         const uint32_t edges = g.head + g.tail;
-        for (uint32_t t = (uint32_t)warp; t < g.nchunks + (warp == 0 ? 1u : 0u); t += kWarps) {
-            const bool edge = t == g.nchunks;  // (warp 0's last item)
+        for (uint32_t t = (uint32_t)warp; t <= g.nchunks; t += kWarps) {
+            const bool edge = t == g.nchunks;
             float v[32];
             uint32_t g0 = 0;
             if (!edge) {

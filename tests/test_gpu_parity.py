@@ -81,6 +81,29 @@ def test_many_short_rows_every_claim_key():
     assert compare(gpu, ref, "many short rows") == rows
 
 
+
+def test_regathered_nucleus_with_edge_elements():
+    # Long misaligned rows whose 0.999 nucleus (about 7,000 high logits) is deeper than the
+    # rank-limited list, so the finish gathers it again from the row; the unaligned head and
+    # tail elements (outside the 16-byte-aligned tiles) are among the high ones and must be
+    # gathered too, whatever the number of tiles.
+    rng = np.random.default_rng(23)
+    rows, n, ld = 4, 151_937, 151_941
+    buf = np.full((rows, ld), -40.0, np.float32)
+    for r in range(rows):
+        hi = rng.choice(n, 7000, replace=False)
+        buf[r, hi] = rng.uniform(0.0, 1.0, 7000).astype(np.float32)
+        buf[r, [0, 1, 2, n - 3, n - 2, n - 1]] = rng.uniform(0.5, 1.0, 6).astype(np.float32)
+    p = O.make_params(rows=rows, temperature=1.0, top_k=0, top_p=0.999, repetition_penalty=1.0)
+    st = (np.arange(rows, dtype=np.uint64) * np.uint64(0x9E3779B97F4A7C15)) | np.uint64(1)
+    gpu = run_device(buf, n, None, None, p, st, ld=ld)
+    ref = run_oracle(np.ascontiguousarray(buf[:, :n]), n, None, None, p, st)
+    assert compare(gpu, ref, "regathered nucleus") == rows
+    infos = gpu[1]
+    staged = infos["cycles"][:, 4] == 1
+    assert staged.all()
+    assert (infos["cycles"][:, 3] > 0).any(), "no row took the regather path"
+
 def test_greedy_rows_with_planted_ties():
     w = W.greedy(row_ids=range(0, 256, 4))
     assert _check_workload(w, "greedy") == 64
