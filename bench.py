@@ -5,14 +5,16 @@
 Workload (per GPU): the headline configuration, 1024 rows x 151,936 f32 logits with the
 mixed per-row parameters of the benchmark's config 3 (temperature U[0.5,1.5], top_k in
 {0,20,40,100}, top_p U[0.8,1.0], repetition penalty U[1.0,1.3] over a 64-token window),
-seeded synthetic data.  A step samples every row once (two launches: the one-block pass
-that orders the rows for claiming, then the sampling kernel).  Rows are
-independent, so N GPUs run N replicas on different rows (weak scaling, no collective).
+seeded synthetic data.  A step samples every row once through the staged pipeline: six
+launches (tile statistics, per-row prep, tile classification, the exact running sum, the
+finish, then lrs_sample_rows on the rows the stages leave).  Rows are independent, so N GPUs
+run N replicas on different rows (weak scaling, no collective).
 
 value      rows/s over all GPUs with inputs resident in HBM (CUDA events, max over ranks)
 e2e        the same metric through the host-buffer entry point (lrs_sample): pinned host
            logits copied in and tokens/statuses copied out inside the timed region
-roofline   algorithmic bytes (4 * vocab + 4 * window per row) / kernel time vs measured HBM copy bandwidth
+roofline   algorithmic bytes (4 * vocab + 4 * window per row) / step time (the six launches) vs
+           measured HBM copy bandwidth; traffic = DRAM bytes per step from the committed ncu summary
 cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of the same rows
            (the first --cpu-rows rows, repeated for about --cpu-seconds on all host threads)
 --impl reference  times that CPU restatement alone (all host threads) on the same workload
@@ -45,6 +47,7 @@ WORKLOAD = ("headline: 1024 rows x 151,936 f32 logits per GPU, Gumbel + Zipf-lik
             "permutation, temperature U[0.5,1.5], top_k {0,20,40,100}, top_p U[0.8,1.0], "
             "repetition penalty U[1.0,1.3] over a 64-token window")
 FALLBACK_HBM_GBS = 6650.0
+STAGE_LAUNCHES = 6  # kernels of one step (the staged pipeline, lrs_stage_launch)
 NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal (the north star quotes 8 TB/s)
 
 
@@ -57,12 +60,12 @@ def peaks():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic(name="lrs_sample_rows_headline.txt"):
-    """dram bytes per launch from the committed ncu summary, if present."""
+def profile_traffic(name="staged_pipeline_headline.txt", key="dram_bytes_per_step_full_size:"):
+    """DRAM bytes per step from the committed ncu summary, if present."""
     path = os.path.join(REPO, "profiles", name)
     try:
         for line in open(path):
-            if line.startswith("dram_bytes_per_launch_full_size:"):
+            if line.startswith(key):
                 return float(line.split(":", 1)[1].split()[0])
     except OSError:
         pass
@@ -271,7 +274,8 @@ def run_vocab_sharded(args, world, rank, local):
                                    f"({V // world} each), one all-gather per step, top_k 50, top_p 0.95, temp 0.7",
                        "parallelism": f"vocabulary over {world} GPU(s)"},
             "exchange_ms_per_step": exch_ms / args.steps, "exchange_share": exch_ms / total_ms,
-            "tokens_match_unsharded": ok, "gpu_launches": 2 * args.steps,
+            "tokens_match_unsharded": ok,
+            "gpu_launches": (1 + STAGE_LAUNCHES) * args.steps,  # the row assembly, then the sampler
         }
         print(json.dumps(line), flush=True)
     vsamp.close()
@@ -500,10 +504,11 @@ def main():
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "nominal_peak": NOMINAL_HBM_GBS, "frac_of_nominal": achieved / NOMINAL_HBM_GBS,
-                         "peak_kind": kind, "kernel": "lrs_sample_rows",
+                         "peak_kind": kind,
+                         "kernel": "staged pipeline: lrs_stage_stats, _prep, _classify, _sum, _finish, lrs_sample_rows",
                          "kernel_ms_mean": mean_launch, "bytes_per_launch": rows * bytes_per_row},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": 2 * args.steps,  # the ordering pass and the sampling kernel
+            "gpu_launches": STAGE_LAUNCHES * args.steps,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
