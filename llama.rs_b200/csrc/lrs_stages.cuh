@@ -852,14 +852,21 @@ __device__ __noinline__ float warp_walk_block(const float* bbase, uint32_t bcnt,
         float4 q = make_float4(ninf, ninf, ninf, ninf);
         if (4u * (uint32_t)lane < bcnt) q = __ldg(reinterpret_cast<const float4*>(bbase + 4 * lane));
         float x[4] = {q.x, q.y, q.z, q.w};
+        // (the four exps side by side; the table only where the rounded double exp is too
+        // close to a rounding midpoint)
+        float d[4];
+        bool ok[4];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
             if ((pen4 >> c) & 1u) x[c] = penalise(x[c], penalty);
-            e[c] = 0.0f;
-            if (x[c] > xthr) {
-                const float d = d_of(x[c], inv_t, M);
-                e[c] = d == 0.0f ? 1.0f : exact_expf(d, tab);
-            }
+            d[c] = x[c] > xthr ? d_of(x[c], inv_t, M) : -1.0f;
+            ok[c] = expf_rounded(d[c], tab, e[c]);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            if (!ok[c]) e[c] = exact_expf_table(d[c], tab, e[c]);
+            if (!(x[c] > xthr)) e[c] = 0.0f;
+            else if (d[c] == 0.0f) e[c] = 1.0f;
         }
     }
     if (s == 0.0f) {  // (every lane adds all 128 in order: the same sum everywhere)
