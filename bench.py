@@ -19,9 +19,10 @@ cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of 
            (the first --cpu-rows rows, repeated for about --cpu-seconds on all host threads)
 --impl reference  times that CPU restatement alone (all host threads) on the same workload
 --workload vocab_sharded  config 5 instead: 64 x 151,936 rows whose columns are split over the
-           N ranks; a step is the exchange (NCCL all-gather of the shards + row assembly) and
-           the sampling of every row on every rank; reports latency, the exchange's share and
-           a check of the tokens against an unsharded sample
+           N ranks; a step is the exchange (an NCCL all-to-all of each row's shards to its owner
+           rank + row assembly), the owners' sampling and an all-gather of the results; reports
+           latency, the exchange's share and bytes, and a check of the tokens against an
+           unsharded sample
 --workload configs  one GPU, the other configurations of the benchmark at their sizes: config 1
            (one row: latency of a draw through the drop-in single-row API, and 10,000 draws as
            rows sharing the logits), config 2 (greedy), config 3 (mixed, 109,051 wide), config 4
@@ -203,7 +204,7 @@ def run_reference(args, world, rank):
 
 
 def run_vocab_sharded(args, world, rank, local):
-    """Config 5: columns split over the ranks, one all-gather per step (lrs.sharded)."""
+    """Config 5: columns split over the ranks; each row sampled by its owner rank (lrs.sharded)."""
     import datetime
 
     import torch
@@ -255,7 +256,7 @@ def run_vocab_sharded(args, world, rank, local):
         ex[i][0].record(stream)
         vsamp.exchange(shard)
         ex[i][1].record(stream)
-        vsamp.bs.sample_device(vsamp.full, params, state, tokens, n=V, hist=hist, hist_len=hlen, status=status)
+        vsamp.sample_owned(params, state, tokens, hist=hist, hist_len=hlen, status=status)
     t1.record(stream)
     torch.cuda.synchronize()
     total_ms = t0.elapsed_time(t1)
@@ -271,9 +272,13 @@ def run_vocab_sharded(args, world, rank, local):
             "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {"workload": f"config 5: {rows} x {V} f32 rows, columns split over {world} GPU(s) "
-                                   f"({V // world} each), one all-gather per step, top_k 50, top_p 0.95, temp 0.7",
-                       "parallelism": f"vocabulary over {world} GPU(s)"},
+                                   f"({V // world} each), top_k 50, top_p 0.95, temp 0.7",
+                       "parallelism": f"vocabulary over {world} GPU(s); row r sampled by the rank owning its "
+                                      f"row block: one all-to-all of the shards to the owners, one all-gather "
+                                      f"of the results"},
             "exchange_ms_per_step": exch_ms / args.steps, "exchange_share": exch_ms / total_ms,
+            "exchange_bytes_per_rank": vsamp.exchange_bytes(),
+            "all_gather_bytes_per_rank": (world - 1) * rows * (V // world) * 4,
             "tokens_match_unsharded": ok,
             "gpu_launches": (1 + STAGE_LAUNCHES) * args.steps,  # the row assembly, then the sampler
         }

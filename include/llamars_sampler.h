@@ -148,6 +148,13 @@ int  lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint3
  * LRS_E_TIMEOUT or LRS_E_INTERNAL; LRS_E_CUDA if the wait itself failed.          */
 int  lrs_poll_error(lrs_ctx* ctx);
 
+/* Test of the bounded waits (no counterpart in the reference): enqueues one block that
+ * waits `bound_cycles` SM cycles for an mbarrier phase that nothing completes, with the
+ * wait primitive every wait of the sampling kernel uses.  The wait runs out and sets the
+ * context's sticky error word to LRS_E_TIMEOUT, which the next call or lrs_poll_error
+ * returns; the context stays usable.  Returns LRS_OK once enqueued.                  */
+int  lrs_test_wait_timeout(lrs_ctx* ctx, uint32_t bound_cycles, void* stream);
+
 /* ---- batched sampling without allocation ----------------------------------------
  * No counterpart in the reference (rust-llama has no GPU path); an addition for callers
  * that cannot let a library allocate device memory, e.g. a server whose GPU memory is

@@ -439,6 +439,23 @@ int lrs_sample_device(lrs_ctx* ctx, const float* d_logits, uint32_t rows, uint32
     return LRS_OK;
 }
 
+int lrs_test_wait_timeout(lrs_ctx* ctx, uint32_t bound_cycles, void* stream) {
+    if (!ctx) return set_err(nullptr, LRS_E_INVALID, "lrs_test_wait_timeout: ctx is NULL");
+    if (bound_cycles == 0) return set_err(ctx, LRS_E_INVALID, "lrs_test_wait_timeout: bound is 0");
+    CK(cudaSetDevice(ctx->device));
+    {
+        const int perr = take_pending_error(ctx, false);
+        if (perr != LRS_OK) return perr;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    CK(lrs_wait_probe_launch(ctx->d_err, (long long)bound_cycles, s));
+    // the error word after this launch, read back as after a sampling launch
+    CK(cudaMemcpyAsync(ctx->h_err, ctx->d_err, sizeof(int32_t), cudaMemcpyDeviceToHost, s));
+    CK(cudaEventRecord(ctx->err_ev, s));
+    ctx->err_pending = true;
+    return LRS_OK;
+}
+
 int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t rows, uint32_t n, uint64_t ld,
                const uint32_t* hist, uint64_t hist_ld, const uint32_t* hist_len, uint32_t* out_tokens,
                float* out_probs) {

@@ -206,17 +206,34 @@ __device__ __forceinline__ uint32_t row_class(const lrs_params& P, uint32_t n) {
 // Bounded wait on an mbarrier phase.  On timeout the CTA's abort flag and the sticky
 // error word are set; every later wait then returns false at once, so all warps run
 // their (bounded) loops to the end and leave.
-__device__ __forceinline__ bool wait_bar(RowShared& sh, uint64_t* bar, uint32_t parity, int32_t* err) {
+__device__ __forceinline__ bool wait_bar_bounded(volatile uint32_t* abort, uint64_t* bar, uint32_t parity,
+                                                 int32_t* err, long long bound) {
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (sh.abort) return false;
-        if (clock64() - t0 > kWaitCycles) {
-            sh.abort = 1u;
+        if (*abort) return false;
+        if (clock64() - t0 > bound) {
+            *abort = 1u;
             atomicExch(err, LRS_E_TIMEOUT);
             return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool wait_bar(RowShared& sh, uint64_t* bar, uint32_t parity, int32_t* err) {
+    return wait_bar_bounded(&sh.abort, bar, parity, err, kWaitCycles);
+}
+
+// Test of the bounded wait: one thread waits for the first phase of an mbarrier that
+// nothing arrives on, with a bound of `bound` cycles; the wait runs out, sets the error
+// word to LRS_E_TIMEOUT and returns (no copy is in flight, no other thread waits).
+__global__ void lrs_wait_probe(int32_t* err, long long bound) {
+    __shared__ uint64_t bar;
+    __shared__ volatile uint32_t abort;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        abort = 0u;
+        (void)wait_bar_bounded(&abort, &bar, 0u, err, bound);
+    }
 }
 
 // Bounded wait until load q of the ring has landed.  A parity wait only distinguishes
@@ -3099,4 +3116,9 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     fb.order = S.fb_rows;
     fb.claim_count = S.fb_count;
     return lrs_kernel_launch(&fb, fallback_grid, smem, s);
+}
+
+cudaError_t lrs_wait_probe_launch(int32_t* err, long long bound, cudaStream_t s) {
+    lrs::lrs_wait_probe<<<1, 32, 0, s>>>(err, bound);
+    return cudaGetLastError();
 }

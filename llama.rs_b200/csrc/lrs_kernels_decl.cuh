@@ -84,3 +84,6 @@ void lrs_kernel_scratch_layout(uint32_t n, uint64_t* stride, uint64_t* bitmap_of
 cudaError_t lrs_kernel_set_smem(size_t bytes);
 cudaError_t lrs_kernel_occupancy(int* ctas_per_sm, size_t smem);
 cudaError_t lrs_kernel_launch(const lrs_kernel_args_t* args, uint32_t grid, size_t smem, cudaStream_t s);
+// Test of the bounded wait (lrs_test_wait_timeout): a wait of `bound` cycles on a barrier
+// nothing completes, which sets *err to LRS_E_TIMEOUT.
+cudaError_t lrs_wait_probe_launch(int32_t* err, long long bound, cudaStream_t s);

@@ -44,7 +44,7 @@ EXPORTS = [
     "lrs_create", "lrs_destroy", "lrs_last_error", "lrs_seed_state", "lrs_set_state", "lrs_get_state",
     "lrs_set_params", "lrs_sample", "lrs_sample_device", "lrs_sampler_new", "lrs_sampler_free",
     "lrs_sampler_state", "lrs_sampler_sample", "lrs_sample_device_noalloc", "lrs_assemble_shards",
-    "lrs_poll_error", "lrs_noalloc_poll_error",
+    "lrs_poll_error", "lrs_noalloc_poll_error", "lrs_test_wait_timeout",
 ]
 
 
@@ -90,6 +90,8 @@ def lib() -> ctypes.CDLL:
         L.lrs_poll_error.restype = I
         L.lrs_noalloc_poll_error.argtypes = [I, P]
         L.lrs_noalloc_poll_error.restype = I
+        L.lrs_test_wait_timeout.argtypes = [P, ctypes.c_uint32, P]
+        L.lrs_test_wait_timeout.restype = I
         L.lrs_assemble_shards.argtypes = [P, U32, U32, U32, P, U64, P]
         L.lrs_assemble_shards.restype = I
         L.lrs_sampler_new.argtypes = [U64, I]
@@ -233,6 +235,11 @@ class BatchSampler:
     def poll_error(self):
         """Waits for the last launch and raises the error it reported (lrs_poll_error)."""
         _check(lib().lrs_poll_error(self._h), self._h)
+
+    def test_wait_timeout(self, bound_cycles: int, stream=None):
+        """Enqueues the test of the bounded wait (lrs_test_wait_timeout): its wait runs out and
+        the next call, or poll_error, reports LRS_E_TIMEOUT."""
+        _check(lib().lrs_test_wait_timeout(self._h, bound_cycles, stream), self._h)
 
     def close(self):
         if getattr(self, "_h", None):
