@@ -566,12 +566,21 @@ int lrs_sample(lrs_ctx* ctx, const float* logits, int logits_on_device, uint32_t
 }
 
 // ------------------------------------------------------------ single-row drop-in ----
+// One synchronous round trip a draw: the row's state, parameters and history go up in one
+// copy from a pinned block (with the logits), the sampling launch reads them in place, and
+// the token, status and advanced state come back in one copy of the block's head.
+namespace {
+constexpr size_t kOneState = 0, kOneParams = 8, kOneHistLen = 32, kOneToken = 36, kOneStatus = 40, kOneHist = 48;
+static_assert(kOneParams + sizeof(lrs_params) <= kOneHistLen, "single-row block layout");
+}  // namespace
+
 struct lrs_sampler {
     uint64_t state;
     int device;
     lrs_ctx* ctx;
-    lrs_params last;
-    bool have_last;
+    unsigned char* h_blk;  // pinned: the block's host copy
+    unsigned char* d_blk;  // the block on the device
+    size_t blk_cap;        // bytes of both
 };
 
 lrs_sampler* lrs_sampler_new(uint64_t seed, int device) {
@@ -579,13 +588,20 @@ lrs_sampler* lrs_sampler_new(uint64_t seed, int device) {
     s->state = seed | 1ull;  // Sampler::new (sampler.rs:33-37)
     s->device = device;
     s->ctx = nullptr;
-    s->have_last = false;
+    s->h_blk = nullptr;
+    s->d_blk = nullptr;
+    s->blk_cap = 0;
     return s;
 }
 
 void lrs_sampler_free(lrs_sampler* s) {
     if (!s) return;
-    if (s->ctx) lrs_destroy(s->ctx);
+    if (s->ctx) {
+        cudaSetDevice(s->ctx->device);
+        if (s->d_blk) cudaFree(s->d_blk);
+        if (s->h_blk) cudaFreeHost(s->h_blk);
+        lrs_destroy(s->ctx);
+    }
     delete s;
 }
 
@@ -596,13 +612,22 @@ uint32_t lrs_sampler_sample(lrs_sampler* s, const float* logits, size_t n, const
     int dummy;
     if (!status) status = &dummy;
     *status = LRS_OK;
-    if (!s || !params || (!logits && n) || (!recent && recent_len) || n > (1u << 22) || recent_len > 0xFFFFFFFFu) {
+    if (!s || !params || (!logits && n) || (!recent && recent_len) || n > (1u << 22) || recent_len > 0xFFFFFFFFu ||
+        params->reserved != 0) {
         *status = LRS_E_INVALID;
         return LRS_TOKEN_NONE;
     }
     if (n == 0) return 0;  // sampler.rs:57-60
     if (!s->ctx || s->ctx->max_vocab < n || s->ctx->max_hist < recent_len) {
-        if (s->ctx) lrs_destroy(s->ctx);
+        if (s->ctx) {
+            cudaSetDevice(s->ctx->device);
+            if (s->d_blk) cudaFree(s->d_blk);
+            if (s->h_blk) cudaFreeHost(s->h_blk);
+            s->d_blk = nullptr;
+            s->h_blk = nullptr;
+            s->blk_cap = 0;
+            lrs_destroy(s->ctx);
+        }
         s->ctx = nullptr;
         uint32_t hcap = 64;
         while (hcap < recent_len) hcap *= 2;
@@ -611,30 +636,70 @@ uint32_t lrs_sampler_sample(lrs_sampler* s, const float* logits, size_t n, const
             *status = rc;
             return LRS_TOKEN_NONE;
         }
-        s->have_last = false;
     }
-    int rc;
-    if (!s->have_last || memcmp(&s->last, params, sizeof(lrs_params)) != 0) {
-        rc = lrs_set_params(s->ctx, params, 1);
-        if (rc != LRS_OK) {
-            *status = rc;
-            return LRS_TOKEN_NONE;
-        }
-        s->last = *params;
-        s->have_last = true;
+    lrs_ctx* ctx = s->ctx;
+    const size_t need = kOneHist + (size_t)ctx->max_hist * sizeof(uint32_t);
+    auto fail = [&](int rc) -> uint32_t {
+        *status = rc;
+        return LRS_TOKEN_NONE;
+    };
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return fail(set_err(ctx, LRS_E_CUDA, "cudaSetDevice failed"));
+    if (s->blk_cap < need) {
+        if (s->d_blk) cudaFree(s->d_blk);
+        if (s->h_blk) cudaFreeHost(s->h_blk);
+        s->d_blk = nullptr;
+        s->h_blk = nullptr;
+        s->blk_cap = 0;
+        if (cudaMalloc(&s->d_blk, need) != cudaSuccess || cudaMallocHost(&s->h_blk, need) != cudaSuccess)
+            return fail(set_err(ctx, LRS_E_NOMEM, "lrs_sampler_sample: staging allocation failed"));
+        s->blk_cap = need;
     }
-    rc = lrs_set_state(s->ctx, &s->state, 1);
-    if (rc == LRS_OK) {
-        uint32_t hl = (uint32_t)recent_len;
-        uint32_t tok = LRS_TOKEN_NONE;
-        rc = lrs_sample(s->ctx, logits, 0, 1, (uint32_t)n, n, recent, recent_len, &hl, &tok, nullptr);
-        if (rc == LRS_OK) {
-            rc = lrs_get_state(s->ctx, &s->state, 1);
-            if (rc == LRS_OK) return tok;
-        }
+    const uint32_t hl = (uint32_t)recent_len;
+    memcpy(s->h_blk + kOneState, &s->state, sizeof(uint64_t));
+    memcpy(s->h_blk + kOneParams, params, sizeof(lrs_params));
+    memcpy(s->h_blk + kOneHistLen, &hl, sizeof(uint32_t));
+    if (hl) memcpy(s->h_blk + kOneHist, recent, (size_t)hl * sizeof(uint32_t));
+    cudaStream_t st = ctx->stream;
+    // the logits: from caller memory that is pinned, else through the context's pinned staging
+    cudaPointerAttributes pa;
+    const bool pinned = cudaPointerGetAttributes(&pa, logits) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+    cudaGetLastError();
+    if (!ctx->d_logits && cudaMalloc(&ctx->d_logits, (size_t)ctx->max_rows * ctx->max_vocab * sizeof(float)) != cudaSuccess)
+        return fail(set_err(ctx, LRS_E_NOMEM, "lrs_sampler_sample: logits allocation failed"));
+    const float* src = logits;
+    if (!pinned) {
+        if (!ctx->h_logits &&
+            cudaMallocHost(&ctx->h_logits, (size_t)ctx->max_rows * ctx->max_vocab * sizeof(float)) != cudaSuccess)
+            return fail(set_err(ctx, LRS_E_NOMEM, "lrs_sampler_sample: staging allocation failed"));
+        memcpy(ctx->h_logits, logits, n * sizeof(float));
+        src = ctx->h_logits;
     }
-    *status = rc;
-    return LRS_TOKEN_NONE;
+    if (cudaMemcpyAsync(ctx->d_logits, src, n * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+        cudaMemcpyAsync(s->d_blk, s->h_blk, kOneHist + (size_t)hl * sizeof(uint32_t), cudaMemcpyHostToDevice, st) !=
+            cudaSuccess)
+        return fail(set_err(ctx, LRS_E_CUDA, "lrs_sampler_sample: copy failed"));
+    int rc = lrs_sample_device(ctx, ctx->d_logits, 1, (uint32_t)n, n,
+                               hl ? reinterpret_cast<const uint32_t*>(s->d_blk + kOneHist) : nullptr, hl,
+                               hl ? reinterpret_cast<const uint32_t*>(s->d_blk + kOneHistLen) : nullptr,
+                               reinterpret_cast<const lrs_params*>(s->d_blk + kOneParams),
+                               reinterpret_cast<uint64_t*>(s->d_blk + kOneState),
+                               reinterpret_cast<uint32_t*>(s->d_blk + kOneToken), nullptr,
+                               reinterpret_cast<int32_t*>(s->d_blk + kOneStatus), nullptr, st);
+    if (rc != LRS_OK) return fail(rc);
+    if (cudaMemcpyAsync(s->h_blk, s->d_blk, kOneHist, cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return fail(set_err(ctx, LRS_E_CUDA, "lrs_sampler_sample: copy back failed"));
+    rc = take_pending_error(ctx, true);  // (the launch's error word has landed with the stream)
+    if (rc != LRS_OK) return fail(rc);
+    int32_t row_status;
+    uint32_t tok;
+    memcpy(&row_status, s->h_blk + kOneStatus, sizeof(int32_t));
+    memcpy(&tok, s->h_blk + kOneToken, sizeof(uint32_t));
+    if (row_status != LRS_OK)
+        return fail(set_err(ctx, row_status, "lrs_sampler_sample: status %d (NaN probabilities: the reference "
+                                             "sampler would panic)", row_status));
+    memcpy(&s->state, s->h_blk + kOneState, sizeof(uint64_t));
+    return tok;
 }
 
 }  // extern "C"

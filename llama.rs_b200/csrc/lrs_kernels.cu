@@ -3066,6 +3066,7 @@ void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L) {
     L->list_n = take(R * sizeof(uint32_t));
     L->fb_rows = take(R * sizeof(uint32_t));
     L->fb_count = take(sizeof(uint32_t));
+    L->live_count = take(sizeof(uint32_t));
     L->bytes = off;
 }
 
@@ -3101,8 +3102,10 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     S.list_n = reinterpret_cast<uint32_t*>(base + L->list_n);
     S.fb_rows = reinterpret_cast<uint32_t*>(base + L->fb_rows);
     S.fb_count = reinterpret_cast<uint32_t*>(base + L->fb_count);
+    S.live_count = reinterpret_cast<uint32_t*>(base + L->live_count);
     cudaError_t e = cudaMemsetAsync(S.list_n, 0, (size_t)rows * sizeof(uint32_t), s);
     if (e == cudaSuccess) e = cudaMemsetAsync(S.fb_count, 0, sizeof(uint32_t), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(S.live_count, 0, sizeof(uint32_t), s);
     if (e == cudaSuccess) e = cudaMemsetAsync(args->row_counter, 0, kLrsRowCounters * sizeof(uint32_t), s);
     if (e != cudaSuccess) return e;
     lrs_stage_stats<<<warps_grid[0], kStageThreads, 0, s>>>(S);

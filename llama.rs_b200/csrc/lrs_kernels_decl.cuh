@@ -45,7 +45,7 @@ struct lrs_kernel_args_t {
 // `vocab` entries: byte offsets into one device buffer of `bytes` bytes (256-byte aligned).
 struct lrs_stage_layout_t {
     uint32_t rows, nt;        // rows and tile slots per row
-    uint64_t tstat, lmax, tprep, tres, rprep, lists, list_n, fb_rows, fb_count, bytes;
+    uint64_t tstat, lmax, tprep, tres, rprep, lists, list_n, fb_rows, fb_count, live_count, bytes;
 };
 void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L);
 // The staged pipeline on args->rows rows, then lrs_sample_rows on the rows it leaves

@@ -94,6 +94,7 @@ struct StageArgs {
     uint32_t* list_n;       // [rows] entries appended (may exceed the capacity: overflow)
     uint32_t* fb_rows;      // rows left to lrs_sample_rows
     uint32_t* fb_count;
+    uint32_t* live_count;   // rows prep leaves to classify (0: classify and sum have nothing to do)
 };
 
 __device__ __forceinline__ void stage_fallback(const StageArgs& S, uint32_t r) {
@@ -508,6 +509,16 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
     for (int w = 0; w < warp; ++w) before += ps.wsum[w];
     double s_total = ps.bd[0] + ps.bd[1];
     for (int w = 0; w < kStageWarps; ++w) s_total += ps.wsum[w];
+    if (!pathK && topp_on && k > kStageListCap) {
+        // Every probability is at most 1/S (the max's exp is 1), so the nucleus holds at least
+        // top_p S elements, S above s_total (1 - delta) (the bound of the tile estimates over
+        // the whole row): a nucleus that cannot fit in the list goes to lrs_sample_rows now.
+        const double delta = (double)n * 0x1p-23 + 0x1p-13;
+        if ((double)P.top_p * s_total * (1.0 - delta) > 1.01 * (double)kStageListCap) {
+            leave(kRowFallback);
+            return;
+        }
+    }
     TilePrep tp{0, 0u, 0.0f, 0.0f};
     int umin = 0x7FFFFFFF, umax = -0x7FFFFFFF;
     if (tin) {
@@ -632,6 +643,7 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         const long long dt = clock64() - t_start;
         rp.cyc_prep = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
         S.rprep[r] = rp;
+        atomicAdd(S.live_count, 1u);
     }
 }
 
@@ -701,6 +713,7 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
     uint8_t* wqb = qb + warp * 1024;
     uint32_t* bc = bcount + warp * 16;
     const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
+    if (*(volatile const uint32_t*)S.live_count == 0u) return;  // (every row finished in prep or left)
     const uint64_t tasks = (uint64_t)a.rows * S.nt;
     const uint64_t stride = (uint64_t)gridDim.x * kClassifyWarps;
     uint64_t task = (uint64_t)blockIdx.x * kClassifyWarps + warp;
@@ -1017,7 +1030,7 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
     const lrs_kernel_args_t& a = S.a;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t r = blockIdx.x * kSumWarps + warp;
-    if (r >= a.rows) return;
+    if (r >= a.rows || *(volatile const uint32_t*)S.live_count == 0u) return;
     RowPrep* rpp = S.rprep + r;
     const uint32_t flags = rpp->flags;
     if (flags & (kRowDone | kRowFallback)) return;
