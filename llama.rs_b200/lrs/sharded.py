@@ -13,8 +13,11 @@ over NVLink / NVSwitch on GPUs, gloo on CPUs) that sends each rank's columns of 
 the row's owner only, so a rank receives (G - 1) / G of its own rows instead of every
 rank's columns of every row; lrs_assemble_shards lays the owner's rows out and
 lrs_sample_device samples them; one all-gather then gives every rank every row's token,
-state and status.  Each collective has a deadline: one that does not complete in time
-raises SamplerError with LRS_E_TIMEOUT (a peer lost another way: LRS_E_NCCL).
+state and status.  Deadlines: on host buffers (gloo) each collective is waited for with a
+deadline, and one that does not complete in time raises SamplerError with LRS_E_TIMEOUT (a
+peer lost another way: LRS_E_NCCL); on GPUs the collectives stay stream-ordered (a host wait
+would stall the launches behind them) and the process group's timeout, enforced by NCCL's
+watchdog, bounds them.
 """
 from __future__ import annotations
 
@@ -107,8 +110,7 @@ class VocabShardedSampler:
     """Config 5 on GPUs: sample rows whose columns are spread over the ranks of `group`; row r is
     sampled by the rank whose `row_block` holds it."""
 
-    def __init__(self, rows: int, vocab: int, max_hist: int = 64, group=None, device: int = 0,
-                 deadline_s: float = 30.0):
+    def __init__(self, rows: int, vocab: int, max_hist: int = 64, group=None, device: int = 0):
         import torch
         import torch.distributed as dist
 
@@ -117,7 +119,6 @@ class VocabShardedSampler:
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
         self.rows, self.vocab = rows, vocab
-        self.deadline_s = deadline_s
         self.shard_n = vocab // self.world
         if self.shard_n * self.world != vocab:
             raise ValueError(f"vocab {vocab} does not split over {self.world} ranks")
@@ -152,7 +153,7 @@ class VocabShardedSampler:
             work = dist.all_to_all_single(self.recv, flat, output_split_sizes=[mine * self.shard_n] * self.world,
                                           input_split_sizes=[len(b) * self.shard_n for b in self.blocks],
                                           group=self.group, async_op=True)
-            _wait(work, self.deadline_s, "config-5 exchange")
+            work.wait()  # (stream-ordered: the process group's timeout bounds it)
         else:
             self.recv.copy_(flat)
         if stream is None:
@@ -188,7 +189,7 @@ class VocabShardedSampler:
         if self.world > 1:
             work = dist.all_gather_into_tensor(self.res.view(-1), self.res[self.rank].contiguous().view(-1),
                                                group=self.group, async_op=True)
-            _wait(work, self.deadline_s, "config-5 results")
+            work.wait()
         for h, b in enumerate(self.blocks):
             n = len(b)
             if n == 0:
