@@ -3103,11 +3103,8 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     S.fb_rows = reinterpret_cast<uint32_t*>(base + L->fb_rows);
     S.fb_count = reinterpret_cast<uint32_t*>(base + L->fb_count);
     S.live_count = reinterpret_cast<uint32_t*>(base + L->live_count);
-    cudaError_t e = cudaMemsetAsync(S.list_n, 0, (size_t)rows * sizeof(uint32_t), s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(S.fb_count, 0, sizeof(uint32_t), s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(S.live_count, 0, sizeof(uint32_t), s);
-    if (e == cudaSuccess) e = cudaMemsetAsync(args->row_counter, 0, kLrsRowCounters * sizeof(uint32_t), s);
-    if (e != cudaSuccess) return e;
+    // (the stats stage zeroes the step's counters and the lists' lengths)
+    cudaError_t e;
     lrs_stage_stats<<<warps_grid[0], kStageThreads, 0, s>>>(S);
     lrs_stage_prep<<<rows, kStageThreads, 0, s>>>(S);
     lrs_stage_classify<<<warps_grid[1], kClassifyWarps * 32, 0, s>>>(S);

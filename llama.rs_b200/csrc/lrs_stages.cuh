@@ -166,8 +166,15 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_stats(const StageArgs
     const float kInf = __int_as_float(0x7F800000);
     const uint64_t tasks = (uint64_t)a.rows * S.nt;
     const uint64_t stride = (uint64_t)gridDim.x * kStageWarps;
+    // the step's counters start from zero (the later stages read them in stream order)
+    if (blockIdx.x == 0 && threadIdx.x < kLrsRowCounters) a.row_counter[threadIdx.x] = 0u;
+    if (blockIdx.x == 0 && threadIdx.x == 0) {
+        *S.fb_count = 0u;
+        *S.live_count = 0u;
+    }
     for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
         const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
+        if (t == 0 && lane == 0) S.list_n[r] = 0u;
         const Geo g = row_geometry(a, r);
         if (t >= g.nchunks) continue;
         const lrs_params P = a.params[r];
@@ -1328,10 +1335,26 @@ __device__ __noinline__ uint32_t regather_nucleus(const StageArgs& S, uint32_t r
     const uint32_t nkeys = sh.misc[1];
     if (nkeys > kStageListCap) return 0xFFFFFFFFu;
     // the keys (p desc, index asc) from the gathered d values, p = fl(libm expf(d) * inv)
-    for (uint32_t i = tid; i < nkeys; i += kThreads) {
-        const unsigned long long k = keys[i];
-        const float p = __fmul_rn(exact_expf(__uint_as_float((uint32_t)(k >> 32)), tab), inv);
-        keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | (k & 0xFFFFFFFFull);
+    // (four a thread side by side)
+    for (uint32_t i0 = tid; i0 < nkeys; i0 += 4u * kThreads) {
+        unsigned long long k[4];
+        float ev[4];
+        bool ok[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t i = i0 + (uint32_t)u * kThreads;
+            k[u] = i < nkeys ? keys[i] : 0ull;
+            ok[u] = expf_rounded(__uint_as_float((uint32_t)(k[u] >> 32)), tab, ev[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint32_t i = i0 + (uint32_t)u * kThreads;
+            if (i < nkeys) {
+                const float d = __uint_as_float((uint32_t)(k[u] >> 32));
+                const float e = ok[u] ? ev[u] : exact_expf_table(d, tab, ev[u]);
+                keys[i] = ((unsigned long long)(~__float_as_uint(__fmul_rn(e, inv))) << 32) | (k[u] & 0xFFFFFFFFull);
+            }
+        }
     }
     csync();
     return nkeys;
@@ -1723,10 +1746,27 @@ __global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CT
     for (int attempt = nk > kStageListCap ? 1 : 0; attempt < 3; ++attempt) {
         if (attempt == 0) {
             const uint2* lst = S.lists + (uint64_t)r * kStageListCap;
-            for (uint32_t i = tid; i < nk; i += kThreads) {
-                const uint2 e = lst[i];
-                const float p = __fmul_rn(exact_expf(__fsub_rn(__uint_as_float(e.x), M), exptab), inv);
-                keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | e.y;
+            // (four entries a thread side by side: the exps' chains overlap)
+            for (uint32_t i0 = tid; i0 < nk; i0 += 4u * kThreads) {
+                uint2 en[4];
+                float d[4], ev[4];
+                bool ok[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t i = i0 + (uint32_t)u * kThreads;
+                    en[u] = i < nk ? lst[i] : make_uint2(__float_as_uint(M), 0u);
+                    d[u] = __fsub_rn(__uint_as_float(en[u].x), M);
+                    ok[u] = expf_rounded(d[u], exptab, ev[u]);
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const uint32_t i = i0 + (uint32_t)u * kThreads;
+                    if (i < nk) {
+                        const float e = ok[u] ? ev[u] : exact_expf_table(d[u], exptab, ev[u]);
+                        const float p = __fmul_rn(e, inv);
+                        keys[i] = ((unsigned long long)(~__float_as_uint(p)) << 32) | en[u].y;
+                    }
+                }
             }
         } else {
             // The nucleus reaches deeper than the list: gather it from the row down to a bucket
