@@ -30,3 +30,19 @@ def test_cuda_expf_relative_error_below_the_classification_bound(tmp_path):
     worst = float(err.max())
     assert worst > 0.0                       # the probe ran
     assert worst < 2.0 ** -21 / 2            # the classification's 2^-21, with a factor 2 to spare
+
+
+def test_branch_free_double_exp_against_cuda_double_exp(tmp_path):
+    # lrs::exp_neg (Cody-Waite reduction, Taylor degree 12) stands in for the double exp of the
+    # correctly rounded float exp: within 1e-14 relative of CUDA's double exp over every float
+    # d in [-104, 0), and never rounding to another float where the midpoint test trusts it.
+    lib = tmp_path / "exp_neg_bound.so"
+    subprocess.run([B.nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "-shared",
+                    "-Xcompiler", "-fPIC", os.path.join(HERE, "csrc", "exp_neg_bound.cu"), "-o", str(lib)],
+                   check=True)
+    out = np.zeros(2, np.uint32)
+    rc = ctypes.CDLL(str(lib)).lrs_test_exp_neg(out.ctypes.data_as(ctypes.c_void_p))
+    assert rc == 0
+    worst = float(out[:1].view(np.float32)[0])
+    assert 0.0 < worst < 1e-14
+    assert out[1] == 0
