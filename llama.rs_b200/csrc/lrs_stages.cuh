@@ -575,7 +575,38 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         // above it, so it bounds the row's k-th largest scaled logit from below); less the
         // tie margin (generous for both the bound and the final k-th value), every element
         // whose probability can reach the k-th probability lies above it.
-        const float th = block_select_desc(ps.vals, nv, k, ps);
+        float th;
+        if (k <= ntile && nv + 32u + ntile <= kStageMaxTiles * 32u + 32u) {
+            // A tile's max is one of its lane maxima, so the k-th largest of the tile maxima and
+            // the edge elements bounds the k-th largest of all from below: select it among
+            // those, keep the values at or above it (in the free end of ps.vals), select there.
+            float* tv = ps.vals + nv;  // (tile maxima, then the edge elements)
+            for (uint32_t t2 = (uint32_t)tid; t2 < ntile; t2 += kStageThreads)
+                tv[t2] = S.tstat[(uint64_t)r * S.nt + t2].x;
+            if (warp == 0) tv[ntile + lane] = ps.vals[nl + lane];
+            __syncthreads();
+            const float th0 = block_select_desc(tv, ntile + 32u, k, ps);
+            if (tid == 0) ps.bc[2] = 0u;
+            __syncthreads();
+            float* kept = ps.vals + nv;  // (the tile maxima are done with)
+            for (uint32_t i0 = 0; i0 < nv; i0 += kStageThreads) {
+                const uint32_t i = i0 + (uint32_t)tid;
+                const float x = i < nv ? ps.vals[i] : -kInf;
+                const bool keep = i < nv && x >= th0;
+                const unsigned m = __ballot_sync(0xFFFFFFFFu, keep);
+                uint32_t o = 0;
+                if (lane == 0 && m) o = atomicAdd(&ps.bc[2], (uint32_t)__popc(m));
+                o = __shfl_sync(0xFFFFFFFFu, o, 0) + (uint32_t)__popc(m & ((1u << lane) - 1u));
+                if (keep && o < kStageMaxTiles * 32u + 32u - nv) kept[o] = x;
+            }
+            __syncthreads();
+            const uint32_t nk = ps.bc[2];
+            __syncthreads();
+            th = nk <= kStageMaxTiles * 32u + 32u - nv ? block_select_desc(kept, nk, k, ps)
+                                                       : block_select_desc(ps.vals, nv, k, ps);
+        } else {
+            th = block_select_desc(ps.vals, nv, k, ps);
+        }
         float cand = -kInf;
         if (th > -kInf) cand = __fsub_rn(th, __fmul_rn(__fadd_rn(__fadd_rn(fabsf(th), fabsf(M)), 1.0f), 0x1p-17f));
         rp.flags = kRowPathK;
