@@ -89,7 +89,10 @@ typedef struct lrs_row_info {
                             top-k/top-p/draw, 7 sorting within 3; rows finished by the staged
                             pipeline: 4 is 1, 0-2 the cycles of its prep, sum and finish stages,
                             3, 6 and 7 those of the finish's regather, sorts and sequential runs,
-                            5 the blocks its sum walked (implementation detail) */
+                            5 the blocks its sum walked; rows of a nucleus larger than a list
+                            (sampled by the big-nucleus stage, n_cand the keys it bucketed): 2 its
+                            cycles, 3 those of counting and scattering the keys, 6 of the two
+                            walks and 7 of the sorts within them (implementation detail) */
     uint32_t reserved;
 } lrs_row_info;
 

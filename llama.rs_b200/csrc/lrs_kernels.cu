@@ -3067,6 +3067,9 @@ void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L) {
     L->fb_rows = take(R * sizeof(uint32_t));
     L->fb_count = take(sizeof(uint32_t));
     L->live_count = take(sizeof(uint32_t));
+    L->big_rows = take(R * sizeof(uint32_t));
+    L->big_count = take(sizeof(uint32_t));
+    L->big_claim = take(sizeof(uint32_t));
     L->bytes = off;
 }
 
@@ -3084,6 +3087,8 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
         if (e == cudaSuccess)
             e = cudaFuncSetAttribute(lrs_stage_finish, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)kStageFinishSmem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(lrs_stage_big, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBigSmem);
         if (e != cudaSuccess) return e;
         warps_grid[0] = sms * (occ0 > 0 ? occ0 : 1);
         warps_grid[1] = sms * (occ1 > 0 ? occ1 : 1);
@@ -3103,6 +3108,10 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     S.fb_rows = reinterpret_cast<uint32_t*>(base + L->fb_rows);
     S.fb_count = reinterpret_cast<uint32_t*>(base + L->fb_count);
     S.live_count = reinterpret_cast<uint32_t*>(base + L->live_count);
+    const bool big = args->scratch != nullptr && fallback_grid > 0u;  // (lrs_stage_big's scratch)
+    S.big_rows = big ? reinterpret_cast<uint32_t*>(base + L->big_rows) : nullptr;
+    S.big_count = reinterpret_cast<uint32_t*>(base + L->big_count);
+    S.big_claim = reinterpret_cast<uint32_t*>(base + L->big_claim);
     // (the stats stage zeroes the step's counters and the lists' lengths)
     cudaError_t e;
     lrs_stage_stats<<<warps_grid[0], kStageThreads, 0, s>>>(S);
@@ -3110,6 +3119,7 @@ cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs
     lrs_stage_classify<<<warps_grid[1], kClassifyWarps * 32, 0, s>>>(S);
     lrs_stage_sum<<<(rows + kSumWarps - 1) / kSumWarps, kSumWarps * 32, 0, s>>>(S);
     lrs_stage_finish<<<rows, kThreads, kStageFinishSmem, s>>>(S);
+    if (big) lrs_stage_big<<<fallback_grid, kThreads, kBigSmem, s>>>(S);
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
     // the rows the stages left: lrs_sample_rows on the list, in list order
     lrs_kernel_args_t fb = *args;

@@ -45,11 +45,15 @@ struct lrs_kernel_args_t {
 // `vocab` entries: byte offsets into one device buffer of `bytes` bytes (256-byte aligned).
 struct lrs_stage_layout_t {
     uint32_t rows, nt;        // rows and tile slots per row
-    uint64_t tstat, lmax, tprep, tres, rprep, lists, list_n, fb_rows, fb_count, live_count, bytes;
+    uint64_t tstat, lmax, tprep, tres, rprep, lists, list_n, fb_rows, fb_count, live_count, big_rows, big_count,
+        big_claim, bytes;
 };
 void lrs_stage_layout(uint32_t rows, uint32_t vocab, lrs_stage_layout_t* L);
 // The staged pipeline on args->rows rows, then lrs_sample_rows on the rows it leaves
-// (fallback_grid CTAs with `smem` bytes; args->row_counter is zeroed here).
+// (fallback_grid CTAs with `smem` bytes; args->row_counter is zeroed here).  Top-p rows whose
+// nucleus is larger than a list are sampled by lrs_stage_big on fallback_grid CTAs, each in
+// the first n words of its lrs_sample_rows scratch (args->scratch, at most fallback_grid
+// CTAs' worth).
 cudaError_t lrs_stage_launch(const lrs_kernel_args_t* args, void* mem, const lrs_stage_layout_t* L,
                              uint32_t fallback_grid, size_t smem, cudaStream_t s);
 

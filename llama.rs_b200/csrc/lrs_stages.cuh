@@ -47,6 +47,7 @@ constexpr uint32_t kRowDone = 1u;        // outputs written by the prep (greedy,
 constexpr uint32_t kRowFallback = 2u;    // sampled by lrs_sample_rows afterwards
 constexpr uint32_t kRowPathK = 4u;       // top-k list (k <= kKMax)
 constexpr uint32_t kRowPathN = 8u;       // top-p nucleus list
+constexpr uint32_t kRowBig = 16u;        // top-p nucleus deeper than a list: lrs_stage_big
 // flags of a tile's prep / result records
 constexpr uint32_t kTileWalk = 1u;       // prep: the estimate allows more than two grids
 constexpr uint32_t kTileOne = 2u;        // prep: the estimate allows grid u0 alone
@@ -95,6 +96,9 @@ struct StageArgs {
     uint32_t* fb_rows;      // rows left to lrs_sample_rows
     uint32_t* fb_count;
     uint32_t* live_count;   // rows prep leaves to classify (0: classify and sum have nothing to do)
+    uint32_t* big_rows;     // rows for lrs_stage_big (null: none; such rows go to lrs_sample_rows)
+    uint32_t* big_count;
+    uint32_t* big_claim;    // lrs_stage_big: the next entry of big_rows a CTA takes
 };
 
 __device__ __forceinline__ void stage_fallback(const StageArgs& S, uint32_t r) {
@@ -171,6 +175,10 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_stats(const StageArgs
     if (blockIdx.x == 0 && threadIdx.x == 0) {
         *S.fb_count = 0u;
         *S.live_count = 0u;
+        if (S.big_rows) {
+            *S.big_count = 0u;
+            *S.big_claim = 0u;
+        }
     }
     for (uint64_t task = (uint64_t)blockIdx.x * kStageWarps + warp; task < tasks; task += stride) {
         const uint32_t r = (uint32_t)(task / S.nt), t = (uint32_t)(task % S.nt);
@@ -516,14 +524,18 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
     for (int w = 0; w < warp; ++w) before += ps.wsum[w];
     double s_total = ps.bd[0] + ps.bd[1];
     for (int w = 0; w < kStageWarps; ++w) s_total += ps.wsum[w];
+    bool big = false;
     if (!pathK && topp_on && k > kStageListCap) {
         // Every probability is at most 1/S (the max's exp is 1), so the nucleus holds at least
         // top_p S elements, S above s_total (1 - delta) (the bound of the tile estimates over
         // the whole row): a nucleus that cannot fit in the list goes to lrs_sample_rows now.
         const double delta = (double)n * 0x1p-23 + 0x1p-13;
         if ((double)P.top_p * s_total * (1.0 - delta) > 1.01 * (double)kStageListCap) {
-            leave(kRowFallback);
-            return;
+            if (!S.big_rows || n > kStageMaxTiles * (uint32_t)kTile) {  // (the window bitmap's bound)
+                leave(kRowFallback);
+                return;
+            }
+            big = true;  // (lrs_stage_big samples it once the sum stage has its denominator)
         }
     }
     TilePrep tp{0, 0u, 0.0f, 0.0f};
@@ -612,6 +624,10 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         rp.flags = kRowPathK;
         rp.cand = cand;
         rp.cand_raw = cand > -kInf ? raw_threshold(cand, inv_t, 0.0f) : -kInf;
+    } else if (big) {  // no list: classify and sum only give the denominator
+        rp.flags = kRowPathN | kRowBig;
+        rp.cand = kInf;
+        rp.cand_raw = kInf;
     } else {
         // The nucleus (sampler.rs:135-146) is the head of the sorted probabilities up to mass
         // top_p.  The list takes every element with d >= theta, theta the shallower of two
@@ -682,6 +698,7 @@ __global__ void __launch_bounds__(kStageThreads) lrs_stage_prep(const StageArgs 
         rp.cyc_prep = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
         S.rprep[r] = rp;
         atomicAdd(S.live_count, 1u);
+        if (big) S.big_rows[atomicAdd(S.big_count, 1u)] = r;
     }
 }
 
@@ -1182,6 +1199,17 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
 }
 
 // ----------------------------------------------------------------- finish ----
+// A top-p row whose nucleus the finish cannot hold goes to lrs_stage_big when it can take it,
+// else to lrs_sample_rows.
+__device__ __forceinline__ void stage_big_or_fallback(const StageArgs& S, uint32_t r, uint32_t n) {
+    if (S.big_rows && n <= kStageMaxTiles * (uint32_t)kTile) {
+        S.rprep[r].flags |= kRowBig;
+        S.big_rows[atomicAdd(S.big_count, 1u)] = r;
+    } else {
+        stage_fallback(S, r);
+    }
+}
+
 // A top-p row whose nucleus is deeper than its list (sampler.rs:135-146): the CTA counts the
 // row's elements by d = fl(x' - M) in buckets of 1/4 over d in (-18, 0] and gathers the exact
 // keys (p desc, index asc) of every element above the deepest bucket edge whose elements fit
@@ -1671,10 +1699,10 @@ __device__ __noinline__ uint32_t nucleus_prefilter(unsigned long long* keys, uin
 // emulation (acc_tile).
 // Returns the stop position or -1; every thread gets the same s.
 __device__ __noinline__ int sorted_run(const SortedKeys keys, uint32_t cnt, int dir, float& s, float thr,
-                                       RowShared& sh) {
+                                       RowShared& sh, uint32_t head_max = 512u) {
     // (the head of a sorted run holds its largest elements, nearly every one an ordered step
     // of the emulation: it goes one by one; the emulation takes the rest)
-    const uint32_t head = cnt < 512u ? cnt : 512u;
+    const uint32_t head = cnt < head_max ? cnt : head_max;
     {
         if (threadIdx.x == 0) {
             // Groups of eight: the sum steps through a group with no branch, and the stop test
@@ -1746,7 +1774,7 @@ __global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CT
     const uint32_t r = blockIdx.x;
     const int tid = threadIdx.x;
     const RowPrep rp = S.rprep[r];
-    if (rp.flags & (kRowDone | kRowFallback)) return;
+    if (rp.flags & (kRowDone | kRowFallback | kRowBig)) return;
     const long long t_start = clock64();
     const uint32_t nk = S.list_n[r];
     if (nk > kStageListCap && (rp.flags & kRowPathK)) {  // a top-k list overflow (ties): lrs_sample_rows
@@ -1806,14 +1834,15 @@ __global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CT
             tm = clock64();
             n_keys = regather_nucleus(S, r, P, M, inv, exptab, keys, sh, cand, attempt - 1, split, above);
             c_regather += clock64() - tm;
-            if (n_keys == 0xFFFFFFFFu) {
-                if (tid == 0) stage_fallback(S, r);
+            if (n_keys == 0xFFFFFFFFu) {  // (deeper than the list's capacity)
+                if (tid == 0) stage_big_or_fallback(S, r, a.n);
                 return;
             }
         }
         // pass 0 of a long top-p list sorts only the head the prefilter keeps; pass 1 the
         // whole list again (from its copy in the row's list area) if the cut is not inside it
         bool inside = false;
+        float short_by = 0.0f;  // (the whole list sorted short of top_p: the mass still missing / p_lim)
         for (int pass = 0; pass < 2 && !inside; ++pass) {
             uint32_t m_keys = n_keys;
             float p_left = 0.0f;
@@ -1850,11 +1879,20 @@ __global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CT
             const float p_lim = fmaxf(p_out, p_left);
             const bool complete = whole && m_keys == n_keys;
             inside = complete || ((stp >= 0 || kk == rp.k) && cut > 0 && sk.p(cut - 1) > p_lim);
+            if (!inside && stp < 0 && m_keys == n_keys && kk < rp.k && p_lim > 0.0f)
+                short_by = (float)(((double)P.top_p - (double)cum * 1.001) / (double)p_lim);
             if (m_keys == n_keys) break;  // (no second pass without a prefilter)
         }
         if (inside) break;
+        // Every element outside the list has a probability of at most p_lim, so the nucleus holds
+        // at least short_by more elements than the list: when no list can hold it, lrs_stage_big
+        // takes the row now (a regather would fail).
+        if (topp_on && (double)n_keys + (double)short_by > (double)kStageListCap) {
+            if (tid == 0) stage_big_or_fallback(S, r, a.n);
+            return;
+        }
         if (attempt == 2) {
-            if (tid == 0) stage_fallback(S, r);
+            if (tid == 0) stage_big_or_fallback(S, r, a.n);
             return;
         }
     }
@@ -1897,4 +1935,539 @@ __global__ void __maxnreg__(144) lrs_stage_finish(const StageArgs S) {  // (2 CT
     inf.cycles[6] = sat(c_sort);
     inf.cycles[7] = sat(c_runs);
     write_row(a, r, LRS_OK, inf.token, inf.prob, true, st, inf);
+}
+
+// ------------------------------------------------------------- big nuclei ----
+// A top-p row whose nucleus cannot fit in a list (flat rows: nuclei of 10^5 tokens,
+// sampler.rs:132-146) is sampled by lrs_stage_big, one CTA per row, after the sum stage
+// has given its exact denominator S:
+//   1. every element's exact p = fl(libm expf(d) * fl(1/S)) (ops.rs:409-416) is counted in
+//      a bucket of its bits below those of the largest p (fl(1/S)): 2^kBigShift float steps
+//      (1/256 binade) a bucket, kBigBuckets - 1 of them (32 binades), the last taking every
+//      smaller p;
+//      CUDA's expf decides the bucket where it cannot differ from libm's value;
+//   2. the keys (p desc, index asc as an ascending 64-bit key) are scattered bucket by bucket
+//      into the CTA's scratch (a counting sort: the buckets are in key order);
+//   3. the top-p sum (sampler.rs:137-145) runs over chunks of whole buckets: a chunk's buckets
+//      are sorted in shared memory (a warp a bucket), written back, and summed by the exact
+//      emulation of the sequential f32 sum (acc_tile);
+//   4. the draw (sampler.rs:155-162) runs over the sorted survivors the same way.
+// A row whose walk reaches the last bucket, or whose bucket is larger than a chunk, goes to
+// lrs_sample_rows (same inputs, same results).
+constexpr int kBigShift = 15;
+constexpr uint32_t kBigBuckets = 8192;
+constexpr uint32_t kBigBitWords = kStageMaxTiles * (uint32_t)kTile / 32u + 8u;  // window bitmap (+ edges)
+constexpr uint32_t kBigMargin = 12u;  // float steps between CUDA's expf-based p and the exact p (at most 7)
+
+struct BigChunk {
+    unsigned long long keys[kChunk];
+    uint16_t perm[2 * kChunk];
+};
+struct BigShared {
+    uint32_t end[kBigBuckets];  // counts, then bucket starts, then (after the scatter) bucket ends
+    uint32_t sorted[kBigBuckets / 32];  // bucket b is sorted in the scratch
+    union {
+        uint32_t bits[kBigBitWords];  // steps 1-2: the window (sampler.rs:82-102)
+        BigChunk ck;                  // steps 3-4
+    } u;
+};
+constexpr size_t kBigSmem = sizeof(BigShared);
+
+// Bucket of p (bits pb) below the largest p (bits top); kBigBuckets - 1: every smaller p.
+__device__ __forceinline__ uint32_t big_bucket(uint32_t top, uint32_t pb) {
+    const uint32_t diff = pb >= top ? 0u : top - pb;
+    const uint32_t b = diff >> kBigShift;
+    return b < kBigBuckets - 1u ? b : kBigBuckets - 1u;
+}
+
+// The scaled logit's d = fl(fl(pen(x) * inv_t) - M) of element i (sampler.rs:96-100, 115-118;
+// ops.rs:409), with the window in `bits`.
+__device__ __forceinline__ float big_d(float x, uint32_t i, const uint32_t* bits, bool pen, float penalty,
+                                       float inv_t, float M) {
+    if (pen && ((bits[i >> 5] >> (i & 31u)) & 1u)) x = penalise(x, penalty);
+    return d_of(x, inv_t, M);
+}
+
+// The largest bucket end at most lim (pos + kChunk: the end of the chunk that starts at pos),
+// or 0 when there is none past pos (the bucket at pos alone is longer, or pos has reached the
+// last bucket).
+__device__ __forceinline__ uint32_t big_chunk_end(const uint32_t* end, uint32_t pos, uint32_t nsorted,
+                                                  uint32_t lim = 0xFFFFFFFFu) {
+    if (pos >= nsorted) return 0u;
+    if (lim == 0xFFFFFFFFu) lim = pos + (uint32_t)kChunk;
+    // largest b <= kBigBuckets - 2 with end[b] <= lim (end is non-decreasing)
+    int lo = -1, hi = (int)kBigBuckets - 2;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (end[mid] <= lim) lo = mid; else hi = mid - 1;
+    }
+    const uint32_t c1 = lo >= 0 ? end[lo] : 0u;
+    return c1 > pos ? c1 : 0u;
+}
+
+// keys[0, cnt) = src[0, cnt), cnt <= kChunk: every load of the thread issued before its stores.
+__device__ __forceinline__ void big_load_chunk(const unsigned long long* src, uint32_t cnt, unsigned long long* keys) {
+    unsigned long long v[kVpt];
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) {
+        const uint32_t i = threadIdx.x + (uint32_t)j * kThreads;
+        v[j] = i < cnt ? __ldcg(src + i) : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) {
+        const uint32_t i = threadIdx.x + (uint32_t)j * kThreads;
+        if (i < cnt) keys[i] = v[j];
+    }
+}
+
+// First and last bucket of the chunk [pos, c1) (pos and c1 bucket boundaries, c1 > pos).
+__device__ __forceinline__ void big_chunk_buckets(const uint32_t* end, uint32_t pos, uint32_t c1, uint32_t& b0,
+                                                  uint32_t& b1) {
+    int lo = 0, hi = (int)kBigBuckets - 2;  // smallest b with end[b] > pos
+    while (lo < hi) {
+        const int mid = (lo + hi) >> 1;
+        if (end[mid] > pos) hi = mid; else lo = mid + 1;
+    }
+    b0 = (uint32_t)lo;
+    lo = (int)b0;
+    hi = (int)kBigBuckets - 2;  // largest b with end[b] <= c1
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (end[mid] <= c1) lo = mid; else hi = mid - 1;
+    }
+    b1 = (uint32_t)lo;
+}
+
+// The chunk [pos, pos + cnt) of B, loaded in shared memory: each of its buckets sorted (a
+// warp a bucket; a bucket of more than 512 keys: the whole chunk by the block), and the sorted
+// chunk written back to B.
+__device__ __noinline__ void big_sort_chunk(unsigned long long* B, uint32_t pos, uint32_t cnt, uint32_t b0,
+                                            uint32_t b1, BigShared& bs, RowShared& sh) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    unsigned long long* keys = bs.u.ck.keys;
+    if (tid == 0) sh.misc[3] = 0u;
+    csync();
+    for (uint32_t b = b0 + (uint32_t)warp; b <= b1; b += kWarps) {
+        const uint32_t lo = (b == 0u ? 0u : bs.end[b - 1u]) - pos, hi = bs.end[b] - pos;
+        const uint32_t c = hi - lo;
+        if (c <= 1u || ((bs.sorted[b >> 5] >> (b & 31u)) & 1u)) continue;
+        if (lane == 0 && c <= 512u) atomicOr(&bs.sorted[b >> 5], 1u << (b & 31u));
+        if (c <= 64u)
+            warp_sort_run<2>(keys, lo, hi, hi);
+        else if (c <= 128u)
+            warp_sort_run<4>(keys, lo, hi, hi);
+        else if (c <= 256u)
+            warp_sort_run<8>(keys, lo, hi, hi);
+        else if (c <= 512u)
+            warp_sort_run<16>(keys, lo, hi, hi);
+        else if (lane == 0)
+            sh.misc[3] = 1u;
+    }
+    csync();
+    if (sh.misc[3]) {
+        (void)stage_sort_u64(keys, cnt, bs.u.ck.perm, bs.u.ck.perm + kChunk);
+        for (uint32_t b = b0 + (uint32_t)tid; b <= b1; b += kThreads) atomicOr(&bs.sorted[b >> 5], 1u << (b & 31u));
+    }
+#pragma unroll
+    for (int j = 0; j < kVpt; ++j) {
+        const uint32_t i = (uint32_t)tid + (uint32_t)j * kThreads;
+        if (i < cnt) __stcg(B + pos + i, keys[i]);
+    }
+    csync();
+}
+
+// A run of whole buckets of the walk, in any order (src: shared or global memory): its
+// increments on the grid of s (unit 2^uu), summed over the block.  When no element is an
+// ordered step (a tie or an element of half a binade on that grid) and the total keeps s inside
+// its binade (and, for the top-p sum, below thr), every order of the run gives the same exact
+// result: s is advanced and the run needs no order.  Same values for every thread.
+template <int DIR>
+__device__ __noinline__ bool big_fast_range(const unsigned long long* src, uint32_t cnt, float& s, float thr,
+                                            RowShared& sh, bool apply = true) {
+    const float kInf = __int_as_float(0x7F800000);
+    const int uu = unit_exp(s);
+    const uint32_t A = grid_count(s, uu);
+    const uint32_t lower = grid_lower(uu);
+    const float tq = (DIR > 0 && thr < kInf) ? ldexpf(thr, -uu) : kInf;
+    uint32_t tot = 0, ev = 0;
+    for (uint32_t base = 0; base < cnt; base += (uint32_t)kChunk) {
+        unsigned long long k[kVpt];
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j) {
+            const uint32_t i = base + threadIdx.x + (uint32_t)j * kThreads;
+            k[j] = i < cnt ? src[i] : ~0ull;  // (generic load: src may be shared or global; ~0: p = 0)
+        }
+#pragma unroll
+        for (int j = 0; j < kVpt; ++j) {
+            const Cls c = classify(~(uint32_t)(k[j] >> 32), uu);
+            tot = sat_add(tot, c.inc);
+            ev |= (c.tie || c.big) ? 1u : 0u;
+        }
+    }
+    const uint32_t total = block_reduce_u32(tot, SatAdd(), sh.red);
+    const uint32_t any = block_reduce_u32(ev, OrOp(), sh.red2);
+    const bool fast = !any && (DIR > 0 ? (A + total <= kTwo24 - 1u && (float)(A + total) < tq) : total < A - lower);
+    if (fast && apply) s = grid_value(uu, DIR > 0 ? A + total : A - total);
+    return fast;
+}
+
+template <int DIR>
+__device__ __forceinline__ float big_step(float c, float v) {
+    if constexpr (DIR > 0) return __fadd_rn(c, v); else return __fsub_rn(c, v);
+}
+template <int DIR>
+__device__ __forceinline__ bool big_hit(float c, float thr) {
+    if constexpr (DIR > 0) return c >= thr; else return c <= 0.0f;
+}
+__device__ __forceinline__ float big_p(const unsigned long long* keys, uint32_t i, uint32_t cnt) {
+    return i < cnt ? __uint_as_float(~(uint32_t)(keys[i] >> 32)) : 0.0f;
+}
+template <int DIR>
+__device__ __forceinline__ int big_serial(const unsigned long long* keys, uint32_t cnt, float& s, float thr,
+                                          RowShared& sh) {
+    if (threadIdx.x == 0) {
+        float cur = s;
+        int stop = -1;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = big_p(keys, (uint32_t)j, cnt);
+        for (uint32_t i = 0; i < cnt; i += 8) {
+            float nx[8], c[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nx[j] = big_p(keys, i + 8u + (uint32_t)j, cnt);
+            // (positions past cnt add 0: they neither move s nor stop it)
+            c[0] = big_step<DIR>(cur, v[0]);
+#pragma unroll
+            for (int j = 1; j < 8; ++j) c[j] = big_step<DIR>(c[j - 1], v[j]);
+            if (big_hit<DIR>(c[7], thr)) {
+                int f = 7;
+#pragma unroll
+                for (int j = 6; j >= 0; --j) f = big_hit<DIR>(c[j], thr) ? j : f;
+                float cf = c[7];
+#pragma unroll
+                for (int j = 6; j >= 0; --j) cf = f == j ? c[j] : cf;
+                stop = (int)i + f;
+                cur = cf;
+                break;
+            }
+            cur = c[7];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = nx[j];
+        }
+        sh.fstate = cur;
+        sh.stop = stop;
+    }
+    csync();
+    s = sh.fstate;
+    const int st = sh.stop;
+    csync();
+    return st;
+}
+
+// The sequential run over positions [0, lim) of the bucketed keys (sampler.rs:137-145 for
+// DIR > 0, sampler.rs:156-161 for DIR < 0).  A window of whole buckets (up to kBigWindow
+// chunks, doubling while the windows need no order) is tried in one step straight from the
+// scratch; otherwise one chunk: in one step if it needs no order, else its buckets sorted
+// and the run taken one element after another.  Returns the stop position or -1 (fail: a
+// bucket longer than a chunk, or the last bucket reached); s: the value after it.
+constexpr uint32_t kBigWindow = 16;
+template <int DIR>
+__device__ __noinline__ int big_walk(unsigned long long* B, uint32_t lim, uint32_t nsorted, float& s, float thr,
+                                     BigShared& bs, RowShared& sh, bool& fail, long long& c_sort) {
+    const int tid = threadIdx.x;
+    uint32_t win = 2;
+    for (uint32_t pos = 0; pos < lim;) {
+        if (DIR < 0 || pos > 0u) {  // (the top-p sum's first chunk holds its first, ordered steps)
+            if (tid == 0) {
+                const uint32_t far = pos + win * (uint32_t)kChunk;
+                sh.misc[0] = big_chunk_end(bs.end, pos, nsorted, far < lim ? far : lim);
+            }
+            csync();
+            const uint32_t wend = sh.misc[0];
+            csync();
+            if (wend > pos + (uint32_t)kChunk) {
+                if (big_fast_range<DIR>(B + pos, wend - pos, s, thr, sh)) {
+                    pos = wend;
+                    win = win * 2u < kBigWindow ? win * 2u : kBigWindow;
+                    continue;
+                }
+                win = 2;
+            }
+        }
+        if (tid == 0) {
+            const uint32_t c1 = big_chunk_end(bs.end, pos, nsorted);
+            uint32_t b0 = 0, b1 = 0;
+            if (c1) big_chunk_buckets(bs.end, pos, c1, b0, b1);
+            sh.misc[0] = c1;
+            sh.misc[1] = b0;
+            sh.misc[2] = b1;
+        }
+        csync();
+        const uint32_t c1 = sh.misc[0], b1 = sh.misc[2];
+        uint32_t b0 = sh.misc[1];
+        csync();
+        if (!c1) {
+            fail = true;
+            return -1;
+        }
+        big_load_chunk(B + pos, c1 - pos, bs.u.ck.keys);
+        csync();
+        const uint32_t wc = (c1 < lim ? c1 : lim) - pos;
+        bool sorted = false;
+        if (c1 > lim) {  // (cut by lim: the first wc positions need their order)
+            big_sort_chunk(B, pos, c1 - pos, b0, b1, bs, sh);
+            sorted = true;
+        }
+        if ((DIR < 0 || pos > 0u) && big_fast_range<DIR>(bs.u.ck.keys, wc, s, thr, sh)) {
+            pos = c1;
+            continue;
+        }
+        uint32_t from = 0;  // (chunk-relative start of the part still to walk)
+        if (!sorted && (DIR < 0 || pos > 0u) && b1 > b0) {
+            // The first bucket holding an ordered step: the longest run of whole buckets from b0
+            // that needs no order (bisection), added in one step; that bucket sorted and walked
+            // one element after another; the rest of the chunk in one step if it needs no order.
+            uint32_t good = b0, bad = b1 + 1u;  // [b0, good) needs no order; [b0, bad) does
+            while (bad - good > 1u) {
+                const uint32_t mid = (good + bad) >> 1;
+                const uint32_t e = bs.end[mid - 1u] - pos;
+                if (big_fast_range<DIR>(bs.u.ck.keys, e, s, thr, sh, false)) good = mid; else bad = mid;
+            }
+            const uint32_t e0 = good > b0 ? bs.end[good - 1u] - pos : 0u;  // (the event bucket: good)
+            if (e0) (void)big_fast_range<DIR>(bs.u.ck.keys, e0, s, thr, sh);
+            const uint32_t e1 = bs.end[good] - pos;
+            const long long t0 = clock64();
+            big_sort_chunk(B, pos, c1 - pos, good, good, bs, sh);
+            c_sort += clock64() - t0;
+            const uint32_t hi = e1 < wc ? e1 : wc;
+            if (hi > e0) {
+                const int st = big_serial<DIR>(bs.u.ck.keys + e0, hi - e0, s, thr, sh);
+                if (st >= 0) return (int)(pos + e0) + st;
+            }
+            if (e1 >= wc) {
+                pos = c1;
+                continue;
+            }
+            if (big_fast_range<DIR>(bs.u.ck.keys + e1, wc - e1, s, thr, sh)) {
+                pos = c1;
+                continue;
+            }
+            from = e1;
+            b0 = good + 1u;
+        }
+        if (!sorted) {
+            const long long t0 = clock64();
+            big_sort_chunk(B, pos, c1 - pos, b0, b1, bs, sh);
+            c_sort += clock64() - t0;
+        }
+        const int st = big_serial<DIR>(bs.u.ck.keys + from, wc - from, s, thr, sh);
+        if (st >= 0) return (int)(pos + from) + st;
+        pos = c1;
+    }
+    return -1;
+}
+
+// One big-nucleus row by the CTA (steps 1-4 above); B: the CTA's scratch (n keys).
+__device__ __noinline__ void big_row(const StageArgs& S, uint32_t r, unsigned long long* B, BigShared& bs,
+                                     RowShared& sh) {
+    const lrs_kernel_args_t& a = S.a;
+    const int tid = threadIdx.x;
+    const long long t_start = clock64();
+    const RowPrep rp = S.rprep[r];
+    if ((rp.flags & (kRowDone | kRowFallback)) || !(rp.flags & kRowBig)) return;  // (the sum may have left it)
+    const lrs_params P = a.params[r];
+    const Geo g = row_geometry(a, r);
+    const uint32_t n = g.n;
+    const float M = rp.M, inv_t = rp.inv_t;
+    const float Ssum = __uint_as_float(rp.pad[0]);
+    const float inv = __fdiv_rn(1.0f, Ssum);    // ops.rs:413
+    const uint32_t top = __float_as_uint(inv);  // the largest p (e = 1)
+    const ExpTable exptab{a.exp_index, a.exp_entries, a.exp_near};
+    const bool pen = P.repetition_penalty != 1.0f;
+    const float penalty = P.repetition_penalty;
+    const uint32_t hlen = (pen && a.hist_len) ? a.hist_len[r] : 0u;
+    const uint32_t* hrow = a.hist ? a.hist + (uint64_t)r * a.hist_ld : nullptr;
+    const uint32_t hstart = window_start(P, hlen);
+    const uint32_t words = (n + 31u) / 32u;
+    if (words > kBigBitWords) {  // (prep sends no such row)
+        if (tid == 0) stage_fallback(S, r);
+        return;
+    }
+    uint32_t* bits = bs.u.bits;
+    // ---- 1. the window's bits; the bucket counts ----
+    for (uint32_t w = tid; w < words; w += kThreads) bits[w] = 0u;
+    for (uint32_t b = tid; b < kBigBuckets; b += kThreads) bs.end[b] = 0u;
+    if (tid == 0) {
+        sh.misc[7] = 0u;
+        sh.events = 0u;
+    }
+    csync();
+    for (uint32_t j = hstart + tid; j < hlen; j += kThreads) {
+        const uint32_t id = hrow[j];
+        if (id < n) atomicOr(&bits[id >> 5], 1u << (id & 31u));
+    }
+    csync();
+    // (kVpt elements a thread per batch, the next batch's loads issued before this one's work)
+    constexpr uint32_t kBatch = (uint32_t)kVpt * kThreads;
+    auto load_batch = [&](uint32_t i0, float (&x)[kVpt]) {
+#pragma unroll
+        for (int u = 0; u < kVpt; ++u) {
+            const uint32_t i = i0 + (uint32_t)u * kThreads;
+            x[u] = i < n ? __ldg(g.row + i) : 0.0f;
+        }
+    };
+    float xa[kVpt];
+    load_batch((uint32_t)tid, xa);
+    for (uint32_t i0 = tid; i0 < n; i0 += kBatch) {
+        float xb[kVpt];
+        load_batch(i0 + kBatch, xb);
+#pragma unroll
+        for (int u = 0; u < kVpt; ++u) {
+            const uint32_t i = i0 + (uint32_t)u * kThreads;
+            if (i < n) {
+                const float d = big_d(xa[u], i, bits, pen, penalty, inv_t, M);
+                const uint32_t pb = __float_as_uint(__fmul_rn(expf(d), inv));
+                uint32_t b = big_bucket(top, pb);
+                if (big_bucket(top, pb + kBigMargin) != big_bucket(top, pb > kBigMargin ? pb - kBigMargin : 0u))
+                    b = big_bucket(top, __float_as_uint(__fmul_rn(exact_expf(d, exptab), inv)));
+                atomicAdd(&bs.end[b], 1u);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kVpt; ++u) xa[u] = xb[u];
+    }
+    csync();
+    {  // bucket starts (exclusive prefix over the buckets, a contiguous run of them a thread)
+        constexpr uint32_t per = (kBigBuckets + kThreads - 1) / kThreads;
+        const uint32_t b0 = (uint32_t)tid * per;
+        uint32_t c = 0;
+        for (uint32_t j = 0; j < per; ++j)
+            if (b0 + j < kBigBuckets) c += bs.end[b0 + j];
+        uint32_t total;
+        uint32_t run = block_excl_scan(c, sh.red, total);
+        for (uint32_t j = 0; j < per; ++j) {
+            if (b0 + j < kBigBuckets) {
+                const uint32_t x = bs.end[b0 + j];
+                bs.end[b0 + j] = run;
+                run += x;
+            }
+        }
+    }
+    csync();
+    const uint32_t nsorted = bs.end[kBigBuckets - 1];  // keys scattered (the last bucket is not)
+    // ---- 2. the keys, bucket by bucket (exact p: p desc, index asc) ----
+    load_batch((uint32_t)tid, xa);
+    for (uint32_t i0 = tid; i0 < n; i0 += kBatch) {
+        float xb[kVpt];
+        load_batch(i0 + kBatch, xb);
+#pragma unroll
+        for (int q = 0; q < kVpt; q += 4) {  // (four exps side by side)
+            float d[4], ev[4];
+            bool ok[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t i = i0 + (uint32_t)(q + u) * kThreads;
+                d[u] = i < n ? big_d(xa[q + u], i, bits, pen, penalty, inv_t, M) : 0.0f;
+                ok[u] = expf_rounded(d[u], exptab, ev[u]);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint32_t i = i0 + (uint32_t)(q + u) * kThreads;
+                if (i < n) {
+                    const float e = ok[u] ? ev[u] : exact_expf_table(d[u], exptab, ev[u]);
+                    const uint32_t pb = __float_as_uint(__fmul_rn(e, inv));
+                    const uint32_t b = big_bucket(top, pb);
+                    if (b < kBigBuckets - 1u) {
+                        const uint32_t slot = atomicAdd(&bs.end[b], 1u);
+                        __stcg(B + slot, ((unsigned long long)(~pb) << 32) | i);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kVpt; ++u) xa[u] = xb[u];
+    }
+    csync();
+    const long long t_scatter = clock64();
+    long long c_sort = 0;  // (diagnostics: cycles sorting chunks)
+    // ---- 3. the top-p cut over the first k (sampler.rs:122-146), chunk by chunk ----
+    const uint32_t kk = rp.k < n ? rp.k : n;
+    float cum = 0.0f;
+    int stop = -1;
+    bool fail = false;
+    for (uint32_t w = tid; w < kBigBuckets / 32u; w += kThreads) bs.sorted[w] = 0u;
+    csync();
+    stop = big_walk<+1>(B, kk, nsorted, cum, P.top_p, bs, sh, fail, c_sort);
+    if (fail) {
+        if (tid == 0) stage_fallback(S, r);
+        return;
+    }
+    // the cutoff (sampler.rs:137-146); the survivor sum is the same sequence (sampler.rs:148-151)
+    const uint32_t cut = stop >= 0 ? (uint32_t)stop + 1u : kk;
+    // ---- 4. the draw over the sorted survivors (sampler.rs:152-162) ----
+    unsigned long long st = a.state[r];
+    uint32_t ps = 0;
+    float r0 = 0.0f;
+    if (cum > 0.0f) {
+        r0 = __fmul_rn(next_f32(&st), cum);  // sampler.rs:155
+        float rv = r0;
+        ps = cut - 1u;
+        bool dfail = false;
+        const int w = big_walk<-1>(B, cut, nsorted, rv, 0.0f, bs, sh, dfail, c_sort);
+        if (w >= 0) ps = (uint32_t)w;
+        if (dfail && tid == 0) sh.misc[7] = 1u;  // (the top-p walk covered [0, cut): should not happen)
+    }
+    if (tid != 0) return;
+    if (sh.misc[7]) {  // (an internal bound of the exact emulation failed: should not happen)
+        stage_fallback(S, r);
+        return;
+    }
+    const unsigned long long chosen = __ldcg(B + ps);
+    lrs_row_info inf = blank_info(2u, rp.k);
+    inf.token = (uint32_t)(chosen & 0xFFFFFFFFu);
+    inf.prob = __uint_as_float(~(uint32_t)(chosen >> 32));
+    inf.cutoff = cut;
+    inf.pos = ps;
+    inf.max = M;
+    inf.sum_exp = Ssum;
+    inf.surv_sum = cum;
+    inf.r0 = r0;
+    inf.n_cand = nsorted;
+    inf.events = rp.pad[1];
+    const long long dt = clock64() - t_start;
+    inf.cycles[2] = dt > 0xFFFFFFFFll ? 0xFFFFFFFFu : (uint32_t)dt;
+    inf.cycles[4] = 1u;  // (finished by the staged pipeline)
+    inf.cycles[5] = rp.walks;
+    auto sat = [](long long v) -> uint32_t { return v > 0xFFFFFFFFll ? 0xFFFFFFFFu : (v < 0 ? 0u : (uint32_t)v); };
+    // (diagnostics: 0 and 1 the prep and sum stages; 3 the counting and scattering; 6 the two
+    // walks; 7 the sorts within 6)
+    inf.cycles[0] = rp.cyc_prep;
+    inf.cycles[1] = rp.cyc_sum;
+    inf.cycles[3] = sat(t_scatter - t_start);
+    inf.cycles[6] = sat(clock64() - t_scatter);
+    inf.cycles[7] = sat(c_sort);
+    write_row(a, r, LRS_OK, inf.token, inf.prob, true, st, inf);
+}
+
+// Persistent: each CTA takes the next row of big_rows and samples it in its own scratch
+// (the first n words of lrs_sample_rows' per-CTA scratch, which that kernel, launched after
+// this one, overwrites before it reads).
+__global__ void __launch_bounds__(kThreads, 2) lrs_stage_big(const StageArgs S) {
+    extern __shared__ __align__(16) unsigned char big_smem[];
+    BigShared& bs = *reinterpret_cast<BigShared*>(big_smem);
+    __shared__ RowShared sh;
+    __shared__ uint32_t claim;
+    if (*(volatile const uint32_t*)S.big_count == 0u) return;
+    unsigned long long* B = S.a.scratch + (uint64_t)blockIdx.x * S.a.scratch_stride;
+    for (;;) {
+        if (threadIdx.x == 0) {
+            const uint32_t i = atomicAdd(S.big_claim, 1u);
+            claim = i < *(volatile const uint32_t*)S.big_count ? S.big_rows[i] : 0xFFFFFFFFu;
+        }
+        csync();
+        const uint32_t r = claim;
+        csync();
+        if (r == 0xFFFFFFFFu) return;
+        big_row(S, r, B, bs, sh);
+    }
 }

@@ -362,3 +362,35 @@ def test_pinned_host_rows_copied_in_pieces():
     np.testing.assert_array_equal(st, rst)
     np.testing.assert_array_equal(probs.view(np.uint32), rinfo["prob"].view(np.uint32))
     bs.close()
+
+
+def test_big_nucleus_rows():
+    # Nuclei of 10^4 - 10^5 tokens, larger than any list: the big-nucleus stage buckets every
+    # key of the row and walks the top-p sum and the draw over them.  Covered: top_k between
+    # the list's capacity and the nucleus (the walk stops at k), penalties over a long window,
+    # rows that start off 16-byte alignment, logits rounded to a coarse grid (runs of equal
+    # probabilities: buckets of more than 512 keys are sorted by the block, a bucket longer
+    # than a chunk sends the row to the persistent kernel), and a flat row with top_p near 1.
+    rng = np.random.default_rng(41)
+    rows, n, ld = 12, 151_936, 151_939
+    buf = (rng.standard_normal((rows, ld)) * 0.5).astype(np.float32)
+    buf[3] = np.round(buf[3] * 64) / 64      # about 250 distinct values: long runs of ties
+    buf[4] = np.round(buf[4] * 512) / 512    # about 2,000 distinct values
+    buf[5, 7] += 6.0                         # one high logit over a flat row
+    buf[6] = (rng.standard_normal(ld) * 2).astype(np.float32)
+    buf[6, 1234] += 12.0                     # config-4 spiked row
+    p = O.make_params(1.0, 0, 0.9, 1.2, 1024, rows=rows)
+    p["top_k"] = [0, 20_000, 9_000, 0, 0, 0, 0, 60_000, 0, 0, 0, 0]
+    p["top_p"] = [0.9, 0.95, 0.97, 0.9, 0.9, 0.8, 0.9, 0.999, 0.5, 0.99, 0.9, 0.9]
+    p["temperature"] = [1.0, 1.0, 1.3, 1.0, 0.9, 1.0, 1.0, 1.0, 1.0, 0.7, 1.5, 1.0]
+    p["repetition_penalty"] = [1.2, 1.0, 1.2, 1.0, 1.2, 1.0, 1.2, 1.1, 1.3, 1.0, 0.8, 1.2]
+    hist = rng.integers(0, n, (rows, 1024)).astype(np.uint32)
+    hl = np.full(rows, 1024, np.uint32)
+    st = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+    # odd rows start 4 bytes past a 16-byte boundary (ld is odd)
+    gpu = run_device(buf, n, hist, hl, p, st, ld=ld)
+    ref = run_oracle(np.ascontiguousarray(buf[:, :n]), n, hist, hl, p, st)
+    assert compare(gpu, ref, "big nuclei") == rows
+    infos = gpu[1]
+    big = (infos["cycles"][:, 4] == 1) & (infos["n_cand"] > 8192)  # (more keys than a list holds)
+    assert big.sum() >= 8, f"only {int(big.sum())} rows took the big-nucleus stage"
