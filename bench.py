@@ -5,15 +5,16 @@
 Workload (per GPU): the headline configuration, 1024 rows x 151,936 f32 logits with the
 mixed per-row parameters of the benchmark's config 3 (temperature U[0.5,1.5], top_k in
 {0,20,40,100}, top_p U[0.8,1.0], repetition penalty U[1.0,1.3] over a 64-token window),
-seeded synthetic data.  A step samples every row once through the staged pipeline: six
+seeded synthetic data.  A step samples every row once through the staged pipeline: seven
 launches (tile statistics, per-row prep, tile classification, the exact running sum, the
-finish, then lrs_sample_rows on the rows the stages leave).  Rows are independent, so N GPUs
+finish, the big-nucleus stage for top-p rows whose nucleus exceeds a list, then
+lrs_sample_rows on the rows the stages leave).  Rows are independent, so N GPUs
 run N replicas on different rows (weak scaling, no collective).
 
 value      rows/s over all GPUs with inputs resident in HBM (CUDA events, max over ranks)
 e2e        the same metric through the host-buffer entry point (lrs_sample): pinned host
            logits copied in and tokens/statuses copied out inside the timed region
-roofline   algorithmic bytes (4 * vocab + 4 * window per row) / step time (the six launches) vs
+roofline   algorithmic bytes (4 * vocab + 4 * window per row) / step time (the seven launches) vs
            measured HBM copy bandwidth; traffic = DRAM bytes per step from the committed ncu summary
 cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of the same rows
            (the first --cpu-rows rows, repeated for about --cpu-seconds on all host threads)
@@ -27,6 +28,11 @@ cpu_baseline  the CPU restatement of sampler.rs (oracle) on a bounded sample of 
            (one row: latency of a draw through the drop-in single-row API, and 10,000 draws as
            rows sharing the logits), config 2 (greedy), config 3 (mixed, 109,051 wide), config 4
            (nucleus stress, 4096 rows, window 1024); rows/s and the roofline fraction of each
+configs    (default run, one GPU; --no-configs skips it) the same configurations 1-4 in brief
+           inside the headline line: configs 2-4 at their full sizes on seeded inputs generated
+           on the device with the workloads' distributions and parameter mixes (the host
+           generator takes minutes at these sizes), config 1 through the drop-in single-row
+           API and as 10,000 draws sharing the logits
 """
 from __future__ import annotations
 
@@ -48,7 +54,7 @@ WORKLOAD = ("headline: 1024 rows x 151,936 f32 logits per GPU, Gumbel + Zipf-lik
             "permutation, temperature U[0.5,1.5], top_k {0,20,40,100}, top_p U[0.8,1.0], "
             "repetition penalty U[1.0,1.3] over a 64-token window")
 FALLBACK_HBM_GBS = 6650.0
-STAGE_LAUNCHES = 6  # kernels of one step (the staged pipeline, lrs_stage_launch)
+STAGE_LAUNCHES = 7  # kernels of one step (the staged pipeline, lrs_stage_launch)
 NOMINAL_HBM_GBS = 8000.0  # B200 HBM3e, nominal (the north star quotes 8 TB/s)
 
 
@@ -369,6 +375,120 @@ def run_configs(args):
     print(json.dumps(out), flush=True)
 
 
+def brief_configs(dev, peak):
+    """Configs 1-4 in brief for the headline line (one GPU): configs 2-4 at their full sizes on
+    seeded inputs generated on the device with the distributions and parameter mixes of
+    lrs.workloads (greedy rows with planted ties; Zipf-like rows under a per-row permutation
+    with the mixed parameters; flat and spiked nucleus-stress rows with a 1,024-token window),
+    config 1 on the workload's own row: one draw at a time through the drop-in single-row API,
+    and 10,000 draws as rows sharing the logits.  rows/s and the roofline fraction of each."""
+    import torch
+    import lrs
+    from lrs import workloads as W
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(4242)
+    rng = np.random.default_rng(4242)
+
+    def timed(x, params, window, reps, ld=None, rows=None, state=None):
+        rows = rows if rows is not None else x.shape[0]
+        V = x.shape[1]
+        bs = lrs.BatchSampler(rows, V, max(window, 1))
+        P = torch.from_numpy(np.ascontiguousarray(params).view(np.uint8)).to(dev)
+        if state is None:
+            state = rng.integers(1, 2**62, rows).astype(np.uint64) | np.uint64(1)
+        st = torch.from_numpy(state.view(np.int64)).to(dev)
+        hist = hl = None
+        if window:
+            hist = torch.randint(0, V, (rows, window), device=dev, generator=gen, dtype=torch.int32)
+            hl = torch.full((rows,), window, dtype=torch.int32, device=dev)
+        tok = torch.zeros(rows, dtype=torch.int32, device=dev)
+        sts = torch.zeros(rows, dtype=torch.int32, device=dev)
+
+        def step():
+            bs.sample_device(x, P, st, tok, n=V, hist=hist, hist_len=hl, status=sts, ld=ld, rows=rows)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        if int((sts != 0).sum()):
+            raise SystemExit("a row reported a non-zero status")
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            step()
+        b.record()
+        torch.cuda.synchronize()
+        bs.close()
+        ms = a.elapsed_time(b) / reps
+        row_bytes = 4 * V * (0 if ld == 0 else 1) + 4 * window
+        return {"rows": rows, "vocab": V, "window": window, "ms_per_step": ms, "rows_per_s": rows / (ms / 1e3),
+                "roofline_frac": (rows * row_bytes / (ms / 1e3) / 1e9) / peak}
+
+    def params(rows, t, k, p, pen, last):
+        out = np.zeros(rows, lrs.PARAMS_DTYPE)
+        out["temperature"], out["top_k"], out["top_p"] = t, k, p
+        out["repetition_penalty"], out["repeat_last_n"] = pen, last
+        return out
+
+    res = {"data": "configs 2-4: seeded inputs generated on the device with the distributions and parameter "
+                   "mixes of lrs.workloads; config 1: the workload's own row"}
+    V = W.QWEN_VOCAB
+    # config 2: 256 greedy rows, the max planted at 2-4 positions in 10% of them
+    x = torch.randn(256, V, device=dev, generator=gen) * 3.0
+    for r in range(3, 256, 10):
+        k = int(rng.integers(2, 5))
+        pos = torch.randperm(V, device=dev, generator=gen)[:k]
+        x[r, pos] = x[r].max() + abs(float(rng.standard_normal())) + 0.5
+    res["config2_greedy"] = timed(x, params(256, 0.0, 0, 1.0, 1.0, 64), 0, 20)
+    del x
+    # config 3: 1024 x 109,051, Gumbel + 2 log(1/rank^1.1) under a per-row permutation, mixed parameters
+    Vp = W.PRUNED_VOCAB
+    u = torch.rand(1024, Vp, device=dev, generator=gen).clamp_(1e-12, 1.0 - 1e-7)
+    head = -2.2 * torch.log(torch.arange(1, Vp + 1, device=dev, dtype=torch.float64)).float()
+    perm = torch.argsort(torch.rand(1024, Vp, device=dev, generator=gen), dim=1)
+    x = (-torch.log(-torch.log(u)) + head[perm]).contiguous()
+    del u, perm
+    p3 = params(1024, 1.0, 0, 1.0, 1.0, 64)
+    p3["temperature"] = rng.uniform(0.5, 1.5, 1024)
+    p3["top_k"] = np.array([0, 20, 40, 100])[rng.integers(0, 4, 1024)]
+    p3["top_p"] = rng.uniform(0.8, 1.0, 1024)
+    p3["repetition_penalty"] = rng.uniform(1.0, 1.3, 1024)
+    res["config3_mixed"] = timed(x, p3, 64, 20)
+    del x
+    # config 4: 4096 x 151,936, even rows flat N(0, 0.5), odd rows N(0, 2) with +12 on one index
+    x = torch.randn(4096, V, device=dev, generator=gen)
+    x[0::2] *= 0.5
+    x[1::2] *= 2.0
+    spikes = torch.randint(0, V, (2048,), device=dev, generator=gen)
+    x[torch.arange(1, 4096, 2, device=dev), spikes] += 12.0
+    res["config4_nucleus"] = timed(x, params(4096, 1.0, 0, 0.9, 1.2, 1024), 1024, 5)
+    del x
+    torch.cuda.empty_cache()
+    # config 1: the single row, 10,000 draws as rows sharing the logits (ld = 0), and one draw at
+    # a time through the drop-in Sampler (host logits, one synchronous round trip a draw)
+    w1 = W.single(1)
+    draws = 10000
+    x = torch.from_numpy(w1.logits).to(dev)
+    p1 = np.repeat(w1.params, draws)
+    res["config1_batched_draws"] = timed(x, p1, w1.window, 5, ld=0, rows=draws,
+                                         state=W.xorshift_states(int(w1.state[0]), draws))
+    s = lrs.Sampler(42)
+    sp = lrs.SamplingParams(temperature=float(w1.params["temperature"][0]), top_k=int(w1.params["top_k"][0]),
+                            top_p=float(w1.params["top_p"][0]),
+                            repetition_penalty=float(w1.params["repetition_penalty"][0]),
+                            repeat_last_n=int(w1.params["repeat_last_n"][0]), seed=42)
+    recent = w1.hist[0, :int(w1.hist_len[0])]
+    for _ in range(5):
+        s.sample(w1.logits[0], sp, recent)
+    n1 = 200
+    t = time.perf_counter()
+    for _ in range(n1):
+        s.sample(w1.logits[0], sp, recent)
+    res["config1_single_draw"] = {"us_per_draw": (time.perf_counter() - t) / n1 * 1e6,
+                                  "api": "lrs_sampler_sample (host logits, synchronous)"}
+    return res
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -382,6 +502,7 @@ def main():
     ap.add_argument("--ref-rows", type=int, default=None,
                     help="--impl reference: rows per step (default: --rows, the GPU arm's rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
+    ap.add_argument("--no-configs", action="store_true", help="skip the brief configs 1-4 in the headline line")
     ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded", "configs"])
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
@@ -500,6 +621,14 @@ def main():
                          f"per row over {threads} host threads ({dt:.1f} s)",
                "value_1_thread": v1, "sample_1_thread": f"first {n1} rows on one host thread ({dt1:.1f} s)"}
 
+    aux = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        bs.close()
+        bs = None
+        del logits
+        torch.cuda.empty_cache()
+        aux = brief_configs(dev, peak)
+
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
@@ -510,15 +639,19 @@ def main():
                          "frac": achieved / peak, "traffic": traffic,
                          "nominal_peak": NOMINAL_HBM_GBS, "frac_of_nominal": achieved / NOMINAL_HBM_GBS,
                          "peak_kind": kind,
-                         "kernel": "staged pipeline: lrs_stage_stats, _prep, _classify, _sum, _finish, lrs_sample_rows",
+                         "kernel": "staged pipeline: lrs_stage_stats, _prep, _classify, _sum, _finish, _big, "
+                                   "lrs_sample_rows",
                          "kernel_ms_mean": mean_launch, "bytes_per_launch": rows * bytes_per_row},
             "e2e": {"value": e2e_value, "unit": "rows/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": STAGE_LAUNCHES * args.steps,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
+        if aux is not None:
+            line["configs"] = aux
         print(json.dumps(line), flush=True)
-    bs.close()
+    if bs is not None:
+        bs.close()
     if pg:
         pg.destroy_process_group()
 
