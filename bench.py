@@ -33,6 +33,8 @@ configs    (default run, one GPU; --no-configs skips it) the same configurations
            on the device with the workloads' distributions and parameter mixes (the host
            generator takes minutes at these sizes), config 1 through the drop-in single-row
            API and as 10,000 draws sharing the logits
+--workload brief  those brief configurations alone (--configs config4,... picks some;
+           --config4-rows sizes config 4 down for profiling)
 """
 from __future__ import annotations
 
@@ -375,13 +377,14 @@ def run_configs(args):
     print(json.dumps(out), flush=True)
 
 
-def brief_configs(dev, peak):
+def brief_configs(dev, peak, only=None, rows4=4096):
     """Configs 1-4 in brief for the headline line (one GPU): configs 2-4 at their full sizes on
     seeded inputs generated on the device with the distributions and parameter mixes of
     lrs.workloads (greedy rows with planted ties; Zipf-like rows under a per-row permutation
     with the mixed parameters; flat and spiked nucleus-stress rows with a 1,024-token window),
     config 1 on the workload's own row: one draw at a time through the drop-in single-row API,
-    and 10,000 draws as rows sharing the logits.  rows/s and the roofline fraction of each."""
+    and 10,000 draws as rows sharing the logits.  rows/s and the roofline fraction of each.
+    only: the configurations to run (config1 .. config4; None: all); rows4: config 4's rows."""
     import torch
     import lrs
     from lrs import workloads as W
@@ -433,37 +436,43 @@ def brief_configs(dev, peak):
     res = {"data": "configs 2-4: seeded inputs generated on the device with the distributions and parameter "
                    "mixes of lrs.workloads; config 1: the workload's own row"}
     V = W.QWEN_VOCAB
+    want = (lambda c: only is None or c in only)
     # config 2: 256 greedy rows, the max planted at 2-4 positions in 10% of them
-    x = torch.randn(256, V, device=dev, generator=gen) * 3.0
-    for r in range(3, 256, 10):
-        k = int(rng.integers(2, 5))
-        pos = torch.randperm(V, device=dev, generator=gen)[:k]
-        x[r, pos] = x[r].max() + abs(float(rng.standard_normal())) + 0.5
-    res["config2_greedy"] = timed(x, params(256, 0.0, 0, 1.0, 1.0, 64), 0, 20)
-    del x
+    if want("config2"):
+        x = torch.randn(256, V, device=dev, generator=gen) * 3.0
+        for r in range(3, 256, 10):
+            k = int(rng.integers(2, 5))
+            pos = torch.randperm(V, device=dev, generator=gen)[:k]
+            x[r, pos] = x[r].max() + abs(float(rng.standard_normal())) + 0.5
+        res["config2_greedy"] = timed(x, params(256, 0.0, 0, 1.0, 1.0, 64), 0, 20)
+        del x
     # config 3: 1024 x 109,051, Gumbel + 2 log(1/rank^1.1) under a per-row permutation, mixed parameters
-    Vp = W.PRUNED_VOCAB
-    u = torch.rand(1024, Vp, device=dev, generator=gen).clamp_(1e-12, 1.0 - 1e-7)
-    head = -2.2 * torch.log(torch.arange(1, Vp + 1, device=dev, dtype=torch.float64)).float()
-    perm = torch.argsort(torch.rand(1024, Vp, device=dev, generator=gen), dim=1)
-    x = (-torch.log(-torch.log(u)) + head[perm]).contiguous()
-    del u, perm
-    p3 = params(1024, 1.0, 0, 1.0, 1.0, 64)
-    p3["temperature"] = rng.uniform(0.5, 1.5, 1024)
-    p3["top_k"] = np.array([0, 20, 40, 100])[rng.integers(0, 4, 1024)]
-    p3["top_p"] = rng.uniform(0.8, 1.0, 1024)
-    p3["repetition_penalty"] = rng.uniform(1.0, 1.3, 1024)
-    res["config3_mixed"] = timed(x, p3, 64, 20)
-    del x
+    if want("config3"):
+        Vp = W.PRUNED_VOCAB
+        u = torch.rand(1024, Vp, device=dev, generator=gen).clamp_(1e-12, 1.0 - 1e-7)
+        head = -2.2 * torch.log(torch.arange(1, Vp + 1, device=dev, dtype=torch.float64)).float()
+        perm = torch.argsort(torch.rand(1024, Vp, device=dev, generator=gen), dim=1)
+        x = (-torch.log(-torch.log(u)) + head[perm]).contiguous()
+        del u, perm
+        p3 = params(1024, 1.0, 0, 1.0, 1.0, 64)
+        p3["temperature"] = rng.uniform(0.5, 1.5, 1024)
+        p3["top_k"] = np.array([0, 20, 40, 100])[rng.integers(0, 4, 1024)]
+        p3["top_p"] = rng.uniform(0.8, 1.0, 1024)
+        p3["repetition_penalty"] = rng.uniform(1.0, 1.3, 1024)
+        res["config3_mixed"] = timed(x, p3, 64, 20)
+        del x
     # config 4: 4096 x 151,936, even rows flat N(0, 0.5), odd rows N(0, 2) with +12 on one index
-    x = torch.randn(4096, V, device=dev, generator=gen)
-    x[0::2] *= 0.5
-    x[1::2] *= 2.0
-    spikes = torch.randint(0, V, (2048,), device=dev, generator=gen)
-    x[torch.arange(1, 4096, 2, device=dev), spikes] += 12.0
-    res["config4_nucleus"] = timed(x, params(4096, 1.0, 0, 0.9, 1.2, 1024), 1024, 5)
-    del x
+    if want("config4"):
+        x = torch.randn(rows4, V, device=dev, generator=gen)
+        x[0::2] *= 0.5
+        x[1::2] *= 2.0
+        spikes = torch.randint(0, V, (rows4 // 2,), device=dev, generator=gen)
+        x[torch.arange(1, rows4, 2, device=dev), spikes] += 12.0
+        res["config4_nucleus"] = timed(x, params(rows4, 1.0, 0, 0.9, 1.2, 1024), 1024, 5)
+        del x
     torch.cuda.empty_cache()
+    if not want("config1"):
+        return res
     # config 1: the single row, 10,000 draws as rows sharing the logits (ld = 0), and one draw at
     # a time through the drop-in Sampler (host logits, one synchronous round trip a draw)
     w1 = W.single(1)
@@ -503,7 +512,9 @@ def main():
                     help="--impl reference: rows per step (default: --rows, the GPU arm's rows)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg (profiling runs)")
     ap.add_argument("--no-configs", action="store_true", help="skip the brief configs 1-4 in the headline line")
-    ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded", "configs"])
+    ap.add_argument("--workload", default="headline", choices=["headline", "vocab_sharded", "configs", "brief"])
+    ap.add_argument("--configs", default=None, help="--workload brief: comma list of config1..config4 (default all)")
+    ap.add_argument("--config4-rows", type=int, default=4096, help="--workload brief: rows of config 4")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":
@@ -515,6 +526,13 @@ def main():
     if args.workload == "configs":
         if rank == 0:
             run_configs(args)
+        return
+    if args.workload == "brief":
+        if rank == 0:
+            import torch
+            torch.cuda.set_device(0)
+            only = set(args.configs.split(",")) if args.configs else None
+            print(json.dumps(brief_configs(torch.device("cuda", 0), peaks()[0], only, args.config4_rows)), flush=True)
         return
 
     import torch
