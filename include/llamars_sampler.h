@@ -205,6 +205,31 @@ int  lrs_noalloc_poll_error(int device, void* stream);
 int  lrs_assemble_shards(const float* d_gathered, uint32_t shards, uint32_t rows, uint32_t shard_n,
                          float* d_out, uint64_t ld_out, void* stream);
 
+/* ---- batched generation loop: its per-row state on the device ---------------------
+ * lrs_history_append  replaces `recent.push(next)` after each draw of the generation loops
+ *                     (model.rs:768, server.rs:187; `recent` starts as the prompt ids,
+ *                     model.rs:758, server.rs:182): for every row r < rows whose d_status[r]
+ *                     is LRS_OK (d_status NULL: every row) and whose token is neither `eos`
+ *                     (the loops stop before the push, model.rs:761-763) nor LRS_TOKEN_NONE,
+ *                     appends d_tokens[r] to row r's history d_hist[r*hist_ld ..] and
+ *                     increments d_hist_len[r], the same history layout lrs_sample_device
+ *                     reads.  A row whose history already holds hist_ld ids first keeps its
+ *                     last `keep` (1 <= keep <= hist_ld / 2, LRS_E_INVALID otherwise): the
+ *                     penalty window (sampler.rs:84-88) stays exact while repeat_last_n <= keep
+ *                     (repeat_last_n == 0, the whole history, while a row has held at most
+ *                     hist_ld ids).  A loop then uploads its prompts once and no history after.
+ * lrs_remap_tokens    sampling on rows of a pruned vocabulary (prune.rs:187-195 renumbers the
+ *                     kept ids in order): d_out[r] = d_map[d_tokens[r]] (the original id of
+ *                     pruned id t is d_map[t], t < map_n) where d_status[r] is LRS_OK (or
+ *                     d_status is NULL), otherwise d_out[r] = d_tokens[r]; d_out may be
+ *                     d_tokens.  Keep the history in pruned ids (the logits' id space).
+ * Both are enqueued on `stream` (cudaStream_t) with device pointers; they return LRS_OK,
+ * LRS_E_INVALID or LRS_E_CUDA.                                                        */
+int  lrs_history_append(const uint32_t* d_tokens, const int32_t* d_status, uint32_t rows, uint32_t eos,
+                        uint32_t* d_hist, uint64_t hist_ld, uint32_t* d_hist_len, uint32_t keep, void* stream);
+int  lrs_remap_tokens(const uint32_t* d_tokens, const int32_t* d_status, uint32_t rows,
+                      const uint32_t* d_map, uint32_t map_n, uint32_t* d_out, void* stream);
+
 /* ---- single-row drop-in (Sampler API) -------------------------------------------
  * lrs_sampler_new    replaces Sampler::new(seed)               (sampler.rs:33-37)
  * lrs_sampler_sample replaces Sampler::sample(logits, params, recent) (sampler.rs:56)

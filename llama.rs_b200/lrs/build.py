@@ -23,7 +23,7 @@ NVCC_FLAGS = [
     "-Xcompiler", "-fPIC,-O2",
     "-Xptxas", "-warn-spills",
 ]
-SOURCES = ["lrs_kernels.cu", "lrs_api.cu", "lrs_noalloc.cu"]
+SOURCES = ["lrs_kernels.cu", "lrs_api.cu", "lrs_noalloc.cu", "lrs_generate.cu"]
 HEADERS = ["lrs_device.cuh", "lrs_grid.h", "lrs_kernels_decl.cuh", "lrs_stages.cuh"]
 
 

@@ -44,7 +44,8 @@ EXPORTS = [
     "lrs_create", "lrs_destroy", "lrs_last_error", "lrs_seed_state", "lrs_set_state", "lrs_get_state",
     "lrs_set_params", "lrs_sample", "lrs_sample_device", "lrs_sampler_new", "lrs_sampler_free",
     "lrs_sampler_state", "lrs_sampler_sample", "lrs_sample_device_noalloc", "lrs_assemble_shards",
-    "lrs_poll_error", "lrs_noalloc_poll_error", "lrs_test_wait_timeout",
+    "lrs_poll_error", "lrs_noalloc_poll_error", "lrs_test_wait_timeout", "lrs_history_append",
+    "lrs_remap_tokens",
 ]
 
 
@@ -94,6 +95,10 @@ def lib() -> ctypes.CDLL:
         L.lrs_test_wait_timeout.restype = I
         L.lrs_assemble_shards.argtypes = [P, U32, U32, U32, P, U64, P]
         L.lrs_assemble_shards.restype = I
+        L.lrs_history_append.argtypes = [P, P, U32, U32, P, U64, P, U32, P]
+        L.lrs_history_append.restype = I
+        L.lrs_remap_tokens.argtypes = [P, P, U32, P, U32, P, P]
+        L.lrs_remap_tokens.restype = I
         L.lrs_sampler_new.argtypes = [U64, I]
         L.lrs_sampler_new.restype = P
         L.lrs_sampler_free.argtypes = [P]
@@ -231,6 +236,33 @@ class BatchSampler:
                                        params.data_ptr(), state.data_ptr(), tokens.data_ptr(), ptr(probs),
                                        ptr(status), ptr(info), stream)
         _check(code, self._h)
+
+    @staticmethod
+    def history_append(tokens, hist, hist_len, status=None, eos=None, keep=None, stream=None, rows=None):
+        """`recent.push(next)` of a batched generation loop on the device (lrs_history_append):
+        appends each row's token (torch CUDA tensors, int32 views of the u32 ids) to its history
+        row unless the row failed (status) or drew `eos`; a full row keeps its last `keep` ids
+        (default half the row).  Async on `stream`."""
+        rows = tokens.numel() if rows is None else rows
+        hld = hist.stride(0)
+        keep = hld // 2 if keep is None else keep
+        eos = TOKEN_NONE if eos is None else eos
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(tokens.device).cuda_stream
+        _check(lib().lrs_history_append(tokens.data_ptr(), None if status is None else status.data_ptr(), rows,
+                                        eos, hist.data_ptr(), hld, hist_len.data_ptr(), keep, stream))
+
+    @staticmethod
+    def remap_tokens(tokens, id_map, out, status=None, stream=None, rows=None):
+        """Pruned-vocabulary ids to the full vocabulary (lrs_remap_tokens): out[r] = id_map[tokens[r]]
+        for rows sampled without error.  Async on `stream`."""
+        rows = tokens.numel() if rows is None else rows
+        if stream is None:
+            import torch
+            stream = torch.cuda.current_stream(tokens.device).cuda_stream
+        _check(lib().lrs_remap_tokens(tokens.data_ptr(), None if status is None else status.data_ptr(), rows,
+                                      id_map.data_ptr(), id_map.numel(), out.data_ptr(), stream))
 
     def poll_error(self):
         """Waits for the last launch and raises the error it reported (lrs_poll_error)."""

@@ -116,6 +116,26 @@ extern "C" {
         stream: *mut c_void,
     ) -> c_int;
     pub fn lrs_noalloc_poll_error(device: c_int, stream: *mut c_void) -> c_int;
+    pub fn lrs_history_append(
+        d_tokens: *const u32,
+        d_status: *const i32,
+        rows: u32,
+        eos: u32,
+        d_hist: *mut u32,
+        hist_ld: u64,
+        d_hist_len: *mut u32,
+        keep: u32,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub fn lrs_remap_tokens(
+        d_tokens: *const u32,
+        d_status: *const i32,
+        rows: u32,
+        d_map: *const u32,
+        map_n: u32,
+        d_out: *mut u32,
+        stream: *mut c_void,
+    ) -> c_int;
     pub fn lrs_sampler_new(seed: u64, device: c_int) -> *mut lrs_sampler;
     pub fn lrs_sampler_free(s: *mut lrs_sampler);
     pub fn lrs_sampler_state(s: *const lrs_sampler) -> u64;

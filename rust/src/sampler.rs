@@ -242,6 +242,49 @@ impl BatchSampler {
         )
     }
 
+    /// `recent.push(next)` of a batched generation loop (model.rs:768, server.rs:187), on the
+    /// device: appends each row's token to its history row (the layout `sample_device` reads)
+    /// unless the row failed or drew `eos`; a full row keeps its last `keep` ids.
+    ///
+    /// # Safety
+    /// Device pointers valid for `rows` rows (`hist_ld` ids each) on the context's GPU.
+    #[allow(clippy::too_many_arguments)]
+    pub unsafe fn history_append(
+        &mut self,
+        d_tokens: *const u32,
+        d_status: *const i32,
+        rows: u32,
+        eos: u32,
+        d_hist: *mut u32,
+        hist_ld: u64,
+        d_hist_len: *mut u32,
+        keep: u32,
+        stream: *mut c_void,
+    ) -> Result<(), SamplerError> {
+        check(
+            ffi::lrs_history_append(d_tokens, d_status, rows, eos, d_hist, hist_ld, d_hist_len, keep, stream),
+            std::ptr::null(),
+        )
+    }
+
+    /// Pruned-vocabulary ids back to the full vocabulary (prune.rs:187-195 renumbers the kept
+    /// ids in order): `d_out[r] = d_map[d_tokens[r]]` for rows sampled without error.
+    ///
+    /// # Safety
+    /// Device pointers valid for `rows` tokens and `map_n` map entries on the context's GPU.
+    pub unsafe fn remap_tokens(
+        &mut self,
+        d_tokens: *const u32,
+        d_status: *const i32,
+        rows: u32,
+        d_map: *const u32,
+        map_n: u32,
+        d_out: *mut u32,
+        stream: *mut c_void,
+    ) -> Result<(), SamplerError> {
+        check(ffi::lrs_remap_tokens(d_tokens, d_status, rows, d_map, map_n, d_out, stream), std::ptr::null())
+    }
+
     /// Waits for the last launch and returns the error it reported, if any.
     pub fn poll_error(&mut self) -> Result<(), SamplerError> {
         check(unsafe { ffi::lrs_poll_error(self.ctx) }, self.ctx)

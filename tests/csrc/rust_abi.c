@@ -63,6 +63,10 @@ typedef int (*rs_lrs_sample_device_noalloc)(int, const float *, uint32_t, uint32
                                             uint64_t, const uint32_t *, const lrs_params *, uint64_t *, uint32_t *,
                                             float *, int32_t *, void *);
 typedef int (*rs_lrs_noalloc_poll_error)(int, void *);
+typedef int (*rs_lrs_history_append)(const uint32_t *, const int32_t *, uint32_t, uint32_t, uint32_t *, uint64_t,
+                                     uint32_t *, uint32_t, void *);
+typedef int (*rs_lrs_remap_tokens)(const uint32_t *, const int32_t *, uint32_t, const uint32_t *, uint32_t, uint32_t *,
+                                   void *);
 typedef lrs_sampler *(*rs_lrs_sampler_new)(uint64_t, int);
 typedef void (*rs_lrs_sampler_free)(lrs_sampler *);
 typedef uint64_t (*rs_lrs_sampler_state)(const lrs_sampler *);
@@ -83,6 +87,8 @@ SAME(lrs_sample_device);
 SAME(lrs_poll_error);
 SAME(lrs_sample_device_noalloc);
 SAME(lrs_noalloc_poll_error);
+SAME(lrs_history_append);
+SAME(lrs_remap_tokens);
 SAME(lrs_sampler_new);
 SAME(lrs_sampler_free);
 SAME(lrs_sampler_state);
@@ -91,7 +97,8 @@ SAME(lrs_sampler_sample);
 static const char *const kSymbols[] = {
     "lrs_create", "lrs_destroy", "lrs_last_error", "lrs_seed_state", "lrs_set_state", "lrs_get_state",
     "lrs_set_params", "lrs_sample", "lrs_sample_device", "lrs_poll_error", "lrs_sample_device_noalloc",
-    "lrs_noalloc_poll_error", "lrs_sampler_new", "lrs_sampler_free", "lrs_sampler_state", "lrs_sampler_sample",
+    "lrs_noalloc_poll_error", "lrs_history_append", "lrs_remap_tokens", "lrs_sampler_new", "lrs_sampler_free",
+    "lrs_sampler_state", "lrs_sampler_sample",
 };
 
 int main(int argc, char **argv) {
@@ -119,6 +126,12 @@ int main(int argc, char **argv) {
     const rs_lrs_sampler_sample samp = (rs_lrs_sampler_sample)dlsym(h, "lrs_sampler_sample");
     int status = 0;
     if (samp(NULL, NULL, 0, NULL, NULL, 0, &status) != LRS_TOKEN_NONE || status != LRS_E_INVALID) return 1;
+    /* argument checks that reject before any device work */
+    const rs_lrs_history_append app = (rs_lrs_history_append)dlsym(h, "lrs_history_append");
+    if (app(NULL, NULL, 0, 0, NULL, 0, NULL, 0, NULL) != LRS_OK) return 1;            /* no rows: nothing to do */
+    if (app(NULL, NULL, 4, 0, NULL, 64, NULL, 32, NULL) != LRS_E_INVALID) return 1;    /* null buffers */
+    const rs_lrs_remap_tokens rmp = (rs_lrs_remap_tokens)dlsym(h, "lrs_remap_tokens");
+    if (rmp(NULL, NULL, 4, NULL, 0, NULL, NULL) != LRS_E_INVALID) return 1;
     printf("rust ABI ok: %zu symbols\n", sizeof kSymbols / sizeof kSymbols[0]);
     dlclose(h);
     return 0;
