@@ -910,16 +910,13 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
 // more) are found by prefix sums on the channel of the sum's current grid and added
 // exactly; only a sum that leaves both grids is classified again.  A sum that starts from
 // zero crosses many binades in its first elements: such a block is added one by one.
-__device__ __noinline__ float warp_walk_block(const float* bbase, uint32_t bcnt, uint32_t pen4, float penalty,
+__device__ __noinline__ float warp_walk_block(float4 q, uint32_t pen4, float penalty,
                                               float inv_t, float M, float xthr, float s, const ExpTable tab,
                                               uint32_t* events) {
     const int lane = threadIdx.x & 31;
     float e[4];
     {
-        const float ninf = __int_as_float(0xFF800000);
-        float4 q = make_float4(ninf, ninf, ninf, ninf);
-        if (4u * (uint32_t)lane < bcnt) q = __ldg(reinterpret_cast<const float4*>(bbase + 4 * lane));
-        float x[4] = {q.x, q.y, q.z, q.w};
+        float x[4] = {q.x, q.y, q.z, q.w};  // (the lane's four raw values; -inf past the block)
         // (the four exps side by side; the table only where the rounded double exp is too
         // close to a rounding midpoint)
         float d[4];
@@ -1019,13 +1016,26 @@ __device__ __noinline__ float warp_walk_block(const float* bbase, uint32_t bcnt,
 constexpr int kSumWarps = 4;  // rows per block of the sum stage (one warp each)
 
 // The running sum over tile t (its grid records from classify): block by block, each block
-// added in one step where the sum stays on a grid it was classified for, else walked.
+// added in one step where the sum stays on a grid it was classified for, else walked.  The
+// tile's values are loaded first, side by side with its records, so that a walk finds its
+// block in registers.
 __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g, uint32_t r, uint32_t t, float s,
                                                const lrs_params& P, float inv_t, float M, const uint32_t* hrow,
                                                uint32_t hstart, uint32_t hlen, uint32_t* wb, const ExpTable tab,
                                                uint32_t* events, uint32_t* walks) {
     const int lane = threadIdx.x & 31;
     const uint64_t ti = (uint64_t)r * S.nt + t;
+    const uint32_t cnt = chunk_count(g, t);
+    const uint32_t g0 = g.head + t * kTile;
+    float4 tq[8];  // (lane L: elements 128 j + 4 L .. + 3 of the tile, -inf past its end)
+    {
+        const float ninf = __int_as_float(0xFF800000);
+        const float* tb = g.row + g0 + 4 * lane;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            tq[j] = 128u * (uint32_t)j + 4u * (uint32_t)lane < cnt ? __ldg(reinterpret_cast<const float4*>(tb + 128 * j))
+                                                                  : make_float4(ninf, ninf, ninf, ninf);
+    }
     const TilePrep tp = S.tprep[ti];
     const uint32_t bflags = S.tres[ti].bflags;
     uint32_t c0 = 0, c1 = 0;
@@ -1033,8 +1043,6 @@ __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g,
         c0 = S.tres[ti].b0[lane];
         c1 = S.tres[ti].b1[lane];
     }
-    const uint32_t cnt = chunk_count(g, t);
-    const uint32_t g0 = g.head + t * kTile;
     const bool pen_on = P.repetition_penalty != 1.0f;
     bool pen = false;
     if (pen_on && hlen) pen = tile_window(hrow, hstart, hlen, g0, cnt, wb);
@@ -1068,8 +1076,11 @@ __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g,
         s = grid_value(uu, A + __shfl_sync(0xFFFFFFFFu, excl, L));
         const uint32_t bw = (uint32_t)L;
         const uint32_t pen4 = pen ? (wb[4 * bw + (lane >> 3)] >> (4 * (lane & 7))) & 15u : 0u;
-        const uint32_t bcnt = cnt - 128u * bw < 128u ? cnt - 128u * bw : 128u;
-        s = warp_walk_block(g.row + g0 + 128u * bw, bcnt, pen4, P.repetition_penalty, inv_t, M, tp.xthr, s, tab, events);
+        float4 q = tq[0];
+#pragma unroll
+        for (int j = 1; j < 8; ++j)
+            if ((uint32_t)j == bw) q = tq[j];
+        s = warp_walk_block(q, pen4, P.repetition_penalty, inv_t, M, tp.xthr, s, tab, events);
         ++*walks;
         b0 = bw + 1;
     }
