@@ -1704,6 +1704,63 @@ __device__ __noinline__ uint32_t nucleus_prefilter(unsigned long long* keys, uin
     return m;
 }
 
+// The sequential f32 run over keys[0, cnt) (p in the high word, inverted) by thread 0, eight
+// values a step with their loads issued a step ahead (sampler.rs:137-145 for DIR > 0, stop at
+// s >= thr; sampler.rs:156-161 for DIR < 0, stop at s <= 0).  Returns the stop position or
+// -1; s: the value after it (or after the run).  Same values for every thread.
+template <int DIR>
+__device__ __forceinline__ float big_step(float c, float v) {
+    if constexpr (DIR > 0) return __fadd_rn(c, v); else return __fsub_rn(c, v);
+}
+template <int DIR>
+__device__ __forceinline__ bool big_hit(float c, float thr) {
+    if constexpr (DIR > 0) return c >= thr; else return c <= 0.0f;
+}
+__device__ __forceinline__ float big_p(const unsigned long long* keys, uint32_t i, uint32_t cnt) {
+    return i < cnt ? __uint_as_float(~(uint32_t)(keys[i] >> 32)) : 0.0f;
+}
+template <int DIR>
+__device__ __forceinline__ int big_serial(const unsigned long long* keys, uint32_t cnt, float& s, float thr,
+                                          RowShared& sh) {
+    if (threadIdx.x == 0) {
+        float cur = s;
+        int stop = -1;
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = big_p(keys, (uint32_t)j, cnt);
+        for (uint32_t i = 0; i < cnt; i += 8) {
+            float nx[8], c[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nx[j] = big_p(keys, i + 8u + (uint32_t)j, cnt);
+            // (positions past cnt add 0: they neither move s nor stop it)
+            c[0] = big_step<DIR>(cur, v[0]);
+#pragma unroll
+            for (int j = 1; j < 8; ++j) c[j] = big_step<DIR>(c[j - 1], v[j]);
+            if (big_hit<DIR>(c[7], thr)) {
+                int f = 7;
+#pragma unroll
+                for (int j = 6; j >= 0; --j) f = big_hit<DIR>(c[j], thr) ? j : f;
+                float cf = c[7];
+#pragma unroll
+                for (int j = 6; j >= 0; --j) cf = f == j ? c[j] : cf;
+                stop = (int)i + f;
+                cur = cf;
+                break;
+            }
+            cur = c[7];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = nx[j];
+        }
+        sh.fstate = cur;
+        sh.stop = stop;
+    }
+    csync();
+    s = sh.fstate;
+    const int st = sh.stop;
+    csync();
+    return st;
+}
+
 // Sequential f32 run over sorted probabilities keys[0..cnt) (sampler.rs:137-139 / 148-151 /
 // 156-158): dir > 0 adds until s >= thr, dir < 0 subtracts until s <= 0.  The first 512
 // positions go one by one on thread 0, the rest chunk by chunk with the block's exact
@@ -1714,7 +1771,10 @@ __device__ __noinline__ int sorted_run(const SortedKeys keys, uint32_t cnt, int 
     // (the head of a sorted run holds its largest elements, nearly every one an ordered step
     // of the emulation: it goes one by one; the emulation takes the rest)
     const uint32_t head = cnt < head_max ? cnt : head_max;
-    {
+    if (!keys.perm) {  // (keys in order: the scalar walker)
+        const int st = dir > 0 ? big_serial<+1>(keys.keys, head, s, thr, sh) : big_serial<-1>(keys.keys, head, s, 0.0f, sh);
+        if (st >= 0 || head == cnt) return st;
+    } else {
         if (threadIdx.x == 0) {
             // Groups of eight: the sum steps through a group with no branch, and the stop test
             // runs once per group (the run is monotone: p >= 0), then finds the first position
@@ -2120,59 +2180,6 @@ __device__ __noinline__ bool big_fast_range(const unsigned long long* src, uint3
     const bool fast = !any && (DIR > 0 ? (A + total <= kTwo24 - 1u && (float)(A + total) < tq) : total < A - lower);
     if (fast && apply) s = grid_value(uu, DIR > 0 ? A + total : A - total);
     return fast;
-}
-
-template <int DIR>
-__device__ __forceinline__ float big_step(float c, float v) {
-    if constexpr (DIR > 0) return __fadd_rn(c, v); else return __fsub_rn(c, v);
-}
-template <int DIR>
-__device__ __forceinline__ bool big_hit(float c, float thr) {
-    if constexpr (DIR > 0) return c >= thr; else return c <= 0.0f;
-}
-__device__ __forceinline__ float big_p(const unsigned long long* keys, uint32_t i, uint32_t cnt) {
-    return i < cnt ? __uint_as_float(~(uint32_t)(keys[i] >> 32)) : 0.0f;
-}
-template <int DIR>
-__device__ __forceinline__ int big_serial(const unsigned long long* keys, uint32_t cnt, float& s, float thr,
-                                          RowShared& sh) {
-    if (threadIdx.x == 0) {
-        float cur = s;
-        int stop = -1;
-        float v[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = big_p(keys, (uint32_t)j, cnt);
-        for (uint32_t i = 0; i < cnt; i += 8) {
-            float nx[8], c[8];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) nx[j] = big_p(keys, i + 8u + (uint32_t)j, cnt);
-            // (positions past cnt add 0: they neither move s nor stop it)
-            c[0] = big_step<DIR>(cur, v[0]);
-#pragma unroll
-            for (int j = 1; j < 8; ++j) c[j] = big_step<DIR>(c[j - 1], v[j]);
-            if (big_hit<DIR>(c[7], thr)) {
-                int f = 7;
-#pragma unroll
-                for (int j = 6; j >= 0; --j) f = big_hit<DIR>(c[j], thr) ? j : f;
-                float cf = c[7];
-#pragma unroll
-                for (int j = 6; j >= 0; --j) cf = f == j ? c[j] : cf;
-                stop = (int)i + f;
-                cur = cf;
-                break;
-            }
-            cur = c[7];
-#pragma unroll
-            for (int j = 0; j < 8; ++j) v[j] = nx[j];
-        }
-        sh.fstate = cur;
-        sh.stop = stop;
-    }
-    csync();
-    s = sh.fstate;
-    const int st = sh.stop;
-    csync();
-    return st;
 }
 
 // The sequential run over positions [0, lim) of the bucketed keys (sampler.rs:137-145 for
