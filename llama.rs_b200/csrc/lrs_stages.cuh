@@ -1508,6 +1508,35 @@ __device__ __forceinline__ void warp_sort_run(unsigned long long* keys, uint32_t
     }
 }
 
+// The warp sorts k[0, c) in place, ascending, c <= 1024: a bitonic network over the next power
+// of two in shared memory, every compare-exchange ascending (a merge opens with mirrored
+// partners), so the positions past c act as +inf and are never read or written.  Loops over
+// any c (the big-nucleus buckets); the finish's fixed runs of 256 keep the register network.
+__device__ __noinline__ void warp_sort_smem(unsigned long long* k, uint32_t c) {
+    const uint32_t lane = threadIdx.x & 31u;
+    if (c < 2u) return;
+    uint32_t lp = 1;
+    while ((1u << lp) < c) ++lp;
+    const uint32_t pairs = 1u << (lp - 1);
+    for (uint32_t ls = 1; ls <= lp; ++ls) {
+        for (int lt = (int)ls - 1; lt >= 0; --lt) {
+            const bool open = lt == (int)ls - 1;  // (the merge's first stage: mirrored partners)
+            for (uint32_t q = lane; q < pairs; q += 32u) {
+                const uint32_t i = ((q >> lt) << (lt + 1)) | (q & ((1u << lt) - 1u));
+                const uint32_t j = open ? (i | ((1u << (lt + 1)) - 1u)) - (i & ((1u << lt) - 1u)) : i + (1u << lt);
+                if (j < c) {
+                    const unsigned long long a = k[i], b = k[j];
+                    if (b < a) {
+                        k[i] = b;
+                        k[j] = a;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
 // The sorted order: position i holds keys[perm[i]] (keys[i] when perm is null).
 struct SortedKeys {
     const unsigned long long* keys;
@@ -2123,14 +2152,8 @@ __device__ __noinline__ void big_sort_chunk(unsigned long long* B, uint32_t pos,
         const uint32_t c = hi - lo;
         if (c <= 1u || ((bs.sorted[b >> 5] >> (b & 31u)) & 1u)) continue;
         if (lane == 0 && c <= 512u) atomicOr(&bs.sorted[b >> 5], 1u << (b & 31u));
-        if (c <= 64u)
-            warp_sort_run<2>(keys, lo, hi, hi);
-        else if (c <= 128u)
-            warp_sort_run<4>(keys, lo, hi, hi);
-        else if (c <= 256u)
-            warp_sort_run<8>(keys, lo, hi, hi);
-        else if (c <= 512u)
-            warp_sort_run<16>(keys, lo, hi, hi);
+        if (c <= 512u)
+            warp_sort_smem(keys + lo, c);
         else if (lane == 0)
             sh.misc[3] = 1u;
     }
