@@ -910,9 +910,35 @@ __global__ void __launch_bounds__(kClassifyWarps * 32) lrs_stage_classify(const 
 // more) are found by prefix sums on the channel of the sum's current grid and added
 // exactly; only a sum that leaves both grids is classified again.  A sum that starts from
 // zero crosses many binades in its first elements: such a block is added one by one.
+// The block's 128 values added to s one after another by lane 0 from the warp's shared buffer
+// (ser: 128 floats), the result on every lane.
+__device__ __forceinline__ float warp_serial128(const float (&e)[4], float* ser, float s) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) ser[4 * lane + c] = e[c];
+    __syncwarp();
+    if (lane == 0) {
+        float v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = ser[j];
+        for (int i = 0; i < 128; i += 8) {
+            float nx[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nx[j] = i + 8 + j < 128 ? ser[i + 8 + j] : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s = __fadd_rn(s, v[j]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = nx[j];
+        }
+    }
+    s = __shfl_sync(0xFFFFFFFFu, s, 0);
+    __syncwarp();  // (the buffer is read no more)
+    return s;
+}
+
 __device__ __noinline__ float warp_walk_block(float4 q, uint32_t pen4, float penalty,
                                               float inv_t, float M, float xthr, float s, const ExpTable tab,
-                                              uint32_t* events) {
+                                              uint32_t* events, float* ser) {
     const int lane = threadIdx.x & 31;
     float e[4];
     {
@@ -934,13 +960,9 @@ __device__ __noinline__ float warp_walk_block(float4 q, uint32_t pen4, float pen
             else if (d[c] == 0.0f) e[c] = 1.0f;
         }
     }
-    if (s == 0.0f) {  // (every lane adds all 128 in order: the same sum everywhere)
-#pragma unroll 4
-        for (int L = 0; L < 32; ++L)
-#pragma unroll
-            for (int c = 0; c < 4; ++c) s = __fadd_rn(s, __shfl_sync(0xFFFFFFFFu, e[c], L));
+    if (s == 0.0f) {  // (the sum starts here: one lane adds all 128 in order)
         if (lane == 0) *events += 128u;
-        return s;
+        return warp_serial128(e, ser, s);
     }
     int consumed = -1;
     for (int round = 0; round < 129; ++round) {
@@ -963,6 +985,13 @@ __device__ __noinline__ float warp_walk_block(float4 q, uint32_t pen4, float pen
         uint32_t x0 = __shfl_up_sync(0xFFFFFFFFu, l0, 1), x1 = __shfl_up_sync(0xFFFFFFFFu, l1, 1);
         if (lane == 0) x0 = x1 = 0u;  // (not l - t: the scans saturate)
         const uint32_t tot0 = __shfl_sync(0xFFFFFFFFu, l0, 31), tot1 = __shfl_sync(0xFFFFFFFFu, l1, 31);
+        if (round == 0 && (grid_count(s, uu) + tot0 >= 2u * kTwo24 ||
+                           __popc(__ballot_sync(0xFFFFFFFFu, sp0 != 0u)) >= 4)) {
+            // (a block whose sum crosses two binades or more, or that holds several ordered
+            // steps: one lane adds all 128 in order, cheaper than a warp step per event)
+            if (lane == 0) *events += 128u;
+            return warp_serial128(e, ser, s);
+        }
         uint32_t base0 = 0, base1 = 0;  // channel prefixes at the last ordered step
         bool again = false;
         for (int step = 0; step < 129; ++step) {
@@ -1022,7 +1051,7 @@ constexpr int kSumWarps = 4;  // rows per block of the sum stage (one warp each)
 __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g, uint32_t r, uint32_t t, float s,
                                                const lrs_params& P, float inv_t, float M, const uint32_t* hrow,
                                                uint32_t hstart, uint32_t hlen, uint32_t* wb, const ExpTable tab,
-                                               uint32_t* events, uint32_t* walks) {
+                                               uint32_t* events, uint32_t* walks, float* ser) {
     const int lane = threadIdx.x & 31;
     const uint64_t ti = (uint64_t)r * S.nt + t;
     const uint32_t cnt = chunk_count(g, t);
@@ -1080,7 +1109,7 @@ __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g,
 #pragma unroll
         for (int j = 1; j < 8; ++j)
             if ((uint32_t)j == bw) q = tq[j];
-        s = warp_walk_block(q, pen4, P.repetition_penalty, inv_t, M, tp.xthr, s, tab, events);
+        s = warp_walk_block(q, pen4, P.repetition_penalty, inv_t, M, tp.xthr, s, tab, events, ser);
         ++*walks;
         b0 = bw + 1;
     }
@@ -1093,6 +1122,7 @@ __device__ __noinline__ float warp_tile_blocks(const StageArgs& S, const Geo& g,
 // lrs_sample_rows).
 __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs S) {
     __shared__ uint32_t wbits[kSumWarps * 32];
+    __shared__ float wser[kSumWarps * 128];  // (a warp's block values for a one-lane sum)
     const lrs_kernel_args_t& a = S.a;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t r = blockIdx.x * kSumWarps + warp;
@@ -1190,7 +1220,8 @@ __global__ void __launch_bounds__(kSumWarps * 32) lrs_stage_sum(const StageArgs 
             bad = true;
             break;
         }
-        s = warp_tile_blocks(S, g, r, tw, s, P, inv_t, M, hrow, hstart, hlen, wb, exptab, &events, &walks);
+        s = warp_tile_blocks(S, g, r, tw, s, P, inv_t, M, hrow, hstart, hlen, wb, exptab, &events, &walks,
+                             wser + warp * 128);
         t0 = tw + 1;
     }
     // the tail closes the sum
