@@ -6,5 +6,7 @@
 //! crate declares (src/ffi.rs) is checked by tests/csrc/rust_abi.c in the CPU test suite.
 pub mod ffi;
 pub mod sampler;
+pub mod stream;
 
 pub use sampler::{BatchSampler, Sampler, SamplerError, SamplingParams};
+pub use stream::{ByteStream, ByteStreams};
