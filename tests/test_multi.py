@@ -1,4 +1,4 @@
-"""Multi-process host logic on CPU (gloo, world size 2) and the shard assembly kernel.
+"""Multi-process host logic on CPU (gloo, world sizes 2 and 4) and the shard assembly kernel.
 
 Row sharding: every rank samples its block of rows; the union over ranks must equal the
 unsharded result.  Vocabulary sharding (config 5): every rank holds a column block; the
@@ -66,9 +66,9 @@ def _worker(rank, world, port, out_dir):
         dist.destroy_process_group()
 
 
-def test_row_and_vocab_sharding_gloo_world2(tmp_path, oracle):
+@pytest.mark.parametrize("world", [2, 4])  # (the vocabulary must split evenly: 151,936 = 4 x 37,984)
+def test_row_and_vocab_sharding_gloo(tmp_path, oracle, world):
     import torch.multiprocessing as mp
-    world = 2
     mp.start_processes(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, start_method="spawn")
     # rows: the union of the blocks is the unsharded batch
     w = W.headline(row_ids=range(24))
